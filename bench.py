@@ -1,0 +1,570 @@
+"""Benchmark of the macmetalpy_b200 hot path (driver contract: one JSON line).
+
+Headline workload ("C2"): binary ufuncs at 2^28
+elements -- float32 add / floor_divide / mod / logaddexp and int32 add /
+floor_divide / mod, with a ~ U(-1000, 1000) and b ~ U(1, 50) * (+-1), plus
+the broadcast add (8192, 1) + (1, 32768) float32 ~ N(0, 1).  One step is one
+pass over that op set through the public API (``cp.add(A, B, out=C)`` ...),
+inputs resident in HBM.  ``value`` = algorithmic HBM bytes of the step
+(12 bytes per element per binary op: two 4-byte reads, one 4-byte write;
+the broadcast add counts its output and both inputs) / device time, summed
+over ranks (weak scaling: every rank owns its own 2^28-element operands;
+the elementwise path has no exchange step, so no collective).  Inputs are
+1 GiB per operand, far above the 126 MB L2, so no flush is needed.
+
+Extra keys: ``roofline`` (the dominant kernel timed live with CUDA events;
+peak from MEASURED_PEAKS.json), ``cpu_baseline`` (the numpy oracle port on
+a bounded sample, 1 thread), ``e2e`` (same op set with pinned host inputs
+copied in and results copied out every step), ``clocks`` (nvidia-smi sampled
+during the timed region), ``gpu_launches`` and ``suite`` (per-config GB/s or
+TFLOP/s for C1, C3, C4, C5, each timed with CUDA events after the main run).
+
+``--impl reference`` times the reference's CPU path for the same ops: the
+numpy oracle port (the reference is Python; its Metal path cannot run on
+Linux) over all host threads, on a bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+N_C2 = 1 << 28
+BC_ROWS, BC_COLS = 8192, 32768
+METRIC = "fused elementwise/reduce/scan HBM GB/s (% of 8 TB/s); fp32 matmul TFLOP/s"
+F32_OPS = ("add", "floor_divide", "mod", "logaddexp")
+I32_OPS = ("add", "floor_divide", "mod")
+
+
+def _peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def _env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        idx = local_rank
+        if vis and all(v.strip().isdigit() for v in vis.split(",")):
+            idx = int(vis.split(",")[local_rank])
+        self.idx = idx
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i",
+                 str(self.idx), "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in loaded:
+            for nm, v in zip(names, r[3][1:]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(loaded)}
+
+
+# --------------------------------------------------------------------------- device inputs
+RNG_SRC = r'''
+// SplitMix64 (Steele, Lea, Flood 2014) of (seed, index): seeded synthetic data
+__device__ __forceinline__ unsigned long long sm64(unsigned long long z) {
+  z += 0x9e3779b97f4a7c15ull;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ double u01(unsigned long long h) { return ((h >> 11) + 0.5) * (1.0 / 9007199254740992.0); }
+extern "C" __global__ void gen_f32(float* out, long long n, unsigned long long seed, int kind, float lo, float hi) {
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  long long st = (long long)gridDim.x * blockDim.x;
+  for (; i < n; i += st) {
+    unsigned long long h = sm64(seed * 0x100000001b3ull + (unsigned long long)i);
+    double u = u01(h);
+    float v;
+    if (kind == 0) v = (float)(lo + (hi - lo) * u);                          // uniform
+    else if (kind == 1) {                                                     // normal (Box-Muller)
+      double u2 = u01(sm64(h));
+      v = (float)(sqrt(-2.0 * log(u)) * cospi(2.0 * u2));
+    } else {                                                                  // +-U(lo, hi)
+      double s = (sm64(h ^ 0x5555ull) & 1ull) ? 1.0 : -1.0;
+      v = (float)(s * (lo + (hi - lo) * u));
+    }
+    out[i] = v;
+  }
+}
+extern "C" __global__ void gen_i32(int* out, long long n, unsigned long long seed, int lo, int hi, int signed_) {
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  long long st = (long long)gridDim.x * blockDim.x;
+  for (; i < n; i += st) {
+    unsigned long long h = sm64(seed * 0x100000001b3ull + (unsigned long long)i);
+    int v = lo + (int)(h % (unsigned long long)(hi - lo));
+    if (signed_ && (sm64(h ^ 0x5555ull) & 1ull)) v = -v;
+    out[i] = v;
+  }
+}
+'''
+
+
+class Gen:
+    def __init__(self, cp):
+        self.cp = cp
+        self.kf = cp.RawKernel(RNG_SRC, "gen_f32")
+        self.ki = cp.RawKernel(RNG_SRC, "gen_i32")
+
+    def _launch(self, k, out, args):
+        n = out.size
+        threads = min(n, 148 * 2048)
+        k(max(threads, 1), (out, np.int64(n)) + args)
+
+    def uniform(self, shape, lo, hi, seed):
+        a = self.cp.empty(shape, dtype=np.float32)
+        self._launch(self.kf, a, (np.uint64(seed), np.int32(0), np.float32(lo), np.float32(hi)))
+        return a
+
+    def normal(self, shape, seed):
+        a = self.cp.empty(shape, dtype=np.float32)
+        self._launch(self.kf, a, (np.uint64(seed), np.int32(1), np.float32(0), np.float32(1)))
+        return a
+
+    def signed_uniform(self, shape, lo, hi, seed):
+        a = self.cp.empty(shape, dtype=np.float32)
+        self._launch(self.kf, a, (np.uint64(seed), np.int32(2), np.float32(lo), np.float32(hi)))
+        return a
+
+    def integers(self, shape, lo, hi, seed, signed=False):
+        a = self.cp.empty(shape, dtype=np.int32)
+        self._launch(self.ki, a, (np.uint64(seed), np.int32(lo), np.int32(hi), np.int32(1 if signed else 0)))
+        return a
+
+
+# --------------------------------------------------------------------------- C2 workload
+def c2_inputs(cp, gen, n=N_C2):
+    d = {}
+    d["af"] = gen.uniform((n,), -1000, 1000, 1)
+    d["bf"] = gen.signed_uniform((n,), 1, 50, 2)
+    d["ai"] = gen.integers((n,), -1000, 1000, 3)
+    d["bi"] = gen.integers((n,), 1, 50, 4, signed=True)
+    d["r"] = gen.normal((BC_ROWS, 1), 5)
+    d["c"] = gen.normal((1, BC_COLS), 6)
+    d["of"] = cp.empty((n,), dtype=np.float32)
+    d["oi"] = cp.empty((n,), dtype=np.int32)
+    d["ob"] = cp.empty((BC_ROWS, BC_COLS), dtype=np.float32)
+    return d
+
+
+def c2_ops(cp, d):
+    """[(name, thunk, algorithmic bytes)] of one step."""
+    n = d["af"].size
+    ops = []
+    for nm in F32_OPS:
+        fn = getattr(cp, nm)
+        ops.append((f"{nm}_f32", (lambda fn=fn: fn(d["af"], d["bf"], out=d["of"])), 12 * n))
+    for nm in I32_OPS:
+        fn = getattr(cp, nm)
+        ops.append((f"{nm}_i32", (lambda fn=fn: fn(d["ai"], d["bi"], out=d["oi"])), 12 * n))
+    bcb = 4 * BC_ROWS * BC_COLS + 4 * (BC_ROWS + BC_COLS)
+    ops.append(("bcast_add_f32", lambda: cp.add(d["r"], d["c"], out=d["ob"]), bcb))
+    return ops
+
+
+def step_bytes(n=N_C2):
+    return (len(F32_OPS) + len(I32_OPS)) * 12 * n + 4 * BC_ROWS * BC_COLS + 4 * (BC_ROWS + BC_COLS)
+
+
+# --------------------------------------------------------------------------- CPU legs (oracle port)
+def cpu_c2_pass(n, threads=1, seed=0):
+    """The reference's CPU path for the C2 op set on n elements (numpy port),
+    split over `threads` host threads (numpy releases the GIL in ufuncs)."""
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    af = rng.uniform(-1000, 1000, n).astype(np.float32)
+    bf = (rng.uniform(1, 50, n) * rng.choice([-1, 1], n)).astype(np.float32)
+    ai = rng.integers(-1000, 1000, n).astype(np.int32)
+    bi = (rng.integers(1, 50, n) * rng.choice([-1, 1], n)).astype(np.int32)
+    rows = max(1, int(BC_ROWS * n / N_C2))
+    r = rng.standard_normal((rows, 1)).astype(np.float32)
+    c = rng.standard_normal((1, BC_COLS)).astype(np.float32)
+    fns = [(O.add, af, bf), (O.floor_divide, af, bf), (O.mod, af, bf), (O.logaddexp, af, bf),
+           (O.add, ai, bi), (O.floor_divide, ai, bi), (O.mod, ai, bi)]
+    nbytes = 7 * 12 * n + 4 * rows * BC_COLS + 4 * (rows + BC_COLS)
+
+    def run_chunk(lo, hi):
+        for f, a, b in fns:
+            f(a[lo:hi], b[lo:hi])
+        rl, rh = lo * rows // n, hi * rows // n
+        O.broadcast_add(r[rl:rh], c)
+
+    t0 = time.perf_counter()
+    if threads <= 1:
+        run_chunk(0, n)
+    else:
+        bounds = [n * i // threads for i in range(threads + 1)]
+        ts = [threading.Thread(target=run_chunk, args=(bounds[i], bounds[i + 1])) for i in range(threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+    dt = time.perf_counter() - t0
+    return nbytes, dt
+
+
+def cpu_baseline(sample_n=1 << 24, reps=2):
+    best = None
+    nbytes = 0
+    for _ in range(reps):
+        nbytes, dt = cpu_c2_pass(sample_n, threads=1)
+        best = dt if best is None else min(best, dt)
+    return {"value": round(nbytes / best / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"C2 op set on {sample_n} elements per operand (broadcast add scaled to "
+                      f"{max(1, int(BC_ROWS * sample_n / N_C2))} rows), numpy oracle, 1 thread, best of {reps}"}
+
+
+def run_reference(args):
+    rank, world, _ = _env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    sample = 1 << 25
+    for _ in range(args.warmup):
+        cpu_c2_pass(sample // 4, threads=threads)
+    times, nbytes = [], 0
+    for s in range(args.steps):
+        nbytes, dt = cpu_c2_pass(sample, threads=threads, seed=s)
+        times.append(dt)
+    tot = sum(times)
+    val = nbytes * args.steps / tot / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32",
+        "data": "synthetic (numpy default_rng, seeded)",
+        "config": {"workload": "C2 binary ufuncs + broadcast add (BASELINE configs[1])",
+                   "elements_per_operand": N_C2, "sample_per_step": sample},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} elements per operand per step, {threads} threads"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-suite", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank, world, local = _env()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import macmetalpy_b200 as cp
+    from macmetalpy_b200._cuda_backend import CudaBackend, Event
+
+    be = CudaBackend()
+    gen = Gen(cp)
+    d = c2_inputs(cp, gen)
+    ops = c2_ops(cp, d)
+
+    def barrier():
+        be.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        for _, f, _ in ops:
+            f()
+    barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    evs = [[Event() for _ in range(len(ops) + 1)] for _ in range(args.steps)]
+    barrier()
+    t_start = Event()
+    t_end = Event()
+    t_start.record()
+    for s in range(args.steps):
+        evs[s][0].record()
+        for j, (_, f, _) in enumerate(ops):
+            f()
+            evs[s][j + 1].record()
+    t_end.record()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = t_start.elapsed_ms(t_end)
+    per_op = [0.0] * len(ops)
+    for s in range(args.steps):
+        for j in range(len(ops)):
+            per_op[j] += evs[s][j].elapsed_ms(evs[s][j + 1])
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sb = step_bytes()
+    value = world * sb * args.steps / (ms / 1e3) / 1e9
+    peaks, peak_kind = _peaks()
+    hbm = float(peaks["hbm_gbs"])
+    dom = max(range(len(ops)), key=lambda j: per_op[j])
+    dom_ms = per_op[dom] / args.steps
+    dom_gbs = ops[dom][2] / (dom_ms / 1e3) / 1e9
+    op_table = {ops[j][0]: round(ops[j][2] / (per_op[j] / args.steps / 1e3) / 1e9, 1) for j in range(len(ops))}
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32",
+        "data": "synthetic, device-generated SplitMix64 streams (seeded), BASELINE distributions",
+        "config": {"workload": "C2: binary ufuncs at 2^28 (add/floor_divide/mod/logaddexp f32, "
+                               "add/floor_divide/mod i32) + broadcast add (8192,1)+(1,32768) f32",
+                   "elements_per_operand_per_gpu": N_C2, "l2": "inputs 1 GiB per operand > 126 MB L2, no flush",
+                   "parallelism": f"shard-local x{world}", "api": "cp.<ufunc>(a, b, out=c)"},
+        "frac_of_hbm_peak": round(value / world / hbm, 4),
+        "per_op_gbs": op_table,
+        "roofline": {"bound": "hbm", "kernel": f"mmp_fused_ew ({ops[dom][0]})", "achieved": round(dom_gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(dom_gbs / hbm, 4),
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": _traffic(ops[dom][0]),
+                     "algorithmic_bytes_per_launch": ops[dom][2], "avg_launch_ms": round(dom_ms, 4)},
+        "clocks": clocks,
+        "gpu_launches": args.steps * len(ops),
+    }
+    if rank == 0 and not args.no_e2e:
+        line["e2e"] = e2e_c2(cp, d, steps=2)
+    if rank == 0 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0 and not args.no_suite and world == 1:
+        del d, ops
+        import gc
+
+        gc.collect()
+        line["suite"] = run_suite(cp, gen)
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _traffic(opname):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    p = os.path.join(REPO, "profiles", "c2_elementwise_ncu.md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.startswith(f"| {opname} |"):
+            parts = [x.strip() for x in ln.strip().strip("|").split("|")]
+            try:
+                return int(float(parts[1]))
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+def e2e_c2(cp, d, steps=2):
+    """Same op set through the public API with host buffers: every step
+    copies its inputs from pinned host memory and its results back."""
+    from macmetalpy_b200 import _cuda_backend as cb
+    from macmetalpy_b200._cuda_backend import Event
+
+    names = ("af", "bf", "ai", "bi", "r", "c")
+    host = {}
+    for k in names:
+        a = d[k]
+        p = ctypes.c_void_p()
+        cb.check(cb.lib.mmp_host_alloc(a.nbytes, ctypes.byref(p)))
+        host[k] = (p, np.ctypeslib.as_array((ctypes.c_char * a.nbytes).from_address(p.value)).view(a.dtype))
+        cb.check(cb.lib.mmp_d2h(p, ctypes.c_void_p(a._ptr), a.nbytes))
+    outs = {}
+    for k in ("of", "oi", "ob"):
+        a = d[k]
+        p = ctypes.c_void_p()
+        cb.check(cb.lib.mmp_host_alloc(a.nbytes, ctypes.byref(p)))
+        outs[k] = p
+    h2d = sum(d[k].nbytes for k in names)
+    d2h = 4 * d["of"].nbytes + 3 * d["oi"].nbytes + d["ob"].nbytes
+    ops = c2_ops(cp, d)
+    out_of = ["of"] * 4 + ["oi"] * 3 + ["ob"]
+
+    def one_step():
+        for k in names:
+            cb.check(cb.lib.mmp_h2d(ctypes.c_void_p(d[k]._ptr), host[k][0], d[k].nbytes))
+        for (nm, f, _), ok in zip(ops, out_of):
+            f()
+            cb.check(cb.lib.mmp_d2h(outs[ok], ctypes.c_void_p(d[ok]._ptr), d[ok].nbytes))
+
+    one_step()
+    s, e = Event(), Event()
+    cp.synchronize()
+    s.record()
+    for _ in range(steps):
+        one_step()
+    e.record()
+    ms = s.elapsed_ms(e)
+    for k in names:
+        cb.lib.mmp_host_free(host[k][0])
+    for k in outs:
+        cb.lib.mmp_host_free(outs[k])
+    return {"value": round(step_bytes() * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "ms_per_step": round(ms / steps, 2)}
+
+
+def _time(cp, fn, iters=5, warm=2):
+    from macmetalpy_b200._cuda_backend import Event
+
+    for _ in range(warm):
+        fn()
+    cp.synchronize()
+    s, e = Event(), Event()
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    return s.elapsed_ms(e) / iters
+
+
+def run_suite(cp, gen):
+    """Per-config throughput (device time, CUDA events) for C1, C3, C4, C5."""
+    hbm = float(_peaks()[0]["hbm_gbs"])
+    out = {}
+
+    def gbs(nbytes, ms):
+        return {"gbs": round(nbytes / (ms / 1e3) / 1e9, 1), "ms": round(ms, 4),
+                "frac": round(nbytes / (ms / 1e3) / 1e9 / hbm, 3)}
+
+    # C1 (2^20, latency-bound) and the same expression at 2^28 (HBM claim)
+    for n, tag in ((1 << 20, "c1_2^20"), (1 << 28, "c1_2^28")):
+        x = gen.normal((n,), 11)
+        y = lambda: cp.sqrt(cp.abs(x)) + cp.exp(-x ** 2)
+        out[f"{tag}_fused_sum"] = gbs(4 * n, _time(cp, lambda: cp.sum(y()), iters=10))
+        out[f"{tag}_fused_mean"] = gbs(4 * n, _time(cp, lambda: cp.mean(y()), iters=10))
+        del x
+    # C3 reductions on (16384, 16384)
+    A = gen.normal((16384, 16384), 21)
+    nb = A.nbytes
+    for nm, fn in (("sum", cp.sum), ("mean", cp.mean), ("var", cp.var), ("argmax", cp.argmax)):
+        out[f"c3_{nm}"] = gbs(nb, _time(cp, lambda fn=fn: fn(A)))
+        for ax in (0, 1):
+            out[f"c3_{nm}_axis{ax}"] = gbs(nb, _time(cp, lambda fn=fn, ax=ax: fn(A, axis=ax)))
+    B = gen.integers((16384, 16384), -100, 101, 22)
+    out["c3_int32_sum"] = gbs(nb, _time(cp, lambda: cp.sum(B)))
+    del B
+    An = A.copy()
+    gen_mask = gen.uniform((16384, 16384), 0, 1, 23)
+    An[...] = cp.where(gen_mask < 0.01, np.float32(np.nan), An)
+    del gen_mask
+    out["c3_nansum"] = gbs(nb, _time(cp, lambda: cp.nansum(An)))
+    out["c3_nanmean"] = gbs(nb, _time(cp, lambda: cp.nanmean(An)))
+    del A, An
+    # C4 scans
+    n = 1 << 30
+    xi = gen.integers((n,), -100, 101, 31)
+    out["c4_cumsum_int32_2^30"] = gbs(12 * n, _time(cp, lambda: cp.cumsum(xi), iters=3))
+    del xi
+    xf = gen.uniform((n,), 0, 1, 32)
+    out["c4_cumsum_f32_2^30"] = gbs(8 * n, _time(cp, lambda: cp.cumsum(xf), iters=3))
+    del xf
+    X2 = gen.normal((4096, 65536), 33)
+    out["c4_cumsum_axis1_4096x65536"] = gbs(8 * X2.size, _time(cp, lambda: cp.cumsum(X2, axis=1), iters=3))
+    del X2
+    # C5 matmul
+    def tflops(flops, ms):
+        return {"tflops": round(flops / (ms / 1e3) / 1e12, 2), "ms": round(ms, 3)}
+
+    Ma = gen.normal((16384, 16384), 41) * np.float32(1 / 128)
+    Mb = gen.normal((16384, 16384), 42) * np.float32(1 / 128)
+    Ma, Mb = Ma.copy(), Mb.copy()
+    out["c5_f32_16384"] = tflops(2 * 16384 ** 3, _time(cp, lambda: cp.matmul(Ma, Mb), iters=2, warm=1))
+    del Ma, Mb
+    Ba = (gen.normal((64, 1024, 1024), 43) * np.float32(1 / 32)).copy()
+    Bb = (gen.normal((64, 1024, 1024), 44) * np.float32(1 / 32)).copy()
+    out["c5_f32_batched_64x1024"] = tflops(2 * 64 * 1024 ** 3, _time(cp, lambda: cp.matmul(Ba, Bb), iters=3))
+    del Ba, Bb
+    Ha = (gen.normal((8192, 8192), 45) * np.float32(1 / 90.5)).astype(np.float16)
+    Hb = (gen.normal((8192, 8192), 46) * np.float32(1 / 90.5)).astype(np.float16)
+    out["c5_f16_8192"] = tflops(2 * 8192 ** 3, _time(cp, lambda: cp.matmul(Ha, Hb), iters=3))
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

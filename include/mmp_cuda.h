@@ -1,0 +1,161 @@
+/*
+ * mmp_cuda.h -- C ABI of libmmp_cuda.so, the B200 (sm_100a) backend of the
+ * macmetalpy_b200 array hot path.
+ *
+ * The reference reaches its GPU through the un-vendored metalgpu bridge,
+ * whose ctypes declarations are at src/macmetalpy/_metal_backend.py:221-263
+ * (init, createBuffer, releaseBuffer, getBufferPointer,
+ * createLibraryFromString, setFunction, runFunction, ...).  Each entry point
+ * below names the reference interface it replaces.  Every function returns 0
+ * on success or a negative MMP_E_* code; the message of the last failure on
+ * the calling thread is available from mmp_last_error().  All work is
+ * enqueued on one stream per device (stream-ordered, asynchronous unless the
+ * function says it synchronises).  Pointers are plain device addresses;
+ * sizes are bytes unless named otherwise.  No torch types cross this ABI.
+ */
+#ifndef MMP_CUDA_H
+#define MMP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MMP_ABI_VERSION 1
+
+/* status codes */
+#define MMP_OK 0
+#define MMP_E_CUDA (-1)      /* a CUDA runtime / driver call failed          */
+#define MMP_E_ARG (-2)       /* invalid argument (shape, dtype, pointer)     */
+#define MMP_E_NVRTC (-3)     /* NVRTC compile failed; log in the log buffer  */
+#define MMP_E_UNSUPPORTED (-4)
+#define MMP_E_DEVICE (-5)    /* a kernel reported an error (bounded wait)    */
+
+/* dtype codes (numpy kinds the reference supports, _dtypes.py:21-31, plus
+ * int8/uint8 and float64 which B200 computes natively) */
+enum mmp_dtype {
+  MMP_BOOL = 0, MMP_INT8 = 1, MMP_UINT8 = 2, MMP_INT16 = 3, MMP_UINT16 = 4,
+  MMP_INT32 = 5, MMP_UINT32 = 6, MMP_INT64 = 7, MMP_UINT64 = 8,
+  MMP_FLOAT16 = 9, MMP_FLOAT32 = 10, MMP_FLOAT64 = 11
+};
+
+/* reduction ops: the reference's reduce_sum/max/min/prod (_kernels.py:422-565),
+ * mean/var/std (ndarray.py:1779-1834), argmax/argmin (_kernels.py:1189-1257),
+ * nan reductions (_kernels.py:612-730, nan_ops.py:112-432) */
+enum mmp_reduce_op {
+  MMP_R_SUM = 0, MMP_R_PROD = 1, MMP_R_MAX = 2, MMP_R_MIN = 3,
+  MMP_R_MEAN = 4, MMP_R_VAR = 5, MMP_R_STD = 6,
+  MMP_R_ARGMAX = 7, MMP_R_ARGMIN = 8,
+  MMP_R_NANSUM = 9, MMP_R_NANMEAN = 10, MMP_R_NANMAX = 11, MMP_R_NANMIN = 12,
+  MMP_R_ANY = 13, MMP_R_ALL = 14
+};
+
+/* scan ops: prefix_sum / prefix_prod (_kernels.py:1148-1170, 1263-1358) */
+enum mmp_scan_op { MMP_S_SUM = 0, MMP_S_PROD = 1 };
+
+/* gemm modes (matmul_op, _kernels.py:735-759) */
+enum mmp_gemm_mode {
+  MMP_GEMM_AUTO = 0,    /* f32 -> 3xTF32 tensor cores, f16 -> f16 tensor cores */
+  MMP_GEMM_3XTF32 = 1,  /* f32 split into big+small TF32 parts, 3 MMAs/tile   */
+  MMP_GEMM_TF32 = 2,    /* f32 rounded to TF32, 1 MMA/tile (fast, ~1e-3)      */
+  MMP_GEMM_F16 = 3,     /* f16 inputs, f32 accumulation in TMEM               */
+  MMP_GEMM_SIMT = 4     /* CUDA-core fallback (any dtype, any stride)         */
+};
+
+/* Merged partial of a full reduction, written when `partial` is non-NULL so
+ * that block-distributed arrays can combine shards across GPUs.  Field use
+ * depends on the op (see mmp_reduce). */
+typedef struct mmp_partial {
+  double s1;       /* sum / shifted first moment / value (as double)          */
+  double s2;       /* shifted second moment (var/std)                          */
+  double shift;    /* shift K used for the moments (var/std)                   */
+  int64_t count;   /* element count (nan ops: non-NaN count)                   */
+  int64_t ival;    /* exact integer sum/prod, or the int value (max/min/arg)   */
+  int64_t index;   /* argmax/argmin flat index, -1 if none                     */
+} mmp_partial;
+
+/* ---- library / device (replaces init/deleteInstance, _metal_backend.py:221-226) */
+int mmp_abi_version(void);
+const char *mmp_last_error(void);
+int mmp_device_count(int *count);
+/* Make `device` current on this thread, create its stream and configure its
+ * stream-ordered memory pool (MetalBackend._setup, _metal_backend.py:197-219). */
+int mmp_init(int device);
+int mmp_get_device(int *device);
+int mmp_sm_count(int *sms);
+/* The stream all work of the current device is enqueued on. */
+int mmp_get_stream(void **stream);
+/* Replace the current device's stream (e.g. with a torch/NCCL stream). */
+int mmp_set_stream(void *stream);
+
+/* ---- memory (createBuffer/releaseBuffer/getBufferPointer, _metal_backend.py:227-240) */
+int mmp_malloc(size_t bytes, void **ptr);     /* stream-ordered cudaMallocAsync  */
+int mmp_free(void *ptr);                      /* stream-ordered cudaFreeAsync    */
+int mmp_memset(void *ptr, int value, size_t bytes);
+int mmp_h2d(void *dst, const void *src, size_t bytes);  /* async on the stream  */
+int mmp_d2h(void *dst, const void *src, size_t bytes);  /* synchronises         */
+int mmp_d2d(void *dst, const void *src, size_t bytes);
+int mmp_host_alloc(size_t bytes, void **ptr);  /* pinned host memory           */
+int mmp_host_free(void *ptr);
+/* Per-device scratch region for multi-block kernels (partials + tickets).
+ * Returned memory is reused by every call on the device (stream-ordered). */
+int mmp_scratch(size_t bytes, void **ptr, void **tickets);
+
+/* ---- synchronisation (synchronize, _metal_backend.py:359-372) */
+int mmp_synchronize(void);
+/* Synchronise, then read and clear the device-side error word that kernels
+ * with bounded waits set instead of hanging (0 = no error). */
+int mmp_check_device_error(int *code);
+
+/* ---- timing */
+int mmp_event_create(void **event);
+int mmp_event_destroy(void *event);
+int mmp_event_record(void *event);
+int mmp_event_elapsed_ms(void *start, void *end, float *ms);
+
+/* ---- runtime compilation (createLibraryFromString/setFunction/runFunction,
+ *      _metal_backend.py:241-257): NVRTC for sm_100a, cached by source+options.
+ * `options` is a '\n'-separated list.  `func` receives a launchable handle. */
+int mmp_compile(const char *source, const char *name, const char *options,
+                void **func, char *log, size_t log_size);
+int mmp_launch(void *func, const unsigned grid[3], const unsigned block[3],
+               unsigned shared_bytes, void **args);
+
+/* ---- typed hot-path kernels */
+
+/* Full reduction of n contiguous elements (ndarray._reduce, ndarray.py:1895-1963;
+ * reductions.argmax, reductions.py:381-418; nan_ops._nan_reduce, nan_ops.py:72-100).
+ * Writes one element of out_dtype to `out` (argmax/argmin: int64 index).
+ * ddof is used by VAR/STD only.  `partial` may be NULL. */
+int mmp_reduce(int op, int dtype, const void *x, int64_t n, int out_dtype,
+               void *out, double ddof, mmp_partial *partial);
+
+/* Reduction over the middle axis of a C-contiguous (outer, k, inner) view
+ * (ndarray._reduce_axis, ndarray.py:2015-2066); out is (outer, inner). */
+int mmp_reduce_axis(int op, int dtype, const void *x, int64_t outer, int64_t k,
+                    int64_t inner, int out_dtype, void *out, double ddof);
+
+/* Inclusive scan along the middle axis of a C-contiguous (outer, k, inner)
+ * view (ndarray._prefix_scan, ndarray.py:2068-2152); y has the same shape in
+ * out_dtype, which must be numpy's accumulation type (int64 for signed ints
+ * and bool, uint64 for unsigned, the input type for floats).  For a 1-D scan
+ * (outer == 1, inner == 1) carry_in, when non-NULL, points to one value in
+ * device memory of the carry type (float64 for float inputs, int64/uint64
+ * for integers) that is combined into every output (distributed scans). */
+int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y,
+             int64_t outer, int64_t k, int64_t inner, const void *carry_in);
+
+/* Row-major C[b] = A[b] @ B[b] for b < batch (ndarray.__matmul__,
+ * ndarray.py:1398-1450; linalg_top.matmul, linalg_top.py:94-111).
+ * Leading dimensions and batch strides are in elements. */
+int mmp_gemm(int dtype, int mode, int64_t batch, int64_t m, int64_t n,
+             int64_t k, const void *a, int64_t lda, int64_t stride_a,
+             const void *b, int64_t ldb, int64_t stride_b, void *c,
+             int64_t ldc, int64_t stride_c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MMP_CUDA_H */

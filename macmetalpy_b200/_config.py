@@ -1,0 +1,62 @@
+"""Global configuration (mirrors ``src/macmetalpy/_config.py:11-64``).
+
+Keys and defaults are the reference's.  ``float64_behavior`` keeps its two
+values; on B200 float64 is computed natively on the GPU, so
+``"cpu_fallback"`` (the default) means "keep float64" and ``"downcast"``
+means "compute in float32", which is how the reference resolves dtypes
+(``_dtypes.resolve_dtype``).  ``fast_math`` compiles fused kernels with
+``--use_fast_math``.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Literal
+
+__all__ = ["MacMetalConfig", "get_config", "set_config"]
+
+
+class MacMetalConfig:
+    """Process-wide configuration singleton."""
+
+    _instance: "MacMetalConfig | None" = None
+    _lock = threading.Lock()
+
+    def __new__(cls) -> "MacMetalConfig":
+        with cls._lock:
+            if cls._instance is None:
+                inst = super().__new__(cls)
+                inst.float64_behavior = "cpu_fallback"
+                inst.warn_on_downcast = True
+                inst.default_float_dtype = "float32"
+                inst.fast_math = False
+                cls._instance = inst
+            return cls._instance
+
+
+def get_config() -> MacMetalConfig:
+    """Return the global configuration singleton."""
+    return MacMetalConfig()
+
+
+def set_config(
+    *,
+    float64_behavior: Literal["downcast", "cpu_fallback"] | None = None,
+    warn_on_downcast: bool | None = None,
+    default_float_dtype: str | None = None,
+    fast_math: bool | None = None,
+) -> None:
+    """Update global configuration values (same keys as the reference)."""
+    cfg = get_config()
+    if float64_behavior is not None:
+        if float64_behavior not in ("downcast", "cpu_fallback"):
+            raise ValueError(
+                f"float64_behavior must be 'downcast' or 'cpu_fallback', got {float64_behavior!r}"
+            )
+        cfg.float64_behavior = float64_behavior
+    if warn_on_downcast is not None:
+        cfg.warn_on_downcast = warn_on_downcast
+    if default_float_dtype is not None:
+        cfg.default_float_dtype = default_float_dtype
+    if fast_math is not None:
+        cfg.fast_math = fast_math

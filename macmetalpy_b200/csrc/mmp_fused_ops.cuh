@@ -1,0 +1,250 @@
+// Scalar element functions used by the kernels the fusion engine emits.
+//
+// The reference builds each fused op from an MSL template
+// (src/macmetalpy/_fusion.py:86-264) and its eager shaders
+// (_kernels.py:21-404).  Its Metal results are not those of its own CPU
+// path in several places (integer floor_divide truncates, _kernels.py:44;
+// float floor_divide is floor(a/b), _kernels.py:32).  The functions here
+// reproduce the CPU path (numpy calls), bit for bit on the integer and
+// division ops:
+//   * float floor_divide: numpy's fmod-based divmod with sign and rounding
+//     fix-ups (numpy npy_math: npy_divmod / npy_floor_divide, the same steps
+//     as CPython's float_divmod); f_remainder is numpy's remainder;
+//   * `%` / mod / remainder: the reference's composite
+//     x1 - floor_divide(x1, x2) * x2 (math_ops.py:540-548), see ref_mod_f;
+//   * integer floor_divide / remainder: floor semantics, division by zero
+//     gives 0, INT_MIN // -1 gives INT_MIN;
+//   * maximum/minimum propagate NaN, fmax/fmin ignore it, with numpy's
+//     comparison order (so signed zeros come out as numpy's do);
+//   * logaddexp / logaddexp2: numpy's max + log1p(exp(-|d|)) form.
+// Float math calls CUDA's libdevice functions (not reproduced here).
+#pragma once
+#include "mmp_device.cuh"
+
+namespace mmpf {
+using mmpd::isnan_;
+
+// ---- math dispatch on float / double
+__device__ __forceinline__ float m_sqrt(float x) { return sqrtf(x); }
+__device__ __forceinline__ double m_sqrt(double x) { return sqrt(x); }
+__device__ __forceinline__ float m_exp(float x) { return expf(x); }
+__device__ __forceinline__ double m_exp(double x) { return exp(x); }
+__device__ __forceinline__ float m_log(float x) { return logf(x); }
+__device__ __forceinline__ double m_log(double x) { return log(x); }
+__device__ __forceinline__ float m_sin(float x) { return sinf(x); }
+__device__ __forceinline__ double m_sin(double x) { return sin(x); }
+__device__ __forceinline__ float m_cos(float x) { return cosf(x); }
+__device__ __forceinline__ double m_cos(double x) { return cos(x); }
+__device__ __forceinline__ float m_tan(float x) { return tanf(x); }
+__device__ __forceinline__ double m_tan(double x) { return tan(x); }
+__device__ __forceinline__ float m_asin(float x) { return asinf(x); }
+__device__ __forceinline__ double m_asin(double x) { return asin(x); }
+__device__ __forceinline__ float m_acos(float x) { return acosf(x); }
+__device__ __forceinline__ double m_acos(double x) { return acos(x); }
+__device__ __forceinline__ float m_atan(float x) { return atanf(x); }
+__device__ __forceinline__ double m_atan(double x) { return atan(x); }
+__device__ __forceinline__ float m_sinh(float x) { return sinhf(x); }
+__device__ __forceinline__ double m_sinh(double x) { return sinh(x); }
+__device__ __forceinline__ float m_cosh(float x) { return coshf(x); }
+__device__ __forceinline__ double m_cosh(double x) { return cosh(x); }
+__device__ __forceinline__ float m_tanh(float x) { return tanhf(x); }
+__device__ __forceinline__ double m_tanh(double x) { return tanh(x); }
+__device__ __forceinline__ float m_log2(float x) { return log2f(x); }
+__device__ __forceinline__ double m_log2(double x) { return log2(x); }
+__device__ __forceinline__ float m_log10(float x) { return log10f(x); }
+__device__ __forceinline__ double m_log10(double x) { return log10(x); }
+__device__ __forceinline__ float m_exp2(float x) { return exp2f(x); }
+__device__ __forceinline__ double m_exp2(double x) { return exp2(x); }
+__device__ __forceinline__ float m_expm1(float x) { return expm1f(x); }
+__device__ __forceinline__ double m_expm1(double x) { return expm1(x); }
+__device__ __forceinline__ float m_log1p(float x) { return log1pf(x); }
+__device__ __forceinline__ double m_log1p(double x) { return log1p(x); }
+__device__ __forceinline__ float m_cbrt(float x) { return cbrtf(x); }
+__device__ __forceinline__ double m_cbrt(double x) { return cbrt(x); }
+__device__ __forceinline__ float m_asinh(float x) { return asinhf(x); }
+__device__ __forceinline__ double m_asinh(double x) { return asinh(x); }
+__device__ __forceinline__ float m_acosh(float x) { return acoshf(x); }
+__device__ __forceinline__ double m_acosh(double x) { return acosh(x); }
+__device__ __forceinline__ float m_atanh(float x) { return atanhf(x); }
+__device__ __forceinline__ double m_atanh(double x) { return atanh(x); }
+__device__ __forceinline__ float m_floor(float x) { return floorf(x); }
+__device__ __forceinline__ double m_floor(double x) { return floor(x); }
+__device__ __forceinline__ float m_ceil(float x) { return ceilf(x); }
+__device__ __forceinline__ double m_ceil(double x) { return ceil(x); }
+__device__ __forceinline__ float m_trunc(float x) { return truncf(x); }
+__device__ __forceinline__ double m_trunc(double x) { return trunc(x); }
+__device__ __forceinline__ float m_rint(float x) { return rintf(x); }
+__device__ __forceinline__ double m_rint(double x) { return rint(x); }
+__device__ __forceinline__ float m_fabs(float x) { return fabsf(x); }
+__device__ __forceinline__ double m_fabs(double x) { return fabs(x); }
+__device__ __forceinline__ float m_fmod(float a, float b) { return fmodf(a, b); }
+__device__ __forceinline__ double m_fmod(double a, double b) { return fmod(a, b); }
+__device__ __forceinline__ float m_pow(float a, float b) { return powf(a, b); }
+__device__ __forceinline__ double m_pow(double a, double b) { return pow(a, b); }
+__device__ __forceinline__ float m_atan2(float a, float b) { return atan2f(a, b); }
+__device__ __forceinline__ double m_atan2(double a, double b) { return atan2(a, b); }
+__device__ __forceinline__ float m_hypot(float a, float b) { return hypotf(a, b); }
+__device__ __forceinline__ double m_hypot(double a, double b) { return hypot(a, b); }
+__device__ __forceinline__ float m_copysign(float a, float b) { return copysignf(a, b); }
+__device__ __forceinline__ double m_copysign(double a, double b) { return copysign(a, b); }
+__device__ __forceinline__ float m_nextafter(float a, float b) { return nextafterf(a, b); }
+__device__ __forceinline__ double m_nextafter(double a, double b) { return nextafter(a, b); }
+
+template <class R> struct Consts;
+template <> struct Consts<float> {
+  __device__ static float loge2() { return 0.693147180559945309417232121458176568f; }
+  __device__ static float log2e() { return 1.442695040888963407359924681001892137f; }
+  __device__ static float nan() { return __int_as_float(0x7fc00000); }
+};
+template <> struct Consts<double> {
+  __device__ static double loge2() { return 0.693147180559945309417232121458176568; }
+  __device__ static double log2e() { return 1.442695040888963407359924681001892137; }
+  __device__ static double nan() { return __longlong_as_double(0x7ff8000000000000ll); }
+};
+
+// ---- float divmod (numpy npy_divmod)
+template <class R>
+__device__ __forceinline__ R f_floor_divide(R a, R b) {
+  if (b == R(0)) return a / b;  // inf or nan, as numpy
+  R mod = m_fmod(a, b);
+  R div = (a - mod) / b;
+  if (mod != R(0)) {
+    if ((b < R(0)) != (mod < R(0))) {
+      mod += b;
+      div -= R(1);
+    }
+  }
+  R floordiv;
+  if (div != R(0)) {
+    floordiv = m_floor(div);
+    if (div - floordiv > R(0.5)) floordiv += R(1);
+  } else {
+    floordiv = m_copysign(R(0), a / b);
+  }
+  return floordiv;
+}
+
+template <class R>
+__device__ __forceinline__ R f_remainder(R a, R b) {
+  R mod = m_fmod(a, b);
+  if (b == R(0)) return mod;  // nan
+  if (mod != R(0)) {
+    if ((b < R(0)) != (mod < R(0))) mod += b;
+  } else {
+    mod = m_copysign(R(0), b);
+  }
+  return mod;
+}
+
+// ---- integer floor division / remainder (numpy semantics)
+template <class I>
+__device__ __forceinline__ I i_floor_divide(I a, I b) {
+  if (b == I(0)) return I(0);
+  if (mmpd::IsSigned<I>::value) {
+    if (b == I(-1)) return (I)(I(0) - a);  // wraps INT_MIN to INT_MIN
+    I q = a / b;
+    if ((a % b != I(0)) && ((a < I(0)) != (b < I(0)))) q -= I(1);
+    return q;
+  }
+  return a / b;
+}
+
+template <class I>
+__device__ __forceinline__ I i_remainder(I a, I b) {
+  if (b == I(0)) return I(0);
+  if (mmpd::IsSigned<I>::value) {
+    if (b == I(-1)) return I(0);
+    I r = a % b;
+    if (r != I(0) && ((r < I(0)) != (b < I(0)))) r += b;
+    return r;
+  }
+  return a % b;
+}
+
+// The reference's mod / remainder / `%` is the composite
+// x1 - floor_divide(x1, x2) * x2 (src/macmetalpy/math_ops.py:540-548), each
+// step rounded to the array dtype T as its CPU path (numpy) evaluates it.
+// This is not np.remainder for floats; it is what the reference returns.
+template <class T, class R>
+__device__ __forceinline__ R ref_mod_f(R a, R b) {
+  R fd = mmpd::cvt<R>(mmpd::cvt<T>(f_floor_divide<R>(a, b)));
+  R t = mmpd::cvt<R>(mmpd::cvt<T>(fd * b));
+  return a - t;
+}
+template <class I>
+__device__ __forceinline__ I ref_mod_i(I a, I b) {
+  I fd = i_floor_divide<I>(a, b);
+  I t = (I)(fd * b);
+  return (I)(a - t);
+}
+
+template <class I>
+__device__ __forceinline__ I i_fmod(I a, I b) {
+  if (b == I(0)) return I(0);
+  if (mmpd::IsSigned<I>::value && b == I(-1)) return I(0);
+  return a % b;
+}
+
+// integer power by squaring; negative exponents give 0 (numpy raises)
+template <class I>
+__device__ __forceinline__ I i_power(I a, I b) {
+  if (mmpd::IsSigned<I>::value && b < I(0)) return I(0);
+  I r = I(1);
+  I base = a;
+  unsigned long long e = (unsigned long long)b;
+  while (e) {
+    if (e & 1ull) r = (I)(r * base);
+    base = (I)(base * base);
+    e >>= 1;
+  }
+  return r;
+}
+
+// ---- max/min with numpy's NaN rules
+template <class R>
+__device__ __forceinline__ R maximum(R a, R b) { return (a >= b || isnan_(a)) ? a : b; }
+template <class R>
+__device__ __forceinline__ R minimum(R a, R b) { return (a <= b || isnan_(a)) ? a : b; }
+template <class R>
+__device__ __forceinline__ R fmax_(R a, R b) { return (a >= b || isnan_(b)) ? a : b; }
+template <class R>
+__device__ __forceinline__ R fmin_(R a, R b) { return (a <= b || isnan_(b)) ? a : b; }
+
+// ---- logaddexp (numpy npy_logaddexp / npy_logaddexp2)
+template <class R>
+__device__ __forceinline__ R logaddexp(R x, R y) {
+  if (x == y) return x + Consts<R>::loge2();  // equal infinities without nan
+  R tmp = x - y;
+  if (tmp > R(0)) return x + m_log1p(m_exp(-tmp));
+  if (tmp <= R(0)) return y + m_log1p(m_exp(tmp));
+  return tmp;  // nan
+}
+template <class R>
+__device__ __forceinline__ R log2_1p(R x) { return Consts<R>::log2e() * m_log1p(x); }
+template <class R>
+__device__ __forceinline__ R logaddexp2(R x, R y) {
+  if (x == y) return x + R(1);
+  R tmp = x - y;
+  if (tmp > R(0)) return x + log2_1p(m_exp2(-tmp));
+  if (tmp <= R(0)) return y + log2_1p(m_exp2(tmp));
+  return tmp;
+}
+
+template <class R>
+__device__ __forceinline__ R sign_(R a) {
+  return a > R(0) ? R(1) : (a < R(0) ? R(-1) : (a == R(0) ? R(0) : a));
+}
+
+template <class R>
+__device__ __forceinline__ R heaviside(R a, R h) {
+  if (isnan_(a)) return a;
+  if (a == R(0)) return h;
+  return a < R(0) ? R(0) : R(1);
+}
+
+template <class I>
+__device__ __forceinline__ I i_abs(I a) {
+  return (mmpd::IsSigned<I>::value && a < I(0)) ? (I)(I(0) - a) : a;
+}
+
+}  // namespace mmpf

@@ -1,0 +1,50 @@
+// Internal helpers shared by the translation units of libmmp_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+
+#include "../../include/mmp_cuda.h"
+
+namespace mmp {
+
+// Record `msg` as this thread's last error and return `code`.
+int set_error(int code, const std::string &msg);
+int cuda_error(cudaError_t e, const char *what);
+
+// Stream of the current device (created by mmp_init on first use).
+cudaStream_t stream();
+int current_device();
+int sm_count();
+// Per-device scratch: at least `bytes` of reusable device memory plus an
+// array of 4096 zero-initialised 32-bit tickets.  Kernels that take a
+// ticket leave it at zero when they finish.
+int scratch(size_t bytes, void **ptr, unsigned **tickets);
+// Device-side error word (bounded waits set it instead of hanging).
+int *device_error_word();
+
+}  // namespace mmp
+
+#define MMP_CUDA_TRY(call)                                   \
+  do {                                                       \
+    cudaError_t _e = (call);                                 \
+    if (_e != cudaSuccess) return mmp::cuda_error(_e, #call); \
+  } while (0)
+
+#define MMP_LAUNCH_CHECK(what)                                  \
+  do {                                                          \
+    cudaError_t _e = cudaGetLastError();                        \
+    if (_e != cudaSuccess) return mmp::cuda_error(_e, what);    \
+  } while (0)
+
+// Size in bytes of an mmp_dtype code (0 for an unknown code).
+static inline size_t mmp_dtype_size(int dt) {
+  switch (dt) {
+    case MMP_BOOL: case MMP_INT8: case MMP_UINT8: return 1;
+    case MMP_INT16: case MMP_UINT16: case MMP_FLOAT16: return 2;
+    case MMP_INT32: case MMP_UINT32: case MMP_FLOAT32: return 4;
+    case MMP_INT64: case MMP_UINT64: case MMP_FLOAT64: return 8;
+    default: return 0;
+  }
+}

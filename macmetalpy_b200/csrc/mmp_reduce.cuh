@@ -1,0 +1,729 @@
+// Reduction kernels for sm_100a: full (one launch, last block finishes),
+// per-row (axis over contiguous elements) and per-column (axis with a
+// contiguous inner extent, split along the reduced axis when the column
+// count alone cannot fill the GPU).
+//
+// Reference kernels these replace: reduce_sum/max/min/prod and reduce_dot
+// (src/macmetalpy/_kernels.py:422-594, a multi-launch tree driven from
+// ndarray._reduce at ndarray.py:1927-1946), nan_reduce_* (_kernels.py:612-730,
+// partials finished on the CPU at nan_ops.py:89-98), the one-thread-per-row
+// axis kernels (_kernels.py:1062-1146, after a transpose copy at
+// ndarray.py:2039-2047) and the two-pass argmax (_kernels.py:1189-1257).
+// Results follow numpy (the reference's CPU path): int sums accumulate in
+// 64 bits, argmax/argmin take the first index of the extreme value and the
+// first NaN wins, mean/var are computed in double.
+//
+// The element loader `L` is a template parameter: the precompiled kernels
+// read a contiguous array, the fusion engine passes a loader that evaluates
+// an elementwise expression, so `sum(f(x))` reads x once and never writes
+// f(x) to memory.
+#pragma once
+#include "mmp_device.cuh"
+
+#define MMP_R_SUM 0
+#define MMP_R_PROD 1
+#define MMP_R_MAX 2
+#define MMP_R_MIN 3
+#define MMP_R_MEAN 4
+#define MMP_R_VAR 5
+#define MMP_R_STD 6
+#define MMP_R_ARGMAX 7
+#define MMP_R_ARGMIN 8
+#define MMP_R_NANSUM 9
+#define MMP_R_NANMEAN 10
+#define MMP_R_NANMAX 11
+#define MMP_R_NANMIN 12
+#define MMP_R_ANY 13
+#define MMP_R_ALL 14
+
+namespace mmpd {
+
+// Device mirror of mmp_partial (include/mmp_cuda.h).
+struct PartialOut {
+  double s1, s2, shift;
+  long long count, ival, index;
+};
+
+constexpr int RBLOCK = 256;
+
+// ---------------------------------------------------------------- shuffles
+template <class A>
+__device__ __forceinline__ A shfl_down(const A &a, int delta) {
+  static_assert(sizeof(A) % 4 == 0, "accumulator must be a multiple of 4 bytes");
+  A r;
+  const unsigned *src = reinterpret_cast<const unsigned *>(&a);
+  unsigned *dst = reinterpret_cast<unsigned *>(&r);
+#pragma unroll
+  for (int i = 0; i < (int)(sizeof(A) / 4); ++i) dst[i] = __shfl_down_sync(0xffffffffu, src[i], delta);
+  return r;
+}
+
+template <class A>
+__device__ __forceinline__ A load_cg(const A *p) {
+  A r;
+  const unsigned *src = reinterpret_cast<const unsigned *>(p);
+  unsigned *dst = reinterpret_cast<unsigned *>(&r);
+#pragma unroll
+  for (int i = 0; i < (int)(sizeof(A) / 4); ++i) dst[i] = __ldcg(src + i);
+  return r;
+}
+
+// ---------------------------------------------------------------- type maps
+template <class T> struct SumAcc { typedef long long type; };
+template <> struct SumAcc<unsigned char> { typedef unsigned long long type; };
+template <> struct SumAcc<unsigned short> { typedef unsigned long long type; };
+template <> struct SumAcc<unsigned int> { typedef unsigned long long type; };
+template <> struct SumAcc<unsigned long long> { typedef unsigned long long type; };
+template <> struct SumAcc<float> { typedef double type; };
+template <> struct SumAcc<__half> { typedef double type; };
+template <> struct SumAcc<double> { typedef double type; };
+
+template <class T> struct AsF { __device__ __forceinline__ static float f(T v) { return (float)v; } };
+template <> struct AsF<__half> { __device__ __forceinline__ static float f(__half v) { return __half2float(v); } };
+template <class T> __device__ __forceinline__ double as_d(T v) { return (double)v; }
+template <> __device__ __forceinline__ double as_d<__half>(__half v) { return (double)__half2float(v); }
+template <class T> __device__ __forceinline__ typename Arith<T>::type ar(T v) { return (typename Arith<T>::type)v; }
+template <> __device__ __forceinline__ float ar<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ bool ar<bool>(bool v) { return v; }
+
+template <class A>
+__device__ __forceinline__ void store_acc_value(void *out, long long idx, int dt, A v) {
+  store_scalar(out, idx, dt, true, (long long)v, (unsigned long long)v, 0.0, !IsSigned<A>::value);
+}
+__device__ __forceinline__ void store_acc_value(void *out, long long idx, int dt, double v) {
+  store_scalar(out, idx, dt, false, 0, 0, v, false);
+}
+__device__ __forceinline__ void store_acc_value(void *out, long long idx, int dt, float v) {
+  store_scalar(out, idx, dt, false, 0, 0, (double)v, false);
+}
+
+// ---------------------------------------------------------------- ops
+// Every op provides: Acc, init(), start(first_value), one(acc, v, idx),
+// vec<V>(acc, v[], base), combine(a, b), finish(acc, n, out, idx, dt, ddof, part).
+
+template <int OPC, class T> struct RedOp;
+
+// sum / mean: float inputs add vectors in f32 and carry the total in f64;
+// integers add exactly in 64 bits (numpy's int32 sum gives int64).
+template <class T, bool MEAN>
+struct SumLike {
+  typedef typename SumAcc<T>::type Acc;
+  __device__ static Acc init() { return Acc(0); }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static void one(Acc &a, T v, long long) {
+    if (IsFloat<T>::value && sizeof(T) < 8) a += (Acc)AsF<T>::f(v);
+    else a += (Acc)ar(v);
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+    if (IsFloat<T>::value && sizeof(T) < 8) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < V; ++j) s += AsF<T>::f(v[j]);
+      a += (Acc)s;
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) a += (Acc)ar(v[j]);
+    }
+  }
+  __device__ static Acc combine(Acc a, Acc b) { return a + b; }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
+                                PartialOut *p) {
+    if (MEAN) {
+      store_acc_value(out, idx, dt, (double)a / (double)n);
+    } else {
+      store_acc_value(out, idx, dt, a);
+    }
+    if (p) {
+      p->s1 = (double)a;
+      p->count = n;
+      p->ival = (long long)a;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_SUM, T> : SumLike<T, false> {};
+template <class T> struct RedOp<MMP_R_MEAN, T> : SumLike<T, true> {};
+
+template <class T> struct ProdAcc { typedef typename SumAcc<T>::type type; };
+template <class T>
+struct RedOp<MMP_R_PROD, T> {
+  typedef typename ProdAcc<T>::type Acc;
+  __device__ static Acc init() { return Acc(1); }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static void one(Acc &a, T v, long long) { a *= (Acc)ar(v); }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) a *= (Acc)ar(v[j]);
+  }
+  __device__ static Acc combine(Acc a, Acc b) { return a * b; }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
+                                PartialOut *p) {
+    store_acc_value(out, idx, dt, a);
+    if (p) {
+      p->s1 = (double)a;
+      p->ival = (long long)a;
+      p->count = n;
+    }
+  }
+};
+
+// max / min (NaN propagates, numpy.maximum.reduce) and nanmax / nanmin
+// (NaN ignored; all-NaN gives NaN).
+template <class T, bool MAX, bool IGNORE_NAN>
+struct ExtremeOp {
+  typedef typename Arith<T>::type V_;
+  struct Acc {
+    V_ v;
+    int has;
+  };
+  __device__ static Acc init() {
+    Acc a;
+    a.v = V_(0);
+    a.has = 0;
+    return a;
+  }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static Acc pick(Acc a, Acc b) {
+    if (!a.has) return b;
+    if (!b.has) return a;
+    bool an = isnan_(a.v), bn = isnan_(b.v);
+    if (IGNORE_NAN) {
+      if (an) return b;
+      if (bn) return a;
+    } else {
+      if (an) return a;
+      if (bn) return b;
+    }
+    if (MAX) return (b.v > a.v) ? b : a;
+    return (b.v < a.v) ? b : a;
+  }
+  __device__ static void one(Acc &a, T v, long long) {
+    Acc b;
+    b.v = ar(v);
+    b.has = 1;
+    a = pick(a, b);
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) one(a, v[j], 0);
+  }
+  __device__ static Acc combine(Acc a, Acc b) { return pick(a, b); }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
+                                PartialOut *p) {
+    store_acc_value(out, idx, dt, a.v);
+    if (p) {
+      p->s1 = as_d(a.v);
+      p->ival = IsFloat<T>::value ? 0 : (long long)a.v;
+      p->count = a.has ? n : 0;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_MAX, T> : ExtremeOp<T, true, false> {};
+template <class T> struct RedOp<MMP_R_MIN, T> : ExtremeOp<T, false, false> {};
+template <class T> struct RedOp<MMP_R_NANMAX, T> : ExtremeOp<T, true, true> {};
+template <class T> struct RedOp<MMP_R_NANMIN, T> : ExtremeOp<T, false, true> {};
+
+// var / std in one pass: every element is shifted by the first element K of
+// its reduction, S1 = sum(x-K) and S2 = sum((x-K)^2) are additive across
+// threads, blocks and GPUs, and var = (S2 - S1^2/n) / (n - ddof).  The shift
+// removes the cancellation of the textbook E[x^2]-E[x]^2 formula.
+template <class T, bool STD>
+struct VarOp {
+  struct Acc {
+    double s1, s2, k;
+  };
+  __device__ static Acc init() {
+    Acc a;
+    a.s1 = 0.0;
+    a.s2 = 0.0;
+    a.k = 0.0;
+    return a;
+  }
+  __device__ static Acc start(Acc a, T first) {
+    a.k = as_d(first);
+    return a;
+  }
+  __device__ static void one(Acc &a, T v, long long) {
+    double d = as_d(v) - a.k;
+    a.s1 += d;
+    a.s2 += d * d;
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+    if (IsFloat<T>::value && sizeof(T) < 8) {
+      float kf = (float)a.k, f1 = 0.f, f2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        float d = AsF<T>::f(v[j]) - kf;
+        f1 += d;
+        f2 += d * d;
+      }
+      a.s1 += (double)f1;
+      a.s2 += (double)f2;
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) one(a, v[j], 0);
+    }
+  }
+  __device__ static Acc combine(Acc a, Acc b) {
+    a.s1 += b.s1;
+    a.s2 += b.s2;
+    return a;
+  }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double ddof,
+                                PartialOut *p) {
+    double dn = (double)n;
+    double m2 = a.s2 - a.s1 * a.s1 / dn;
+    if (m2 < 0.0) m2 = 0.0;
+    double denom = dn - ddof;
+    if (denom < 0.0) denom = 0.0;
+    double var = m2 / denom;
+    store_acc_value(out, idx, dt, STD ? sqrt(var) : var);
+    if (p) {
+      p->s1 = a.s1;
+      p->s2 = a.s2;
+      p->shift = a.k;
+      p->count = n;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_VAR, T> : VarOp<T, false> {};
+template <class T> struct RedOp<MMP_R_STD, T> : VarOp<T, true> {};
+
+// argmax / argmin: (value, index) pairs; the larger (smaller) value wins,
+// equal values keep the lower index, and NaN beats every number (numpy
+// returns the index of the first NaN).
+template <class T, bool MAX>
+struct ArgOp {
+  typedef typename Arith<T>::type V_;
+  struct Acc {
+    V_ v;
+    long long i;
+  };
+  __device__ static Acc init() {
+    Acc a;
+    a.v = V_(0);
+    a.i = -1;
+    return a;
+  }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static Acc pick(const Acc &a, const Acc &b) {
+    if (b.i < 0) return a;
+    if (a.i < 0) return b;
+    bool an = isnan_(a.v), bn = isnan_(b.v);
+    if (an || bn) {
+      if (an && bn) return (b.i < a.i) ? b : a;
+      return an ? a : b;
+    }
+    if (MAX) {
+      if (b.v > a.v) return b;
+      if (a.v > b.v) return a;
+    } else {
+      if (b.v < a.v) return b;
+      if (a.v < b.v) return a;
+    }
+    return (b.i < a.i) ? b : a;
+  }
+  __device__ static void one(Acc &a, T v, long long idx) {
+    Acc b;
+    b.v = ar(v);
+    b.i = idx;
+    a = pick(a, b);
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long base) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) one(a, v[j], base + j);
+  }
+  __device__ static Acc combine(Acc a, Acc b) { return pick(a, b); }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
+                                PartialOut *p) {
+    store_scalar(out, idx, dt, true, a.i, (unsigned long long)a.i, 0.0, false);
+    if (p) {
+      p->s1 = as_d(a.v);
+      p->ival = IsFloat<T>::value ? 0 : (long long)a.v;
+      p->index = a.i;
+      p->count = n;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_ARGMAX, T> : ArgOp<T, true> {};
+template <class T> struct RedOp<MMP_R_ARGMIN, T> : ArgOp<T, false> {};
+
+// nansum / nanmean: NaNs count as absent; the count of present values is
+// carried for nanmean (count 0 gives NaN, as numpy does).
+template <class T, bool MEAN>
+struct NanSumOp {
+  struct Acc {
+    double s;
+    long long c;
+  };
+  __device__ static Acc init() {
+    Acc a;
+    a.s = 0.0;
+    a.c = 0;
+    return a;
+  }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static void one(Acc &a, T v, long long) {
+    if (!isnan_(v)) {
+      a.s += as_d(v);
+      a.c += 1;
+    }
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+    if (IsFloat<T>::value && sizeof(T) < 8) {
+      float s = 0.f;
+      int c = 0;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        float f = AsF<T>::f(v[j]);
+        bool ok = !isnan_(f);
+        s += ok ? f : 0.f;
+        c += ok ? 1 : 0;
+      }
+      a.s += (double)s;
+      a.c += c;
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) one(a, v[j], 0);
+    }
+  }
+  __device__ static Acc combine(Acc a, Acc b) {
+    a.s += b.s;
+    a.c += b.c;
+    return a;
+  }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
+                                PartialOut *p) {
+    double r = MEAN ? (a.c > 0 ? a.s / (double)a.c : __longlong_as_double(0x7ff8000000000000ll)) : a.s;
+    store_acc_value(out, idx, dt, r);
+    if (p) {
+      p->s1 = a.s;
+      p->count = a.c;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_NANSUM, T> : NanSumOp<T, false> {};
+template <class T> struct RedOp<MMP_R_NANMEAN, T> : NanSumOp<T, true> {};
+
+template <class T, bool ANY>
+struct BoolOp {
+  typedef int Acc;
+  __device__ static Acc init() { return ANY ? 0 : 1; }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static void one(Acc &a, T v, long long) {
+    bool nz = cvt<bool>(v);
+    if (ANY) a |= nz ? 1 : 0;
+    else a &= nz ? 1 : 0;
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) one(a, v[j], 0);
+  }
+  __device__ static Acc combine(Acc a, Acc b) { return ANY ? (a | b) : (a & b); }
+  __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
+                                PartialOut *p) {
+    store_scalar(out, idx, dt, true, a, (unsigned long long)a, 0.0, false);
+    if (p) {
+      p->ival = a;
+      p->count = n;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_ANY, T> : BoolOp<T, true> {};
+template <class T> struct RedOp<MMP_R_ALL, T> : BoolOp<T, false> {};
+
+// ---------------------------------------------------------------- loaders
+// Contiguous array loader; `aligned` says whether x is aligned to a vector.
+template <class T>
+struct ContigLoader {
+  typedef T value_type;
+  const T *x;
+  int aligned;
+  __device__ __forceinline__ T operator()(long long i) const { return x[i]; }
+  template <int V>
+  __device__ __forceinline__ void vec(long long i, T (&v)[V]) const {
+    Vec<T, V> t = ldvec_stream<T, V>(x + i);
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = t.v[j];
+  }
+};
+
+// Elements per vector load: 16 bytes, at most 8 elements.
+template <class T> struct VW { static const int value = (16 / sizeof(T)) > 8 ? 8 : (16 / sizeof(T)); };
+
+// ---------------------------------------------------------------- block reduce
+template <class Op>
+__device__ __forceinline__ typename Op::Acc warp_reduce(typename Op::Acc a) {
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) a = Op::combine(a, shfl_down(a, d));
+  return a;
+}
+
+// Reduce across the block; the result is valid in thread 0.
+template <class Op, int NT>
+__device__ __forceinline__ typename Op::Acc block_reduce(typename Op::Acc a) {
+  typedef typename Op::Acc Acc;
+  __shared__ Acc sm[NT / 32];
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  a = warp_reduce<Op>(a);
+  __syncthreads();  // sm may still be read by a previous call
+  if (lane == 0) sm[w] = a;
+  __syncthreads();
+  if (w == 0) {
+    a = (lane < NT / 32) ? sm[lane] : Op::init();
+    a = warp_reduce<Op>(a);
+  }
+  return a;
+}
+
+// ---------------------------------------------------------------- full reduce
+// One launch for any n: every block reduces a grid-strided share (four
+// vectors in flight per thread), writes its partial to scratch, and the last
+// block to take a ticket merges the partials in block order (deterministic)
+// and writes the result.  The ticket is returned to zero for the next call.
+template <int OPC, class T, class L>
+__device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void *out, int out_dt,
+                                                 double ddof, void *scratch, unsigned *ticket,
+                                                 PartialOut *part) {
+  typedef RedOp<OPC, T> Op;
+  typedef typename Op::Acc Acc;
+  constexpr int V = VW<T>::value;
+  Acc acc = Op::init();
+  if (n > 0) acc = Op::start(acc, ld(0));
+  const Acc acc0 = acc;
+  long long tid = (long long)blockIdx.x * RBLOCK + threadIdx.x;
+  long long nth = (long long)gridDim.x * RBLOCK;
+  long long done = 0;
+  if (ld.aligned) {
+    long long nv = n / V;
+    long long i = tid;
+    for (; i + 3 * nth < nv; i += 4 * nth) {
+      T a0[V], a1[V], a2[V], a3[V];
+      ld.template vec<V>(i * V, a0);
+      ld.template vec<V>((i + nth) * V, a1);
+      ld.template vec<V>((i + 2 * nth) * V, a2);
+      ld.template vec<V>((i + 3 * nth) * V, a3);
+      Op::template vec<V>(acc, a0, i * V);
+      Op::template vec<V>(acc, a1, (i + nth) * V);
+      Op::template vec<V>(acc, a2, (i + 2 * nth) * V);
+      Op::template vec<V>(acc, a3, (i + 3 * nth) * V);
+    }
+    for (; i < nv; i += nth) {
+      T a0[V];
+      ld.template vec<V>(i * V, a0);
+      Op::template vec<V>(acc, a0, i * V);
+    }
+    done = nv * V;
+  }
+  for (long long j = done + tid; j < n; j += nth) Op::one(acc, ld(j), j);
+  acc = block_reduce<Op, RBLOCK>(acc);
+  if (gridDim.x == 1) {
+    if (threadIdx.x == 0) Op::finish(acc, n, out, 0, out_dt, ddof, part);
+    return;
+  }
+  __shared__ int is_last;
+  if (threadIdx.x == 0) {
+    reinterpret_cast<Acc *>(scratch)[blockIdx.x] = acc;
+    __threadfence();
+    unsigned t = atomicAdd(ticket, 1u);
+    is_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  Acc m = acc0;
+  bool first = true;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += RBLOCK) {
+    Acc pb = load_cg(reinterpret_cast<const Acc *>(scratch) + b);
+    m = first ? pb : Op::combine(m, pb);
+    first = false;
+  }
+  if (first) m = acc0;
+  m = block_reduce<Op, RBLOCK>(m);
+  if (threadIdx.x == 0) {
+    Op::finish(m, n, out, 0, out_dt, ddof, part);
+    *ticket = 0u;
+  }
+}
+
+template <int OPC, class T, class L>
+__global__ void __launch_bounds__(RBLOCK) reduce_full_kernel(L ld, long long n, void *out, int out_dt,
+                                                             double ddof, void *scratch,
+                                                             unsigned *ticket, PartialOut *part) {
+  reduce_full_body<OPC, T, L>(ld, n, out, out_dt, ddof, scratch, ticket, part);
+}
+
+// ---------------------------------------------------------------- row reduce
+// out[r] = reduce(x[r*k : r*k+k]) with one block per row (k large) ...
+template <int OPC, class T, class L>
+__device__ __forceinline__ void reduce_rows_block_body(const L &ld, long long rows, long long k, void *out,
+                                                       int out_dt, double ddof) {
+  typedef RedOp<OPC, T> Op;
+  typedef typename Op::Acc Acc;
+  constexpr int V = VW<T>::value;
+  const bool vec_ok = ld.aligned && (k % V == 0);
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    long long base = r * k;
+    Acc acc = Op::start(Op::init(), ld(base));
+    long long done = 0;
+    if (vec_ok) {
+      long long nv = k / V;
+      long long i = threadIdx.x;
+      for (; i + RBLOCK < nv; i += 2 * RBLOCK) {
+        T a0[V], a1[V];
+        ld.template vec<V>(base + i * V, a0);
+        ld.template vec<V>(base + (i + RBLOCK) * V, a1);
+        Op::template vec<V>(acc, a0, i * V);
+        Op::template vec<V>(acc, a1, (i + RBLOCK) * V);
+      }
+      for (; i < nv; i += RBLOCK) {
+        T a0[V];
+        ld.template vec<V>(base + i * V, a0);
+        Op::template vec<V>(acc, a0, i * V);
+      }
+      done = nv * V;
+    }
+    for (long long j = done + threadIdx.x; j < k; j += RBLOCK) Op::one(acc, ld(base + j), j);
+    acc = block_reduce<Op, RBLOCK>(acc);
+    if (threadIdx.x == 0) Op::finish(acc, k, out, r, out_dt, ddof, nullptr);
+  }
+}
+template <int OPC, class T, class L>
+__global__ void __launch_bounds__(RBLOCK) reduce_rows_block_kernel(L ld, long long rows, long long k,
+                                                                   void *out, int out_dt, double ddof) {
+  reduce_rows_block_body<OPC, T, L>(ld, rows, k, out, out_dt, ddof);
+}
+
+// ... or one warp per row (k small).
+template <int OPC, class T, class L>
+__device__ __forceinline__ void reduce_rows_warp_body(const L &ld, long long rows, long long k, void *out,
+                                                      int out_dt, double ddof) {
+  typedef RedOp<OPC, T> Op;
+  typedef typename Op::Acc Acc;
+  int lane = threadIdx.x & 31;
+  long long w = ((long long)blockIdx.x * RBLOCK + threadIdx.x) >> 5;
+  long long nw = ((long long)gridDim.x * RBLOCK) >> 5;
+  for (long long r = w; r < rows; r += nw) {
+    long long base = r * k;
+    Acc acc = Op::start(Op::init(), ld(base));
+    for (long long j = lane; j < k; j += 32) Op::one(acc, ld(base + j), j);
+    acc = warp_reduce<Op>(acc);
+    if (lane == 0) Op::finish(acc, k, out, r, out_dt, ddof, nullptr);
+  }
+}
+template <int OPC, class T, class L>
+__global__ void __launch_bounds__(RBLOCK) reduce_rows_warp_kernel(L ld, long long rows, long long k,
+                                                                  void *out, int out_dt, double ddof) {
+  reduce_rows_warp_body<OPC, T, L>(ld, rows, k, out, out_dt, ddof);
+}
+
+// ---------------------------------------------------------------- column reduce
+// x is (outer, k, inner); out[o*inner + c] = reduce_r x[(o*k + r)*inner + c].
+// Block = 32 x 8 threads covering 32*CV adjacent columns; the 8 thread rows
+// split the reduced axis, gridDim.y further splits it into chunks whose
+// partials are merged in chunk order by the last block of each column tile.
+template <int OPC, class T, class L, int CV>
+__device__ __forceinline__ void reduce_cols_body(const L &ld, long long outer, long long k, long long inner,
+                                                 long long kchunk, void *out, int out_dt, double ddof,
+                                                 void *scratch, unsigned *tickets) {
+  typedef RedOp<OPC, T> Op;
+  typedef typename Op::Acc Acc;
+  const long long ctiles = (inner + 32 * CV - 1) / (32 * CV);
+  const long long o = blockIdx.x / ctiles;
+  const long long ct = blockIdx.x % ctiles;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const long long c0 = ct * 32 * CV + (long long)tx * CV;
+  const long long r0 = (long long)blockIdx.y * kchunk;
+  long long r1 = r0 + kchunk;
+  if (r1 > k) r1 = k;
+  const long long obase = o * k * inner;
+  Acc acc[CV];
+#pragma unroll
+  for (int j = 0; j < CV; ++j) {
+    long long c = c0 + j;
+    acc[j] = Op::init();
+    if (c < inner) acc[j] = Op::start(acc[j], ld(obase + c));
+  }
+  Acc acc0[CV];
+#pragma unroll
+  for (int j = 0; j < CV; ++j) acc0[j] = acc[j];
+  const bool full = (c0 + CV <= inner);
+  for (long long r = r0 + ty; r < r1; r += 8) {
+    long long off = obase + r * inner + c0;
+    if (CV > 1 && full) {
+      T v[CV];
+      ld.template vec<CV>(off, v);
+#pragma unroll
+      for (int j = 0; j < CV; ++j) Op::one(acc[j], v[j], r);
+    } else {
+#pragma unroll
+      for (int j = 0; j < CV; ++j)
+        if (c0 + j < inner) Op::one(acc[j], ld(off + j), r);
+    }
+  }
+  __shared__ Acc sm[8][32 * CV];
+#pragma unroll
+  for (int j = 0; j < CV; ++j) sm[ty][tx * CV + j] = acc[j];
+  __syncthreads();
+  if (ty == 0) {
+#pragma unroll
+    for (int j = 0; j < CV; ++j) {
+      Acc a = sm[0][tx * CV + j];
+      for (int y = 1; y < 8; ++y) a = Op::combine(a, sm[y][tx * CV + j]);
+      acc[j] = a;
+    }
+  }
+  if (gridDim.y == 1) {
+    if (ty == 0) {
+#pragma unroll
+      for (int j = 0; j < CV; ++j)
+        if (c0 + j < inner) Op::finish(acc[j], k, out, o * inner + c0 + j, out_dt, ddof, nullptr);
+    }
+    return;
+  }
+  Acc *part = reinterpret_cast<Acc *>(scratch);
+  if (ty == 0) {
+#pragma unroll
+    for (int j = 0; j < CV; ++j)
+      if (c0 + j < inner) part[((long long)blockIdx.y * outer + o) * inner + c0 + j] = acc[j];
+    __threadfence();
+  }
+  __syncthreads();
+  __shared__ int is_last;
+  if (threadIdx.x == 0) {
+    unsigned t = atomicAdd(tickets + blockIdx.x, 1u);
+    is_last = (t == gridDim.y - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (ty == 0) {
+#pragma unroll
+    for (int j = 0; j < CV; ++j) {
+      long long c = c0 + j;
+      if (c >= inner) continue;
+      Acc a = acc0[j];
+      for (unsigned s = 0; s < gridDim.y; ++s) {
+        Acc ps = load_cg(part + ((long long)s * outer + o) * inner + c);
+        a = (s == 0) ? ps : Op::combine(a, ps);
+      }
+      Op::finish(a, k, out, o * inner + c, out_dt, ddof, nullptr);
+    }
+  }
+  if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
+}
+template <int OPC, class T, class L, int CV>
+__global__ void __launch_bounds__(RBLOCK) reduce_cols_kernel(L ld, long long outer, long long k,
+                                                             long long inner, long long kchunk,
+                                                             void *out, int out_dt, double ddof,
+                                                             void *scratch, unsigned *tickets) {
+  reduce_cols_body<OPC, T, L, CV>(ld, outer, k, inner, kchunk, out, out_dt, ddof, scratch, tickets);
+}
+
+}  // namespace mmpd

@@ -1,0 +1,482 @@
+// Device runtime of libmmp_cuda.so: devices, streams, stream-ordered memory,
+// copies, events, per-device scratch, NVRTC compilation and launch.
+//
+// This replaces the reference's MetalBackend singleton and its metalgpu
+// bridge (src/macmetalpy/_metal_backend.py:179-372): the buffer pool with
+// deferred reuse (_metal_backend.py:23-77) becomes the CUDA stream-ordered
+// memory pool, the per-call library switch (_metal_backend.py:321-352)
+// becomes an NVRTC module cache keyed by source and options, and the
+// `_sync` no-op kernel (_metal_backend.py:359-372) becomes a stream
+// synchronisation.  The driver API is reached through
+// cudaGetDriverEntryPoint, so the library loads on hosts without a driver.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nvrtc.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "mmp_internal.h"
+
+namespace mmp {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char *what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                  cudaGetErrorString(e) + ")";
+  return set_error(MMP_E_CUDA, m);
+}
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kTickets = 4096;
+
+struct DevState {
+  bool ready = false;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  unsigned *tickets = nullptr;
+  int *err_word = nullptr;
+  int sms = 0;
+};
+
+DevState g_dev[kMaxDevices];
+std::mutex g_mu;
+
+// ---- driver API through the runtime's entry-point query
+typedef CUresult (*PFN_LoadData)(CUmodule *, const void *);
+typedef CUresult (*PFN_GetFunction)(CUfunction *, CUmodule, const char *);
+typedef CUresult (*PFN_Launch)(CUfunction, unsigned, unsigned, unsigned,
+                               unsigned, unsigned, unsigned, unsigned,
+                               CUstream, void **, void **);
+typedef CUresult (*PFN_FuncSetAttr)(CUfunction, CUfunction_attribute, int);
+typedef CUresult (*PFN_GetErrorString)(CUresult, const char **);
+
+struct Driver {
+  PFN_LoadData load_data = nullptr;
+  PFN_GetFunction get_function = nullptr;
+  PFN_Launch launch = nullptr;
+  PFN_FuncSetAttr set_attr = nullptr;
+  PFN_GetErrorString err_string = nullptr;
+  bool ok = false;
+};
+Driver g_drv;
+
+int driver_error(CUresult r, const char *what) {
+  const char *s = "unknown";
+  if (g_drv.err_string) g_drv.err_string(r, &s);
+  return set_error(MMP_E_CUDA, std::string(what) + ": " + s);
+}
+
+struct CompiledFn {
+  CUmodule module;
+  CUfunction fn;
+  int max_dyn_smem_set;
+};
+std::unordered_map<std::string, CompiledFn> g_fn_cache;
+
+DevState *cur(int *dev_out = nullptr) {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return nullptr;
+  if (d < 0 || d >= kMaxDevices) return nullptr;
+  if (dev_out) *dev_out = d;
+  return &g_dev[d];
+}
+
+int ensure_ready() {
+  int d = 0;
+  DevState *s = cur(&d);
+  if (!s) return set_error(MMP_E_CUDA, "no CUDA device available");
+  if (s->ready) return MMP_OK;
+  return mmp_init(d);
+}
+
+}  // namespace
+
+void *driver_fn(const char *name) {
+  void *p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return p;
+}
+
+static int load_driver() {
+  if (g_drv.ok) return MMP_OK;
+  g_drv.load_data = (PFN_LoadData)driver_fn("cuModuleLoadData");
+  g_drv.get_function = (PFN_GetFunction)driver_fn("cuModuleGetFunction");
+  g_drv.launch = (PFN_Launch)driver_fn("cuLaunchKernel");
+  g_drv.set_attr = (PFN_FuncSetAttr)driver_fn("cuFuncSetAttribute");
+  g_drv.err_string = (PFN_GetErrorString)driver_fn("cuGetErrorString");
+  if (!g_drv.load_data || !g_drv.get_function || !g_drv.launch || !g_drv.set_attr)
+    return set_error(MMP_E_CUDA, "CUDA driver entry points unavailable");
+  g_drv.ok = true;
+  return MMP_OK;
+}
+
+cudaStream_t stream() {
+  DevState *s = cur();
+  if (!s) return nullptr;
+  if (!s->ready) {
+    if (ensure_ready() != MMP_OK) return nullptr;
+  }
+  return s->stream;
+}
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int sm_count() {
+  DevState *s = cur();
+  if (!s) return 148;
+  if (!s->ready) ensure_ready();
+  return s->sms > 0 ? s->sms : 148;
+}
+
+int scratch(size_t bytes, void **ptr, unsigned **tickets) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  DevState *s = cur();
+  if (bytes > s->scratch_bytes) {
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    want = (want + 4095) & ~size_t(4095);
+    if (s->scratch) MMP_CUDA_TRY(cudaFreeAsync(s->scratch, s->stream));
+    s->scratch = nullptr;
+    s->scratch_bytes = 0;
+    MMP_CUDA_TRY(cudaMallocAsync(&s->scratch, want, s->stream));
+    s->scratch_bytes = want;
+  }
+  if (ptr) *ptr = s->scratch;
+  if (tickets) *tickets = s->tickets;
+  return MMP_OK;
+}
+
+int *device_error_word() {
+  DevState *s = cur();
+  if (!s || !s->ready) {
+    if (ensure_ready() != MMP_OK) return nullptr;
+    s = cur();
+  }
+  return s->err_word;
+}
+
+}  // namespace mmp
+
+using namespace mmp;
+
+extern "C" {
+
+int mmp_abi_version(void) { return MMP_ABI_VERSION; }
+
+const char *mmp_last_error(void) { return g_last_error.c_str(); }
+
+int mmp_device_count(int *count) {
+  if (!count) return set_error(MMP_E_ARG, "count is NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *count = 0;
+    return cuda_error(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return MMP_OK;
+}
+
+int mmp_init(int device) {
+  if (device < 0 || device >= 64) return set_error(MMP_E_ARG, "device out of range");
+  std::lock_guard<std::mutex> lk(g_mu);
+  MMP_CUDA_TRY(cudaSetDevice(device));
+  DevState &s = g_dev[device];
+  if (s.ready) return MMP_OK;
+  int rc = load_driver();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+  s.own_stream = true;
+  cudaMemPool_t pool;
+  MMP_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device));
+  uint64_t thresh = UINT64_MAX;  // keep freed blocks cached in the pool
+  MMP_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thresh));
+  MMP_CUDA_TRY(cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device));
+  // tickets + error word live in one small permanent allocation
+  void *p = nullptr;
+  MMP_CUDA_TRY(cudaMalloc(&p, sizeof(unsigned) * kTickets + 256));
+  MMP_CUDA_TRY(cudaMemset(p, 0, sizeof(unsigned) * kTickets + 256));
+  s.tickets = (unsigned *)p;
+  s.err_word = (int *)((char *)p + sizeof(unsigned) * kTickets);
+  s.ready = true;
+  return MMP_OK;
+}
+
+int mmp_get_device(int *device) {
+  if (!device) return set_error(MMP_E_ARG, "device is NULL");
+  MMP_CUDA_TRY(cudaGetDevice(device));
+  return MMP_OK;
+}
+
+int mmp_sm_count(int *sms) {
+  if (!sms) return set_error(MMP_E_ARG, "sms is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  *sms = cur()->sms;
+  return MMP_OK;
+}
+
+int mmp_get_stream(void **st) {
+  if (!st) return set_error(MMP_E_ARG, "stream is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  *st = (void *)cur()->stream;
+  return MMP_OK;
+}
+
+int mmp_set_stream(void *st) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  DevState *s = cur();
+  MMP_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  if (s->own_stream) cudaStreamDestroy(s->stream);
+  s->stream = (cudaStream_t)st;
+  s->own_stream = false;
+  return MMP_OK;
+}
+
+int mmp_malloc(size_t bytes, void **ptr) {
+  if (!ptr) return set_error(MMP_E_ARG, "ptr is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  *ptr = nullptr;
+  if (bytes == 0) bytes = 256;
+  cudaError_t e = cudaMallocAsync(ptr, bytes, cur()->stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    char buf[96];
+    snprintf(buf, sizeof buf, "cudaMallocAsync(%zu bytes)", bytes);
+    return cuda_error(e, buf);
+  }
+  return MMP_OK;
+}
+
+int mmp_free(void *ptr) {
+  if (!ptr) return MMP_OK;
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaFreeAsync(ptr, cur()->stream));
+  return MMP_OK;
+}
+
+int mmp_memset(void *ptr, int value, size_t bytes) {
+  if (bytes == 0) return MMP_OK;
+  if (!ptr) return set_error(MMP_E_ARG, "ptr is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaMemsetAsync(ptr, value, bytes, cur()->stream));
+  return MMP_OK;
+}
+
+int mmp_h2d(void *dst, const void *src, size_t bytes) {
+  if (bytes == 0) return MMP_OK;
+  if (!dst || !src) return set_error(MMP_E_ARG, "null pointer in h2d");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, cur()->stream));
+  return MMP_OK;
+}
+
+int mmp_d2h(void *dst, const void *src, size_t bytes) {
+  if (bytes == 0) return MMP_OK;
+  if (!dst || !src) return set_error(MMP_E_ARG, "null pointer in d2h");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  cudaStream_t st = cur()->stream;
+  MMP_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st));
+  MMP_CUDA_TRY(cudaStreamSynchronize(st));
+  return MMP_OK;
+}
+
+int mmp_d2d(void *dst, const void *src, size_t bytes) {
+  if (bytes == 0) return MMP_OK;
+  if (!dst || !src) return set_error(MMP_E_ARG, "null pointer in d2d");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, cur()->stream));
+  return MMP_OK;
+}
+
+int mmp_host_alloc(size_t bytes, void **ptr) {
+  if (!ptr) return set_error(MMP_E_ARG, "ptr is NULL");
+  MMP_CUDA_TRY(cudaMallocHost(ptr, bytes ? bytes : 1));
+  return MMP_OK;
+}
+
+int mmp_host_free(void *ptr) {
+  if (ptr) MMP_CUDA_TRY(cudaFreeHost(ptr));
+  return MMP_OK;
+}
+
+int mmp_scratch(size_t bytes, void **ptr, void **tickets) {
+  unsigned *t = nullptr;
+  int rc = mmp::scratch(bytes, ptr, &t);
+  if (tickets) *tickets = t;
+  return rc;
+}
+
+int mmp_synchronize(void) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaStreamSynchronize(cur()->stream));
+  return MMP_OK;
+}
+
+int mmp_check_device_error(int *code) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  DevState *s = cur();
+  int v = 0;
+  MMP_CUDA_TRY(cudaStreamSynchronize(s->stream));
+  MMP_CUDA_TRY(cudaMemcpy(&v, s->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) MMP_CUDA_TRY(cudaMemset(s->err_word, 0, sizeof(int)));
+  if (code) *code = v;
+  return MMP_OK;
+}
+
+int mmp_event_create(void **event) {
+  if (!event) return set_error(MMP_E_ARG, "event is NULL");
+  cudaEvent_t e;
+  MMP_CUDA_TRY(cudaEventCreate(&e));
+  *event = (void *)e;
+  return MMP_OK;
+}
+
+int mmp_event_destroy(void *event) {
+  if (event) MMP_CUDA_TRY(cudaEventDestroy((cudaEvent_t)event));
+  return MMP_OK;
+}
+
+int mmp_event_record(void *event) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaEventRecord((cudaEvent_t)event, cur()->stream));
+  return MMP_OK;
+}
+
+int mmp_event_elapsed_ms(void *start, void *end, float *ms) {
+  MMP_CUDA_TRY(cudaEventSynchronize((cudaEvent_t)end));
+  MMP_CUDA_TRY(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));
+  return MMP_OK;
+}
+
+int mmp_compile(const char *source, const char *name, const char *options,
+                void **func, char *log, size_t log_size) {
+  if (!source || !name || !func) return set_error(MMP_E_ARG, "null argument to mmp_compile");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  int dev = current_device();
+  std::string key = std::to_string(dev) + '\x1f' + name + '\x1f' +
+                    (options ? options : "") + '\x1f' + source;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_fn_cache.find(key);
+    if (it != g_fn_cache.end()) {
+      *func = (void *)it->second.fn;
+      return MMP_OK;
+    }
+  }
+  std::vector<std::string> opts;
+  if (options) {
+    std::string all(options), cur_opt;
+    for (char c : all) {
+      if (c == '\n') {
+        if (!cur_opt.empty()) opts.push_back(cur_opt);
+        cur_opt.clear();
+      } else {
+        cur_opt.push_back(c);
+      }
+    }
+    if (!cur_opt.empty()) opts.push_back(cur_opt);
+  }
+  std::vector<const char *> copts;
+  for (auto &o : opts) copts.push_back(o.c_str());
+
+  nvrtcProgram prog;
+  nvrtcResult nr = nvrtcCreateProgram(&prog, source, "mmp_rtc.cu", 0, nullptr, nullptr);
+  if (nr != NVRTC_SUCCESS) return set_error(MMP_E_NVRTC, nvrtcGetErrorString(nr));
+  std::string expr = std::string("&") + name;
+  nvrtcAddNameExpression(prog, expr.c_str());
+  nr = nvrtcCompileProgram(prog, (int)copts.size(), copts.data());
+  size_t lsz = 0;
+  nvrtcGetProgramLogSize(prog, &lsz);
+  std::string plog(lsz, '\0');
+  if (lsz) nvrtcGetProgramLog(prog, &plog[0]);
+  if (log && log_size) {
+    size_t n = plog.size() < log_size - 1 ? plog.size() : log_size - 1;
+    memcpy(log, plog.data(), n);
+    log[n] = 0;
+  }
+  if (nr != NVRTC_SUCCESS) {
+    nvrtcDestroyProgram(&prog);
+    return set_error(MMP_E_NVRTC, std::string("NVRTC: ") + nvrtcGetErrorString(nr) + "\n" + plog);
+  }
+  const char *lowered = nullptr;
+  std::string lowered_name = name;
+  if (nvrtcGetLoweredName(prog, expr.c_str(), &lowered) == NVRTC_SUCCESS && lowered)
+    lowered_name = lowered;
+  size_t csz = 0;
+  nr = nvrtcGetCUBINSize(prog, &csz);
+  if (nr != NVRTC_SUCCESS || csz == 0) {
+    nvrtcDestroyProgram(&prog);
+    return set_error(MMP_E_NVRTC, "NVRTC produced no cubin (pass a real sm_100a architecture)");
+  }
+  std::vector<char> cubin(csz);
+  nvrtcGetCUBIN(prog, cubin.data());
+  nvrtcDestroyProgram(&prog);
+
+  CUmodule mod;
+  CUresult r = g_drv.load_data(&mod, cubin.data());
+  if (r != CUDA_SUCCESS) return driver_error(r, "cuModuleLoadData");
+  CUfunction fn;
+  r = g_drv.get_function(&fn, mod, lowered_name.c_str());
+  if (r != CUDA_SUCCESS) return driver_error(r, "cuModuleGetFunction");
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_fn_cache[key] = CompiledFn{mod, fn, 0};
+  }
+  *func = (void *)fn;
+  return MMP_OK;
+}
+
+int mmp_launch(void *func, const unsigned grid[3], const unsigned block[3],
+               unsigned shared_bytes, void **args) {
+  if (!func || !grid || !block) return set_error(MMP_E_ARG, "null argument to mmp_launch");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  if (grid[0] == 0 || grid[1] == 0 || grid[2] == 0) return MMP_OK;  // empty launch
+  if (shared_bytes > 48 * 1024) {
+    CUresult r = g_drv.set_attr((CUfunction)func, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                (int)shared_bytes);
+    if (r != CUDA_SUCCESS) return driver_error(r, "cuFuncSetAttribute");
+  }
+  CUresult r = g_drv.launch((CUfunction)func, grid[0], grid[1], grid[2], block[0], block[1],
+                            block[2], shared_bytes, (CUstream)cur()->stream, args, nullptr);
+  if (r != CUDA_SUCCESS) return driver_error(r, "cuLaunchKernel");
+  return MMP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+// mmp_scan: inclusive cumsum / cumprod along the middle axis of
+// (outer, k, inner).  See mmp_scan.cuh for the algorithm.
+#include <cuda_runtime.h>
+
+#include "mmp_dispatch.h"
+#include "mmp_scan.cuh"
+
+using namespace mmpd;
+
+namespace mmp {
+namespace {
+
+// Look-back state of the current device: tile aggregates, inclusive
+// prefixes, flags and the tile counter.  Zeroed when (re)allocated; flags
+// carry a launch epoch so they never need clearing between launches.
+struct ScanState {
+  void *buf = nullptr;
+  size_t tiles = 0;
+  unsigned epoch = 0;
+};
+ScanState g_scan[64];
+
+int scan_state(long long tiles, void **agg, void **incl, unsigned **flags, unsigned **counter,
+               unsigned *epoch) {
+  int dev = current_device();
+  ScanState &s = g_scan[dev];
+  cudaStream_t st = stream();
+  if ((size_t)tiles > s.tiles) {
+    size_t want = (size_t)tiles < 4096 ? 4096 : (size_t)tiles;
+    if (s.buf) MMP_CUDA_TRY(cudaFreeAsync(s.buf, st));
+    s.buf = nullptr;
+    s.tiles = 0;
+    size_t bytes = want * (8 + 8 + 4) + 256;
+    MMP_CUDA_TRY(cudaMallocAsync(&s.buf, bytes, st));
+    MMP_CUDA_TRY(cudaMemsetAsync(s.buf, 0, bytes, st));
+    s.tiles = want;
+    s.epoch = 0;
+  }
+  s.epoch = (s.epoch + 1) & 0x3fffffffu;
+  if (s.epoch == 0) {  // wrapped: clear stale flags once
+    MMP_CUDA_TRY(cudaMemsetAsync(s.buf, 0, s.tiles * 20 + 256, st));
+    s.epoch = 1;
+  }
+  char *b = (char *)s.buf;
+  *agg = b;
+  *incl = b + s.tiles * 8;
+  *flags = (unsigned *)(b + s.tiles * 16);
+  *counter = (unsigned *)(b + s.tiles * 20);
+  *epoch = s.epoch;
+  return MMP_OK;
+}
+
+template <class T> struct ScanOut { typedef long long type; static constexpr int code = MMP_INT64; };
+template <> struct ScanOut<unsigned short> { typedef unsigned long long type; static constexpr int code = MMP_UINT64; };
+template <> struct ScanOut<unsigned int> { typedef unsigned long long type; static constexpr int code = MMP_UINT64; };
+template <> struct ScanOut<unsigned long long> { typedef unsigned long long type; static constexpr int code = MMP_UINT64; };
+template <> struct ScanOut<__half> { typedef __half type; static constexpr int code = MMP_FLOAT16; };
+template <> struct ScanOut<float> { typedef float type; static constexpr int code = MMP_FLOAT32; };
+template <> struct ScanOut<double> { typedef double type; static constexpr int code = MMP_FLOAT64; };
+
+}  // namespace
+
+template <int PRODI, class T>
+struct ScanRun {
+  static int run(const void *xv, int out_dt, void *yv, long long outer, long long k, long long inner,
+                 const void *carry) {
+    typedef typename ScanOut<T>::type O;
+    constexpr bool PROD = PRODI != 0;
+    if (out_dt != ScanOut<T>::code)
+      return set_error(MMP_E_ARG, "scan output dtype must be the numpy accumulation type");
+    cudaStream_t st = stream();
+    if (!st) return set_error(MMP_E_CUDA, "no stream");
+    const T *x = (const T *)xv;
+    O *y = (O *)yv;
+    typedef typename ScanTypes<T>::carry_t CT;
+    const CT *cin = (const CT *)carry;
+    const int sms = sm_count();
+    if (inner > 1) {
+      long long total = outer * inner;
+      long long blocks = (total + SBLOCK - 1) / SBLOCK;
+      long long maxb = (long long)sms * 8;
+      scan_cols_kernel<T, O, PROD><<<(unsigned)(blocks < maxb ? blocks : maxb), SBLOCK, 0, st>>>(x, y, outer,
+                                                                                              k, inner);
+      MMP_LAUNCH_CHECK("scan_cols_kernel");
+      return MMP_OK;
+    }
+    const long long rows = outer;
+    if (k < STILE / 4) {
+      long long blocks = (rows + 7) / 8;
+      long long maxb = (long long)sms * 8;
+      scan_rows_warp_kernel<T, O, PROD><<<(unsigned)(blocks < maxb ? blocks : maxb), SBLOCK, 0, st>>>(
+          x, y, rows, k, cin);
+      MMP_LAUNCH_CHECK("scan_rows_warp_kernel");
+      return MMP_OK;
+    }
+    long long tpr = (k + STILE - 1) / STILE;
+    long long total = rows * tpr;
+    if (total > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
+    void *agg, *incl;
+    unsigned *flags, *counter, epoch;
+    int rc = scan_state(total, &agg, &incl, &flags, &counter, &epoch);
+    if (rc) return rc;
+    typedef typename ScanTypes<T>::carry_t C;
+    TileState<C> ts;
+    ts.agg = (C *)agg;
+    ts.incl = (C *)incl;
+    ts.flag = flags;
+    int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
+    scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, 0, st>>>(
+        x, y, rows, k, tpr, total, ts, counter, epoch, device_error_word(), cin, vec_ok);
+    MMP_LAUNCH_CHECK("scan_tiles_kernel");
+    return MMP_OK;
+  }
+};
+
+}  // namespace mmp
+
+extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y, int64_t outer, int64_t k,
+                        int64_t inner, const void *carry_in) {
+  if (outer < 0 || k < 0 || inner < 0) return mmp::set_error(MMP_E_ARG, "negative extent");
+  if (outer == 0 || k == 0 || inner == 0) return MMP_OK;
+  if (!x || !y) return mmp::set_error(MMP_E_ARG, "null pointer");
+  if (op == MMP_S_SUM) return mmp::dispatch_dtype<mmp::ScanRun, 0>(dtype, x, out_dtype, y, (long long)outer,
+                                                                  (long long)k, (long long)inner, carry_in);
+  if (op == MMP_S_PROD) return mmp::dispatch_dtype<mmp::ScanRun, 1>(dtype, x, out_dtype, y, (long long)outer,
+                                                                   (long long)k, (long long)inner, carry_in);
+  return mmp::set_error(MMP_E_ARG, "unsupported scan op");
+}

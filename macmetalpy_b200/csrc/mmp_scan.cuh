@@ -1,0 +1,294 @@
+// Inclusive scans (cumsum / cumprod) for sm_100a.
+//
+// Reference: parallel_scan_shader (src/macmetalpy/_kernels.py:1263-1358) runs
+// three launches -- a serial scan of 1024 elements per thread, a scan of the
+// block totals on ONE thread, and a propagate pass -- and keeps the input
+// dtype (int32 stays int32); the axis variant (prefix_sum, _kernels.py:1148)
+// scans one row per thread after a transpose copy (ndarray.py:2068-2152).
+// Results here follow numpy (the reference's CPU path): integer cumsum
+// accumulates and returns 64-bit integers, float cumsum returns the input
+// float type.
+//
+// Rows of a (rows, k) view are cut into tiles of TILE elements.  Each block
+// takes the next tile id from a global counter (so every lower tile is
+// already running), scans its tile in registers and shared memory, publishes
+// the tile aggregate, looks back over its predecessors within the same row
+// (decoupled look-back) until it meets a published inclusive prefix, then
+// publishes its own inclusive prefix and writes its outputs: one read and
+// one write of the data, one launch.  Every wait is bounded; a wait that
+// runs out sets the device error word and the block carries on, so a fault
+// shows up as an error from mmp_check_device_error, never as a hang.
+//
+// Float inputs are scanned inside a tile in f32 and carried between tiles in
+// f64, so the error stays near the f32 rounding of each output instead of
+// growing with the prefix length.
+#pragma once
+#include "mmp_device.cuh"
+
+namespace mmpd {
+
+constexpr int SBLOCK = 256;
+constexpr int SITEMS = 16;
+constexpr int STILE = SBLOCK * SITEMS;
+
+template <class T> struct ScanTypes {  // signed integers and bool
+  typedef long long local_t;
+  typedef long long carry_t;
+};
+template <> struct ScanTypes<unsigned short> { typedef unsigned long long local_t; typedef unsigned long long carry_t; };
+template <> struct ScanTypes<unsigned int> { typedef unsigned long long local_t; typedef unsigned long long carry_t; };
+template <> struct ScanTypes<unsigned long long> { typedef unsigned long long local_t; typedef unsigned long long carry_t; };
+template <> struct ScanTypes<float> { typedef float local_t; typedef double carry_t; };
+template <> struct ScanTypes<__half> { typedef float local_t; typedef double carry_t; };
+template <> struct ScanTypes<double> { typedef double local_t; typedef double carry_t; };
+
+template <bool PROD> struct ScanOp {
+  template <class A> __device__ __forceinline__ static A id() { return PROD ? A(1) : A(0); }
+  template <class A> __device__ __forceinline__ static A op(A a, A b) { return PROD ? a * b : a + b; }
+};
+
+template <class L, class T>
+__device__ __forceinline__ L to_local(T v) { return (L)v; }
+template <>
+__device__ __forceinline__ float to_local<float, __half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ long long to_local<long long, bool>(bool v) { return v ? 1 : 0; }
+
+// Per-launch tile state; flag = (epoch << 2) | state, state 1 = aggregate,
+// 2 = inclusive prefix.  A flag from an older launch reads as "not ready",
+// so the state never needs clearing between launches.
+template <class C>
+struct TileState {
+  C *agg;
+  C *incl;
+  unsigned *flag;
+};
+
+__device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
+  return *reinterpret_cast<const volatile unsigned *>(p);
+}
+template <class C>
+__device__ __forceinline__ C ld_volatile_c(const C *p) {
+  return *reinterpret_cast<const volatile C *>(p);
+}
+
+// Wait for the state of tile `t` in this launch; bounded.
+__device__ __forceinline__ unsigned wait_flag(const unsigned *flag, long long t, unsigned epoch,
+                                              int *err) {
+  unsigned f = 0;
+  unsigned ns = 8;
+  for (long long it = 0; it < (1ll << 22); ++it) {
+    f = ld_volatile(flag + t);
+    if ((f >> 2) == (epoch & 0x3fffffffu) && (f & 3u)) return f & 3u;
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+  }
+  atomicExch(err, 2);  // look-back wait ran out
+  return 0;
+}
+
+template <class T, class O, bool PROD>
+__global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
+    const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tiles_per_row,
+    long long total_tiles, TileState<typename ScanTypes<T>::carry_t> st, unsigned *tile_counter,
+    unsigned epoch, int *err, const typename ScanTypes<T>::carry_t *carry_in, int vec_ok) {
+  typedef typename ScanTypes<T>::local_t A;
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> Op;
+  __shared__ long long s_tile;
+  __shared__ A s_warp[SBLOCK / 32];
+  __shared__ C s_excl;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) s_tile = (long long)atomicAdd(tile_counter, 1u);
+  __syncthreads();
+  const long long tile = s_tile;
+  if (tid == 0 && tile == total_tiles - 1) *tile_counter = 0u;  // every id is handed out
+  if (tile >= total_tiles) return;
+  const long long row = tile / tiles_per_row;
+  const long long j = tile - row * tiles_per_row;
+  const long long start = row * k + j * STILE;
+  long long count = k - j * STILE;
+  if (count > STILE) count = STILE;
+  const unsigned ep = epoch & 0x3fffffffu;
+
+  // ---- load SITEMS consecutive elements per thread and scan them
+  A v[SITEMS];
+  const long long my0 = (long long)tid * SITEMS;
+  if (vec_ok && count == STILE) {
+    constexpr int VE = (16 / sizeof(T)) < SITEMS ? (16 / sizeof(T)) : SITEMS;
+#pragma unroll
+    for (int q = 0; q < SITEMS / VE; ++q) {
+      Vec<T, VE> t = ldvec_stream<T, VE>(x + start + my0 + q * VE);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) v[q * VE + e] = to_local<A, T>(t.v[e]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) {
+      long long i = my0 + e;
+      v[e] = (i < count) ? to_local<A, T>(x[start + i]) : Op::template id<A>();
+    }
+  }
+#pragma unroll
+  for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
+  // ---- exclusive scan of the thread totals across the block
+  A tot = v[SITEMS - 1];
+  A inc = tot;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    A o = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc = Op::op(o, inc);
+  }
+  if (lane == 31) s_warp[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    A wv = (lane < SBLOCK / 32) ? s_warp[lane] : Op::template id<A>();
+#pragma unroll
+    for (int d = 1; d < SBLOCK / 32; d <<= 1) {
+      A o = __shfl_up_sync(0xffffffffu, wv, d);
+      if (lane >= d) wv = Op::op(o, wv);
+    }
+    if (lane < SBLOCK / 32) s_warp[lane] = wv;  // inclusive warp prefixes
+  }
+  __syncthreads();
+  A warp_excl = (w > 0) ? s_warp[w - 1] : Op::template id<A>();
+  // inc is the inclusive prefix of thread totals within the warp; the
+  // exclusive prefix is the neighbour's inclusive one.
+  A thread_excl;
+  {
+    A o = __shfl_up_sync(0xffffffffu, inc, 1);
+    A wexcl_in_warp = (lane == 0) ? Op::template id<A>() : o;
+    thread_excl = Op::op(warp_excl, wexcl_in_warp);
+  }
+  const A tile_agg = s_warp[SBLOCK / 32 - 1];
+
+  // ---- decoupled look-back over earlier tiles of the same row
+  if (w == 0) {
+    C excl = Op::template id<C>();
+    if (j == 0) {
+      if (carry_in && rows == 1) excl = (C)(*carry_in);
+      if (lane == 0) {
+        st.incl[tile] = Op::op(excl, (C)tile_agg);
+        __threadfence();
+        atomicExch(st.flag + tile, (ep << 2) | 2u);
+      }
+    } else {
+      if (lane == 0) {
+        st.agg[tile] = (C)tile_agg;
+        __threadfence();
+        atomicExch(st.flag + tile, (ep << 2) | 1u);
+      }
+      const long long row_first = row * tiles_per_row;
+      long long look = tile - 1;  // highest tile id still to fold in
+      bool done = false;
+      while (!done) {
+        long long t = look - lane;
+        unsigned f;
+        C val = Op::template id<C>();
+        if (t >= row_first) {
+          f = wait_flag(st.flag, t, ep, err);
+          __threadfence();
+          if (f == 2) val = ld_volatile_c(st.incl + t);
+          else if (f == 1) val = ld_volatile_c(st.agg + t);
+        } else {
+          f = 2;  // before the row start: acts as an inclusive prefix of identity
+          if (carry_in && rows == 1 && t == row_first - 1) val = (C)(*carry_in);
+        }
+        unsigned incl_mask = __ballot_sync(0xffffffffu, f == 2);
+        int stop = incl_mask ? (__ffs(incl_mask) - 1) : 31;
+        // fold lanes 0..stop (closest tile first) -- order: tile-1, tile-2, ...
+        C part = (lane <= stop) ? val : Op::template id<C>();
+        // combine with the lane order reversed so the fold is deterministic
+#pragma unroll
+        for (int d = 16; d >= 1; d >>= 1) part = Op::op(part, __shfl_down_sync(0xffffffffu, part, d));
+        excl = Op::op(excl, part);
+        if (incl_mask) done = true;
+        else look -= 32;
+      }
+      if (lane == 0) {
+        st.incl[tile] = Op::op(excl, (C)tile_agg);
+        __threadfence();
+        atomicExch(st.flag + tile, (ep << 2) | 2u);
+      }
+    }
+    if (lane == 0) s_excl = excl;
+  }
+  __syncthreads();
+  const C excl = s_excl;
+
+  // ---- outputs: carry (C) + tile-local prefix (A)
+  O res[SITEMS];
+#pragma unroll
+  for (int e = 0; e < SITEMS; ++e) {
+    A loc = Op::op(thread_excl, v[e]);
+    res[e] = cvt<O>(Op::op(excl, (C)loc));
+  }
+  if (vec_ok && count == STILE) {
+    constexpr int VO = (16 / sizeof(O)) < SITEMS ? (16 / sizeof(O)) : SITEMS;
+#pragma unroll
+    for (int q = 0; q < SITEMS / VO; ++q) {
+      Vec<O, VO> t;
+#pragma unroll
+      for (int e = 0; e < VO; ++e) t.v[e] = res[q * VO + e];
+      stvec_stream<O, VO>(y + start + my0 + q * VO, t);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) {
+      long long i = my0 + e;
+      if (i < count) y[start + i] = res[e];
+    }
+  }
+}
+
+// One warp per row for short rows (k < STILE / 4).
+template <class T, class O, bool PROD>
+__global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,
+                                                                O *__restrict__ y, long long rows,
+                                                                long long k, const typename ScanTypes<T>::carry_t *carry_in) {
+  typedef typename ScanTypes<T>::local_t A;
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> Op;
+  const int lane = threadIdx.x & 31;
+  long long wid = ((long long)blockIdx.x * SBLOCK + threadIdx.x) >> 5;
+  long long nw = ((long long)gridDim.x * SBLOCK) >> 5;
+  for (long long r = wid; r < rows; r += nw) {
+    C carry = Op::template id<C>();
+    if (carry_in && rows == 1) carry = (C)(*carry_in);
+    for (long long c0 = 0; c0 < k; c0 += 32) {
+      long long i = c0 + lane;
+      A v = (i < k) ? to_local<A, T>(x[r * k + i]) : Op::template id<A>();
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        A o = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v = Op::op(o, v);
+      }
+      if (i < k) y[r * k + i] = cvt<O>(Op::op(carry, (C)v));
+      A last = __shfl_sync(0xffffffffu, v, 31);
+      carry = Op::op(carry, (C)last);
+    }
+  }
+}
+
+// Scan along a strided axis of an (outer, k, inner) view, inner > 1: one
+// thread per column walks down the k rows (coalesced across columns).
+template <class T, class O, bool PROD>
+__global__ void __launch_bounds__(SBLOCK) scan_cols_kernel(const T *__restrict__ x,
+                                                           O *__restrict__ y, long long outer,
+                                                           long long k, long long inner) {
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> Op;
+  long long g = (long long)blockIdx.x * SBLOCK + threadIdx.x;
+  long long total = outer * inner;
+  for (; g < total; g += (long long)gridDim.x * SBLOCK) {
+    long long o = g / inner, c = g - o * inner;
+    long long base = o * k * inner + c;
+    C carry = Op::template id<C>();
+    for (long long r = 0; r < k; ++r) {
+      carry = Op::op(carry, (C)to_local<typename ScanTypes<T>::local_t, T>(x[base + r * inner]));
+      y[base + r * inner] = cvt<O>(carry);
+    }
+  }
+}
+
+}  // namespace mmpd

@@ -1,0 +1,150 @@
+"""Generate the golden vectors in ``golden_v1.npz`` from the REFERENCE itself.
+
+Run in a container that has the reference checked out (read-only) at
+``$MMP_REFERENCE`` (default ``/root/reference``); the GPU box never runs this.
+The reference refuses to import off macOS (``src/macmetalpy/__init__.py:5-6``)
+and its Metal path cannot run on Linux, so the script sets
+``sys.platform = "darwin"`` only while importing, then raises every CPU/GPU
+size threshold (``ndarray.py:41-44`` and the per-op tables ``:113-132``,
+``reductions.py:378``) so that each op takes the reference's own CPU branch
+-- the path the B200 build must match.  Paths whose only large-size branch is
+Metal are not exercised here (sizes stay below ``nan_ops``/``matmul``'s
+literal 4,194,304 thresholds), except ``__matmul__``, which has no CPU
+branch: for it the script records ``np.matmul``, the function the
+reference's ``cp.matmul`` CPU branch calls (``linalg_top.py:99-102``).
+
+Every input is seeded (numpy ``default_rng``) and shaped like the BASELINE
+configs at reduced size.  Usage: ``python tests/golden/make_golden.py``.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import warnings
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("MMP_REFERENCE", "/root/reference")
+
+
+def import_reference():
+    sys.path.insert(0, os.path.join(REF, "src"))
+    saved = sys.platform
+    sys.platform = "darwin"
+    try:
+        import macmetalpy as mp
+    finally:
+        sys.platform = saved
+    nd = sys.modules["macmetalpy.ndarray"]
+    big = 1 << 62
+    for name in ("_GPU_THRESHOLD", "_GPU_THRESHOLD_LIGHT", "_GPU_THRESHOLD_MEMORY", "_GPU_REDUCTION_THRESHOLD"):
+        setattr(nd, name, big)
+    for table in (nd._UNARY_THRESHOLD, nd._BINARY_THRESHOLD):
+        for k in table:
+            table[k] = big
+    sys.modules["macmetalpy.reductions"]._GPU_THRESHOLD_MEMORY = big
+    return mp
+
+
+def main():
+    mp = import_reference()
+    warnings.simplefilter("ignore")
+    g = {}
+    # C1: fused elementwise + reduction, reduced from 2^20 to 4096 elements
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal(4096).astype(np.float32)
+    X = mp.array(x)
+    y = mp.sqrt(mp.abs(X)) + mp.exp(-X ** 2)
+    g["c1_x"] = x
+    g["c1_y"] = y.get()
+    g["c1_sum"] = np.asarray(mp.sum(y).get())
+    g["c1_mean"] = np.asarray(mp.mean(y).get())
+
+    # C2: binary ufuncs (float32, int32) and a broadcast add
+    rng = np.random.default_rng(1)
+    n = 4096
+    a = rng.uniform(-1000, 1000, n).astype(np.float32)
+    b = (rng.uniform(1, 50, n) * rng.choice([-1, 1], n)).astype(np.float32)
+    ai = rng.integers(-1000, 1000, n).astype(np.int32)
+    bi = (rng.integers(1, 50, n) * rng.choice([-1, 1], n)).astype(np.int32)
+    A, B, AI, BI = mp.array(a), mp.array(b), mp.array(ai), mp.array(bi)
+    g["c2_a"], g["c2_b"], g["c2_ai"], g["c2_bi"] = a, b, ai, bi
+    g["c2_add_f32"] = mp.add(A, B).get()
+    g["c2_floordiv_f32"] = mp.floor_divide(A, B).get()
+    g["c2_mod_f32"] = (A % B).get()
+    g["c2_logaddexp_f32"] = mp.logaddexp(A, B).get()
+    g["c2_add_i32"] = mp.add(AI, BI).get()
+    g["c2_floordiv_i32"] = mp.floor_divide(AI, BI).get()
+    g["c2_mod_i32"] = (AI % BI).get()
+    r = rng.standard_normal((64, 1)).astype(np.float32)
+    c = rng.standard_normal((1, 128)).astype(np.float32)
+    g["c2_bc_r"], g["c2_bc_c"] = r, c
+    g["c2_bc_add"] = (mp.array(r) + mp.array(c)).get()
+    # edge operands: signed zeros, exact multiples, infinities, NaN
+    ea = np.array([0.0, -0.0, 7.0, -7.0, 7.5, -7.5, np.inf, -np.inf, np.nan, 1e30, -1e-30, 5.0],
+                  np.float32)
+    eb = np.array([3.0, 3.0, -3.5, 3.5, 2.5, 2.5, 2.0, 2.0, 1.0, 3.0, 7.0, np.inf], np.float32)
+    g["c2_edge_a"], g["c2_edge_b"] = ea, eb
+    g["c2_edge_floordiv"] = mp.floor_divide(mp.array(ea), mp.array(eb)).get()
+    g["c2_edge_mod"] = (mp.array(ea) % mp.array(eb)).get()
+    g["c2_edge_logaddexp"] = mp.logaddexp(mp.array(ea), mp.array(eb)).get()
+    ia = np.array([7, -7, 7, -7, 0, -2147483648, 2147483647, 5], np.int32)
+    ib = np.array([2, 2, -2, -2, 5, -1, 1, 0], np.int32)
+    g["c2_iedge_a"], g["c2_iedge_b"] = ia, ib
+    g["c2_iedge_floordiv"] = mp.floor_divide(mp.array(ia), mp.array(ib)).get()
+    g["c2_iedge_mod"] = (mp.array(ia) % mp.array(ib)).get()
+
+    # C3: reductions on a (64, 96) matrix
+    rng = np.random.default_rng(2)
+    M = rng.standard_normal((64, 96)).astype(np.float32)
+    MI = rng.integers(-100, 101, (64, 96)).astype(np.int32)
+    MN = M.copy()
+    nan_idx = rng.choice(M.size, M.size // 100, replace=False)
+    MN.reshape(-1)[nan_idx] = np.nan
+    g["c3_m"], g["c3_mi"], g["c3_mn"] = M, MI, MN
+    Md, MId, MNd = mp.array(M), mp.array(MI), mp.array(MN)
+    for nm, fn in (("sum", mp.sum), ("mean", mp.mean), ("var", mp.var)):
+        g[f"c3_{nm}"] = np.asarray(fn(Md).get())
+        for ax in (0, 1):
+            g[f"c3_{nm}_ax{ax}"] = fn(Md, axis=ax).get()
+    g["c3_argmax"] = np.asarray(mp.argmax(Md))
+    g["c3_argmax_ax0"] = mp.argmax(Md, axis=0).get()
+    g["c3_argmax_ax1"] = mp.argmax(Md, axis=1).get()
+    g["c3_isum"] = np.asarray(mp.sum(MId).get())
+    g["c3_nansum"] = np.asarray(mp.nansum(MNd).get())
+    g["c3_nanmean"] = np.asarray(mp.nanmean(MNd).get())
+    tie = np.array([3, 7, 7, 1, 7], np.float32)
+    g["c3_tie"], g["c3_tie_argmax"] = tie, np.asarray(mp.argmax(mp.array(tie)))
+
+    # C4: scans
+    rng = np.random.default_rng(3)
+    si = rng.integers(-100, 101, 8192).astype(np.int32)
+    sf = rng.uniform(0, 1, 8192).astype(np.float32)
+    s2 = rng.standard_normal((16, 512)).astype(np.float32)
+    g["c4_si"], g["c4_sf"], g["c4_s2"] = si, sf, s2
+    g["c4_cumsum_i32"] = mp.cumsum(mp.array(si)).get()
+    g["c4_cumsum_f32"] = mp.cumsum(mp.array(sf)).get()
+    g["c4_cumsum_ax1"] = mp.cumsum(mp.array(s2), axis=1).get()
+
+    # C5: matmul
+    rng = np.random.default_rng(4)
+    ma = (rng.standard_normal((64, 96)) / np.sqrt(96)).astype(np.float32)
+    mb = (rng.standard_normal((96, 80)) / np.sqrt(96)).astype(np.float32)
+    ba = (rng.standard_normal((4, 32, 48)) / np.sqrt(48)).astype(np.float32)
+    bb = (rng.standard_normal((4, 48, 40)) / np.sqrt(48)).astype(np.float32)
+    ha = (rng.standard_normal((64, 64)) / 8).astype(np.float16)
+    hb = (rng.standard_normal((64, 64)) / 8).astype(np.float16)
+    g["c5_a"], g["c5_b"], g["c5_ba"], g["c5_bb"], g["c5_ha"], g["c5_hb"] = ma, mb, ba, bb, ha, hb
+    g["c5_mm"] = mp.matmul(mp.array(ma), mp.array(mb)).get()
+    g["c5_bmm"] = mp.matmul(mp.array(ba), mp.array(bb)).get()
+    g["c5_hmm"] = mp.matmul(mp.array(ha), mp.array(hb)).get()
+
+    out = os.path.join(HERE, "golden_v1.npz")
+    np.savez_compressed(out, **g)
+    print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,80 @@
+"""cumsum / cumprod vs the oracle: int32 -> int64 bit-exact across tile
+boundaries (4096-element tiles), float32 within 1e-4 of the float64 scan,
+row (axis=-1) and column (axis=0) scans, carry-in."""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [1, 2, 31, 1023, 1024, 1025, 4095, 4096, 4097, 3 * 4096 + 5, 40000, (1 << 20) + 7, 1 << 22]
+
+
+@pytest.fixture(scope="module")
+def cp():
+    import macmetalpy_b200 as cp
+    return cp
+
+
+def scan_err(got, ref, x):
+    scale = np.cumsum(np.abs(np.asarray(x, np.float64)), axis=-1) * 1e-7 + 1e-30
+    return float(np.max(np.abs(np.asarray(got, np.float64) - ref) / np.maximum(np.abs(ref), scale)))
+
+
+@pytest.mark.parametrize("n", SIZES)
+def test_int32_cumsum_exact(cp, n):
+    x = np.random.default_rng(n).integers(-100, 101, n).astype(np.int32)
+    got = cp.cumsum(cp.array(x))
+    want = O.cumsum(x)
+    assert got.dtype == np.int64
+    np.testing.assert_array_equal(got.get(), want)
+
+
+@pytest.mark.parametrize("n", SIZES)
+def test_f32_cumsum(cp, n):
+    x = np.random.default_rng(n + 1).uniform(0, 1, n).astype(np.float32)
+    got = cp.cumsum(cp.array(x)).get()
+    assert got.dtype == np.float32
+    assert scan_err(got, O.cumsum_f64(x), x) <= 1e-4
+
+
+@pytest.mark.parametrize("shape", [(16, 512), (3, 10000), (4, 65536), (1000, 7), (5, 4096), (2, 4097)])
+def test_rows_axis1(cp, shape):
+    x = np.random.default_rng(sum(shape)).standard_normal(shape).astype(np.float32)
+    got = cp.cumsum(cp.array(x), axis=1).get()
+    ref = O.cumsum_f64(x, axis=1)
+    assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) <= 1e-4
+    xi = np.random.default_rng(1).integers(-100, 101, shape).astype(np.int32)
+    np.testing.assert_array_equal(cp.cumsum(cp.array(xi), axis=1).get(), O.cumsum(xi, axis=1))
+
+
+def test_cols_axis0_and_3d(cp):
+    xi = np.random.default_rng(2).integers(-100, 101, (300, 70)).astype(np.int32)
+    np.testing.assert_array_equal(cp.cumsum(cp.array(xi), axis=0).get(), O.cumsum(xi, axis=0))
+    x3 = np.random.default_rng(3).integers(-9, 10, (4, 5, 6)).astype(np.int64)
+    for ax in (0, 1, 2, None):
+        np.testing.assert_array_equal(cp.cumsum(cp.array(x3), axis=ax).get(), O.cumsum(x3, axis=ax))
+
+
+def test_dtypes(cp):
+    for dt in (np.int16, np.uint16, np.uint32, np.bool_, np.int64):
+        x = np.random.default_rng(4).integers(0, 3, 10000).astype(dt)
+        got = cp.cumsum(cp.array(x))
+        want = np.cumsum(x)
+        assert got.dtype == want.dtype, dt
+        np.testing.assert_array_equal(got.get(), want)
+    x = np.random.default_rng(5).uniform(0.999, 1.001, 5000).astype(np.float32)
+    got = cp.cumprod(cp.array(x)).get()
+    ref = np.cumprod(x.astype(np.float64))
+    assert np.max(np.abs(got - ref) / ref) <= 1e-4
+
+
+def test_repeated_calls_reuse_state(cp):
+    x = np.random.default_rng(6).integers(-5, 6, 100000).astype(np.int32)
+    X = cp.array(x)
+    want = np.cumsum(x)
+    for _ in range(5):
+        np.testing.assert_array_equal(cp.cumsum(X).get(), want)
+    cp.synchronize()
