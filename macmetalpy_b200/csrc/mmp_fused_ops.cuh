@@ -24,7 +24,9 @@
 namespace mmpf {
 using mmpd::isnan_;
 
-// ---- math dispatch on float / double
+// ---- math dispatch on float / double.  float32 functions whose CUDA
+// error bound is above 2 ulp (tan, sinh, cosh, asinh, acosh, atanh, pow,
+// atan2, hypot) are evaluated in double and rounded once.
 __device__ __forceinline__ float m_sqrt(float x) { return sqrtf(x); }
 __device__ __forceinline__ double m_sqrt(double x) { return sqrt(x); }
 __device__ __forceinline__ float m_exp(float x) { return expf(x); }
@@ -35,7 +37,7 @@ __device__ __forceinline__ float m_sin(float x) { return sinf(x); }
 __device__ __forceinline__ double m_sin(double x) { return sin(x); }
 __device__ __forceinline__ float m_cos(float x) { return cosf(x); }
 __device__ __forceinline__ double m_cos(double x) { return cos(x); }
-__device__ __forceinline__ float m_tan(float x) { return tanf(x); }
+__device__ __forceinline__ float m_tan(float x) { return (float)tan((double)x); }
 __device__ __forceinline__ double m_tan(double x) { return tan(x); }
 __device__ __forceinline__ float m_asin(float x) { return asinf(x); }
 __device__ __forceinline__ double m_asin(double x) { return asin(x); }
@@ -43,9 +45,9 @@ __device__ __forceinline__ float m_acos(float x) { return acosf(x); }
 __device__ __forceinline__ double m_acos(double x) { return acos(x); }
 __device__ __forceinline__ float m_atan(float x) { return atanf(x); }
 __device__ __forceinline__ double m_atan(double x) { return atan(x); }
-__device__ __forceinline__ float m_sinh(float x) { return sinhf(x); }
+__device__ __forceinline__ float m_sinh(float x) { return (float)sinh((double)x); }
 __device__ __forceinline__ double m_sinh(double x) { return sinh(x); }
-__device__ __forceinline__ float m_cosh(float x) { return coshf(x); }
+__device__ __forceinline__ float m_cosh(float x) { return (float)cosh((double)x); }
 __device__ __forceinline__ double m_cosh(double x) { return cosh(x); }
 __device__ __forceinline__ float m_tanh(float x) { return tanhf(x); }
 __device__ __forceinline__ double m_tanh(double x) { return tanh(x); }
@@ -61,11 +63,11 @@ __device__ __forceinline__ float m_log1p(float x) { return log1pf(x); }
 __device__ __forceinline__ double m_log1p(double x) { return log1p(x); }
 __device__ __forceinline__ float m_cbrt(float x) { return cbrtf(x); }
 __device__ __forceinline__ double m_cbrt(double x) { return cbrt(x); }
-__device__ __forceinline__ float m_asinh(float x) { return asinhf(x); }
+__device__ __forceinline__ float m_asinh(float x) { return (float)asinh((double)x); }
 __device__ __forceinline__ double m_asinh(double x) { return asinh(x); }
-__device__ __forceinline__ float m_acosh(float x) { return acoshf(x); }
+__device__ __forceinline__ float m_acosh(float x) { return (float)acosh((double)x); }
 __device__ __forceinline__ double m_acosh(double x) { return acosh(x); }
-__device__ __forceinline__ float m_atanh(float x) { return atanhf(x); }
+__device__ __forceinline__ float m_atanh(float x) { return (float)atanh((double)x); }
 __device__ __forceinline__ double m_atanh(double x) { return atanh(x); }
 __device__ __forceinline__ float m_floor(float x) { return floorf(x); }
 __device__ __forceinline__ double m_floor(double x) { return floor(x); }
@@ -77,13 +79,38 @@ __device__ __forceinline__ float m_rint(float x) { return rintf(x); }
 __device__ __forceinline__ double m_rint(double x) { return rint(x); }
 __device__ __forceinline__ float m_fabs(float x) { return fabsf(x); }
 __device__ __forceinline__ double m_fabs(double x) { return fabs(x); }
-__device__ __forceinline__ float m_fmod(float a, float b) { return fmodf(a, b); }
-__device__ __forceinline__ double m_fmod(double a, double b) { return fmod(a, b); }
-__device__ __forceinline__ float m_pow(float a, float b) { return powf(a, b); }
+// Exact fmod.  The remainder a - n*b (n = trunc(a/b)) is always
+// representable, so when the quotient is below 2^24 (2^53 for double) it is
+// computed directly: q = trunc(|a|/|b|) is the true quotient or one above
+// it (rounding of the division can only carry up to the next integer), and
+// fma(-q, |b|, |a|) is then exactly the remainder, or negative, in which case
+// q - 1 gives it.  Larger quotients, infinities, NaN and b == 0 take the
+// library fmod.  Bit-identical to fmodf/fmod, several times cheaper.
+__device__ __forceinline__ float m_fmod(float a, float b) {
+  float ab = fabsf(a), bb = fabsf(b);
+  if (ab < bb * 16777216.0f && bb > 0.0f && bb <= 3.402823466e38f) {
+    float q = truncf(ab / bb);
+    float r = fmaf(-q, bb, ab);
+    if (r < 0.0f) r = fmaf(-(q - 1.0f), bb, ab);
+    return copysignf(r, a);
+  }
+  return fmodf(a, b);
+}
+__device__ __forceinline__ double m_fmod(double a, double b) {
+  double ab = fabs(a), bb = fabs(b);
+  if (ab < bb * 9007199254740992.0 && bb > 0.0 && bb <= 1.7976931348623157e308) {
+    double q = trunc(ab / bb);
+    double r = fma(-q, bb, ab);
+    if (r < 0.0) r = fma(-(q - 1.0), bb, ab);
+    return copysign(r, a);
+  }
+  return fmod(a, b);
+}
+__device__ __forceinline__ float m_pow(float a, float b) { return (float)pow((double)a, (double)b); }
 __device__ __forceinline__ double m_pow(double a, double b) { return pow(a, b); }
-__device__ __forceinline__ float m_atan2(float a, float b) { return atan2f(a, b); }
+__device__ __forceinline__ float m_atan2(float a, float b) { return (float)atan2((double)a, (double)b); }
 __device__ __forceinline__ double m_atan2(double a, double b) { return atan2(a, b); }
-__device__ __forceinline__ float m_hypot(float a, float b) { return hypotf(a, b); }
+__device__ __forceinline__ float m_hypot(float a, float b) { return (float)hypot((double)a, (double)b); }
 __device__ __forceinline__ double m_hypot(double a, double b) { return hypot(a, b); }
 __device__ __forceinline__ float m_copysign(float a, float b) { return copysignf(a, b); }
 __device__ __forceinline__ double m_copysign(double a, double b) { return copysign(a, b); }

@@ -1,10 +1,485 @@
-// Tensor-core GEMM for sm_100a (tcgen05 + TMEM + TMA).  Placeholder until
-// the tcgen05 kernel lands: reports "unsupported" so mmp_gemm falls back.
+// Tensor-core GEMM for sm_100a: TMA -> shared-memory ring -> tcgen05.mma
+// with the accumulator in TMEM -> tcgen05.ld epilogue.
+//
+// Replaces the reference's matmul_op (src/macmetalpy/_kernels.py:735-759),
+// a naive one-thread-per-output kernel that accumulates in the element type.
+//
+// float32 uses the 3xTF32 split: every operand x is written once as
+// big = tf32_round(x) and small = x - big (both exactly representable), and
+// each k-step issues small*big + big*small + big*big into the same float32
+// TMEM accumulator, which keeps float32-level accuracy on the TF32 tensor
+// pipe.  float16 runs kind::f16 with float32 accumulation.
+//
+// A pre-pass writes both operands K-major, zero-padded to whole tiles
+// (A -> [batch][Mp][Kp], B -> B^T [batch][Np][Kp]); that is the only layout
+// the kernel reads, so any M, N, K, leading dimension and alignment works,
+// and every TMA box is fully in bounds.
+//
+// Kernel: one CTA per 128 x 256 output tile (grouped rasterisation for L2
+// reuse), 6 warps: warp 0 issues TMA loads (one elected lane), warp 1
+// allocates TMEM and issues MMAs (one elected lane), warps 2-5 drain TMEM
+// and store C.  Stages are handed over with mbarriers; tcgen05.commit frees
+// a stage when the MMAs reading it have completed.  Every wait is bounded
+// (2 s on %globaltimer): a wait that runs out sets the device error word and
+// the CTA finishes (draining its own TMA loads, freeing TMEM) instead of
+// hanging.  No TMA multicast is used.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "mmp_device.cuh"
 #include "mmp_internal.h"
 
 namespace mmp {
-int gemm_tc(int, int, long long, long long, long long, long long, const void *, long long, long long,
-            const void *, long long, long long, void *, long long, long long) {
-  return set_error(MMP_E_UNSUPPORTED, "tensor-core GEMM not built");
+void *driver_fn(const char *name);
 }
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int NTHREADS = 192;
+constexpr int GROUP_M = 16;  // m-blocks per rasterisation group
+
+enum { MODE_3XTF32 = 0, MODE_TF32 = 1, MODE_F16 = 2 };
+
+template <int MODE> struct Cfg {
+  static constexpr int ELEM = (MODE == MODE_F16) ? 2 : 4;
+  static constexpr int BK = 128 / ELEM;          // one 128-byte swizzle row of K
+  static constexpr int NOPS = (MODE == MODE_3XTF32) ? 2 : 1;  // tiles per operand
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = (MODE == MODE_3XTF32) ? 2 : 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int UMMA_K_BYTES = 32;  // K of one MMA: 8 tf32 or 16 f16
+  static constexpr int KSTEPS = 128 / UMMA_K_BYTES;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase of parity `parity`; gives up after ~2 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > 2000000000ull) {
+      atomicExch(err, 3);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major tile written by TMA with 128-byte
+// swizzle (8-row x 128-byte atoms, 1024 bytes apart), sm100 version field.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused with swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset between 8-row groups
+  d |= (uint64_t)1 << 46;             // descriptor version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D = f32, A/B format, both K-major, N and M.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, int M, int N) {
+  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+template <int MODE>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  if constexpr (MODE == MODE_F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+  }
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+                   const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1, void *C,
+                   long long M, long long N, long long ldc, long long sC, int m_blocks, int n_blocks,
+                   int k_tiles, int a_bcast, int b_bcast, int *err) {
+  typedef Cfg<MODE> G;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = (uint64_t *)(smem + G::STAGES * G::STAGE_BYTES);
+  uint64_t *empty = full + G::STAGES;
+  uint64_t *accum = empty + G::STAGES;
+  uint32_t *tmem_holder = (uint32_t *)(accum + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // grouped rasterisation: GROUP_M m-blocks share the n sweep (L2 reuse)
+  const int pid = blockIdx.x;
+  const int per_group = GROUP_M * n_blocks;
+  const int first_m = (pid / per_group) * GROUP_M;
+  const int gsize = min(m_blocks - first_m, GROUP_M);
+  const int m_blk = first_m + (pid % per_group) % gsize;
+  const int n_blk = (pid % per_group) / gsize;
+  const int bz = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int ca = a_bcast ? 0 : bz, cb = b_bcast ? 0 : bz;
+      int issued = 0;
+      for (int kt = 0; kt < k_tiles; ++kt) {
+        const int s = kt % G::STAGES;
+        const uint32_t ph = (uint32_t)(kt / G::STAGES) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, err)) break;
+        uint8_t *st = smem + s * G::STAGE_BYTES;
+        mbar_expect_tx(&full[s], G::STAGE_BYTES);
+        const int kc = kt * G::BK;
+        tma_load_3d(st, &tmA0, &full[s], kc, m_blk * BM, ca);
+        if (G::NOPS == 2) tma_load_3d(st + G::A_BYTES, &tmA1, &full[s], kc, m_blk * BM, ca);
+        tma_load_3d(st + G::NOPS * G::A_BYTES, &tmB0, &full[s], kc, n_blk * BN, cb);
+        if (G::NOPS == 2) tma_load_3d(st + G::NOPS * G::A_BYTES + G::B_BYTES, &tmB1, &full[s], kc, n_blk * BN, cb);
+        issued = kt + 1;
+      }
+      // drain: every load this CTA issued has landed before it may exit
+      for (int kt = (issued > G::STAGES ? issued - G::STAGES : 0); kt < issued; ++kt)
+        mbar_wait(&full[kt % G::STAGES], (uint32_t)(kt / G::STAGES) & 1u, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID = make_idesc(MODE == MODE_F16 ? 0u : 2u, BM, BN);
+      for (int kt = 0; kt < k_tiles; ++kt) {
+        const int s = kt % G::STAGES;
+        const uint32_t ph = (uint32_t)(kt / G::STAGES) & 1u;
+        if (!mbar_wait(&full[s], ph, err)) break;
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * G::STAGE_BYTES);
+        const uint32_t b0 = base + G::NOPS * G::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G::KSTEPS; ++kk) {
+          const uint32_t off = kk * G::UMMA_K_BYTES;
+          const uint64_t da0 = sw128_desc(base + off);
+          const uint64_t db0 = sw128_desc(b0 + off);
+          const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+          if (MODE == MODE_3XTF32) {
+            const uint64_t da1 = sw128_desc(base + G::A_BYTES + off);
+            const uint64_t db1 = sw128_desc(b0 + G::B_BYTES + off);
+            umma<MODE>(tmem, da1, db0, ID, acc);  // small * big
+            umma<MODE>(tmem, da0, db1, ID, 1u);   // big * small
+            umma<MODE>(tmem, da0, db0, ID, 1u);   // big * big
+          } else {
+            umma<MODE>(tmem, da0, db0, ID, acc);
+          }
+        }
+        umma_commit(&empty[s]);  // stage reusable once these MMAs are done
+      }
+      umma_commit(accum);  // accumulator complete
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its quadrant)
+    const bool ok = mbar_wait(accum, 0u, err);
+    tc_fence_after();
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const long long gm = (long long)m_blk * BM + row;
+    const long long n0 = (long long)n_blk * BN;
+    const bool row_ok = ok && gm < M;
+    char *crow = (char *)C + ((long long)bz * sC + gm * ldc) * (MODE == MODE_F16 ? 2 : 4);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+      if (!row_ok) continue;
+      const long long col0 = n0 + c * 32;
+      if (col0 >= N) continue;
+      if (MODE == MODE_F16) {
+        __half *p = (__half *)crow + col0;
+        if (col0 + 32 <= N && ((uintptr_t)p & 15) == 0) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            __half2 h0 = __floats2half2_rn(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+            __half2 h1 = __floats2half2_rn(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+            __half2 h2 = __floats2half2_rn(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+            __half2 h3 = __floats2half2_rn(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+            w.x = *reinterpret_cast<uint32_t *>(&h0);
+            w.y = *reinterpret_cast<uint32_t *>(&h1);
+            w.z = *reinterpret_cast<uint32_t *>(&h2);
+            w.w = *reinterpret_cast<uint32_t *>(&h3);
+            reinterpret_cast<uint4 *>(p)[v] = w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < N) p[j] = __float2half_rn(__uint_as_float(r[j]));
+        }
+      } else {
+        float *p = (float *)crow + col0;
+        if (col0 + 32 <= N && ((uintptr_t)p & 15) == 0) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            reinterpret_cast<float4 *>(p)[v] =
+                make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
+                            __uint_as_float(r[4 * v + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < N) p[j] = __uint_as_float(r[j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- pre-pass
+__device__ __forceinline__ float tf32_round(float v) {
+  uint32_t u = __float_as_uint(v);
+  if ((u & 0x7f800000u) == 0x7f800000u) return v;  // inf / nan unchanged
+  u = (u + 0x1000u) & 0xffffe000u;
+  return __uint_as_float(u);
+}
+
+// A[b] (M x K, row stride lda) -> out0/out1 [b][Mp][Kp], zero padded.
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) prep_rows_kernel(const T *__restrict__ A, long long lda, long long sA,
+                                                        long long M, long long K, long long Mp, long long Kp,
+                                                        long long batch, T *__restrict__ out0,
+                                                        T *__restrict__ out1) {
+  const long long total = batch * Mp * Kp;
+  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const long long k = i % Kp;
+    const long long t = i / Kp;
+    const long long m = t % Mp;
+    const long long b = t / Mp;
+    T v = (m < M && k < K) ? A[b * sA + m * lda + k] : T(0);
+    if constexpr (MODE == MODE_3XTF32) {
+      float big = tf32_round((float)v);
+      out0[i] = big;
+      out1[i] = (float)v - big;
+    } else if constexpr (MODE == MODE_TF32) {
+      out0[i] = tf32_round((float)v);
+    } else {
+      out0[i] = v;
+    }
+  }
+}
+
+// B[b] (K x N, row stride ldb) -> out[b][Np][Kp] = B^T, through a 32x32
+// shared tile so that reads and writes are both coalesced.
+template <class T, int MODE>
+__global__ void __launch_bounds__(256) prep_cols_kernel(const T *__restrict__ B, long long ldb, long long sB,
+                                                        long long K, long long N, long long Np, long long Kp,
+                                                        T *__restrict__ out0, T *__restrict__ out1) {
+  __shared__ T tile[32][33];
+  const long long b = blockIdx.z;
+  const long long n0 = (long long)blockIdx.x * 32, k0 = (long long)blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < 32; r += 8) {
+    const long long k = k0 + r, n = n0 + tx;
+    tile[r][tx] = (k < K && n < N) ? B[b * sB + k * ldb + n] : T(0);
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const long long n = n0 + r, k = k0 + tx;
+    const long long o = (b * Np + n) * Kp + k;
+    T v = tile[tx][r];
+    if constexpr (MODE == MODE_3XTF32) {
+      float big = tf32_round((float)v);
+      out0[o] = big;
+      out1[o] = (float)v - big;
+    } else if constexpr (MODE == MODE_TF32) {
+      out0[o] = tf32_round((float)v);
+    } else {
+      out0[o] = v;
+    }
+  }
+}
+
+typedef CUresult (*PFN_Encode)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                               const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static int make_map(CUtensorMap *map, const void *base, bool f16, long long kp, long long rows, long long batch,
+                    int box_k, int box_rows) {
+  static PFN_Encode enc = nullptr;
+  if (!enc) enc = (PFN_Encode)mmp::driver_fn("cuTensorMapEncodeTiled");
+  if (!enc) return mmp::set_error(MMP_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int es = f16 ? 2 : 4;
+  cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(kp * es), (cuuint64_t)(kp * rows * es)};
+  cuuint32_t box[3] = {(cuuint32_t)box_k, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                   const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return mmp::set_error(MMP_E_CUDA, "cuTensorMapEncodeTiled failed");
+  return MMP_OK;
+}
+
+template <int MODE, class T>
+static int run(long long batch, long long m, long long n, long long k, const void *a, long long lda, long long sa,
+               const void *b, long long ldb, long long sb, void *c, long long ldc, long long sc) {
+  typedef Cfg<MODE> G;
+  cudaStream_t st = mmp::stream();
+  if (!st) return mmp::set_error(MMP_E_CUDA, "no stream");
+  const long long Mp = (m + BM - 1) / BM * BM;
+  const long long Np = (n + BN - 1) / BN * BN;
+  const long long Kp = (k + G::BK - 1) / G::BK * G::BK;
+  const int a_bc = (sa == 0 && batch > 1) ? 1 : 0;
+  const int b_bc = (sb == 0 && batch > 1) ? 1 : 0;
+  const long long ba = a_bc ? 1 : batch, bb = b_bc ? 1 : batch;
+  const long long m_blocks = Mp / BM, n_blocks = Np / BN, k_tiles = Kp / G::BK;
+  if (m_blocks * n_blocks > 0x7fffffffll || batch > 65535 || k_tiles > 0x7fffffffll)
+    return mmp::set_error(MMP_E_UNSUPPORTED, "GEMM too large for one launch");
+  const size_t es = G::ELEM;
+  const size_t a_el = (size_t)ba * Mp * Kp, b_el = (size_t)bb * Np * Kp;
+  const size_t ws_bytes = G::NOPS * (a_el + b_el) * es + 1024;
+  char *ws = nullptr;
+  MMP_CUDA_TRY(cudaMallocAsync((void **)&ws, ws_bytes, st));
+  T *A0 = (T *)ws;
+  T *A1 = A0 + a_el;                       // used by 3xTF32 only
+  T *B0 = A0 + (G::NOPS == 2 ? 2 * a_el : a_el);
+  T *B1 = B0 + b_el;
+  {
+    const long long tot = (long long)a_el;
+    long long blocks = (tot + 255) / 256;
+    if (blocks > (long long)mmp::sm_count() * 16) blocks = (long long)mmp::sm_count() * 16;
+    prep_rows_kernel<T, MODE><<<(unsigned)blocks, 256, 0, st>>>((const T *)a, lda, sa, m, k, Mp, Kp, ba, A0, A1);
+    dim3 g2((unsigned)(Np / 32), (unsigned)(Kp / 32), (unsigned)bb);
+    prep_cols_kernel<T, MODE><<<g2, 256, 0, st>>>((const T *)b, ldb, sb, k, n, Np, Kp, B0, B1);
+  }
+  CUtensorMap mA0, mA1, mB0, mB1;
+  const bool f16 = MODE == MODE_F16;
+  int rc = make_map(&mA0, A0, f16, Kp, Mp, ba, G::BK, BM);
+  if (!rc) rc = make_map(&mA1, G::NOPS == 2 ? (const void *)A1 : (const void *)A0, f16, Kp, Mp, ba, G::BK, BM);
+  if (!rc) rc = make_map(&mB0, B0, f16, Kp, Np, bb, G::BK, BN);
+  if (!rc) rc = make_map(&mB1, G::NOPS == 2 ? (const void *)B1 : (const void *)B0, f16, Kp, Np, bb, G::BK, BN);
+  if (rc) {
+    cudaFreeAsync(ws, st);
+    return rc;
+  }
+  static bool attr = false;
+  if (!attr) {
+    MMP_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+    attr = true;
+  }
+  dim3 grid((unsigned)(m_blocks * n_blocks), (unsigned)batch, 1);
+  gemm_tc_kernel<MODE><<<grid, NTHREADS, G::SMEM, st>>>(mA0, mA1, mB0, mB1, c, m, n, ldc, sc, (int)m_blocks,
+                                                        (int)n_blocks, (int)k_tiles, a_bc, b_bc,
+                                                        mmp::device_error_word());
+  cudaError_t e = cudaGetLastError();
+  cudaFreeAsync(ws, st);
+  if (e != cudaSuccess) return mmp::cuda_error(e, "gemm_tc_kernel");
+  return MMP_OK;
+}
+
+}  // namespace tc
+
+namespace mmp {
+
+int gemm_tc(int dtype, int mode, long long batch, long long m, long long n, long long k, const void *a, long long lda,
+            long long sa, const void *b, long long ldb, long long sb, void *c, long long ldc, long long sc) {
+  if (mode == MMP_GEMM_AUTO && m * n * k < (1ll << 21))
+    return set_error(MMP_E_UNSUPPORTED, "small problem: CUDA-core path");
+  if (dtype == MMP_FLOAT32) {
+    if (mode == MMP_GEMM_AUTO || mode == MMP_GEMM_3XTF32)
+      return tc::run<tc::MODE_3XTF32, float>(batch, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc);
+    if (mode == MMP_GEMM_TF32)
+      return tc::run<tc::MODE_TF32, float>(batch, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc);
+  }
+  if (dtype == MMP_FLOAT16 && (mode == MMP_GEMM_AUTO || mode == MMP_GEMM_F16))
+    return tc::run<tc::MODE_F16, __half>(batch, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc);
+  return set_error(MMP_E_UNSUPPORTED, "no tensor-core path for this dtype/mode");
+}
+
 }  // namespace mmp

@@ -99,7 +99,8 @@ def _scalar_result(dt) -> ndarray:
     return ndarray._empty((), dt)
 
 
-def _reduce(a, kind: str, axis=None, keepdims=False, ddof=0.0, dtype=None, out=None, partial=False):
+def _reduce(a, kind: str, axis=None, keepdims=False, ddof=0.0, dtype=None, out=None, partial=False,
+            out_dt=None):
     a = _asarray(a)
     if dtype is not None:
         a = a.astype(resolve_dtype(dtype), copy=False)
@@ -107,7 +108,7 @@ def _reduce(a, kind: str, axis=None, keepdims=False, ddof=0.0, dtype=None, out=N
         k = kind
     else:  # no NaN in integer/bool arrays (nan_ops.py:132-134)
         k = kind[3:]
-    odt = out_dtype(k, a._dtype)
+    odt = out_dtype(k, a._dtype) if out_dt is None else np.dtype(out_dt)
     axes = _norm_axes(axis, a.ndim)
     if axes is not None and len(axes) == a.ndim:
         axes = None if not (k in ("argmax", "argmin") and a.ndim > 1) else axes
@@ -254,7 +255,9 @@ def _arg(a, kind, axis, out, keepdims):
         if out is not None:
             return _finish(r, out)
         return int(r.get())
-    return _reduce(a, kind, (int(axis),), keepdims, out=out)
+    # axis arg-reductions return int32, as the reference's _reduce_axis
+    # (reductions.py:410, ndarray.py:2015-2035) does on both of its paths
+    return _reduce(a, kind, (int(axis),), keepdims, out=out, out_dt=np.int32)
 
 
 def argmax(a, axis=None, out=None, keepdims=False):

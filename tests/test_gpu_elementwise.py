@@ -39,7 +39,15 @@ def test_binary_sweep_bit_exact(cp, n, dtype):
     np.testing.assert_array_equal((A % B).get(), O.mod(a, b))
     if dtype == np.float32:
         got = cp.logaddexp(A, B).get()
-        assert O.ulp_error(got, np.logaddexp(a.astype(np.float64), b.astype(np.float64))).max(initial=0) <= 2
+        ref64 = np.logaddexp(a.astype(np.float64), b.astype(np.float64))
+        # <= 2 ulp except where the result cancels towards 0 (x ~ -log1p(e^-|d|)),
+        # where the float32 algorithm itself (numpy's, the reference's) loses digits:
+        # there the bar is 2 ulp of the larger operand
+        scale = np.maximum(np.abs(ref64), np.maximum(np.abs(a), np.abs(b)).astype(np.float64))
+        err = np.abs(got.astype(np.float64) - ref64) / np.spacing(scale.astype(np.float32)).astype(np.float64)
+        assert err.max(initial=0) <= 2
+        refnp = O.logaddexp(a, b)
+        assert (np.abs(got.astype(np.float64) - refnp) <= 2 * np.spacing(np.abs(refnp))).all()
 
 
 @pytest.mark.parametrize("dtype", [np.int16, np.uint16, np.int64, np.uint32, np.float16, np.float64])
@@ -168,4 +176,5 @@ def test_shared_subexpression(cp):
     s = cp.sin(X)
     r = s * s + s
     sn = np.sin(x.astype(np.float64))
-    assert O.ulp_error(r.get(), sn * sn + sn).max() < 8
+    # absolute bar: the sum cancels near s = -1 and s = 0
+    assert np.max(np.abs(r.get() - (sn * sn + sn))) <= 4 * np.spacing(np.float32(2))

@@ -41,7 +41,8 @@ def test_c1_expression_and_fused_reductions(cp):
     x64 = x.astype(np.float64)
     y64 = np.sqrt(np.abs(x64)) + np.exp(-(x64 * x64))
     assert O.ulp_error(y.get(), y64).max() <= 2.0
-    np.testing.assert_allclose(y.get(), G["c1_y"], rtol=2e-7, atol=0)
+    # libm (reference) and CUDA exp may differ by an ulp: within 2 ulp of the reference
+    assert (np.abs(y.get() - G["c1_y"]) <= 2 * np.spacing(G["c1_y"])).all()
     s = cp.sum(y)  # fused: the expression runs inside the reduction
     m = cp.mean(y)
     assert s.dtype == np.float32 and m.dtype == np.float32
