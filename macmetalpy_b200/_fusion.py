@@ -252,7 +252,7 @@ def _binary_expr(op: str, dt, a: str, b: str) -> str:
     if op == "floor_divide_op":
         if isbool:
             return f"({a} && {b})"
-        return f"mmpf::f_floor_divide<{R}>({a}, {b})" if f else f"mmpf::i_floor_divide<{R}>({a}, {b})"
+        return f"mmpf::floor_divide_f<{R}>({a}, {b})" if f else f"mmpf::i_floor_divide<{R}>({a}, {b})"
     if op == "mod_op":  # the reference's composite a - floor_divide(a, b) * b
         if isbool:
             return f"(({a}) && !({b}))"

@@ -151,6 +151,41 @@ __device__ __forceinline__ R f_floor_divide(R a, R b) {
   return floordiv;
 }
 
+// float32 floor_divide with the same result as numpy's algorithm above,
+// cheaper: for |a/b| < 2^20 with a normal, finite b, the truncated quotient q
+// and remainder r of |a| / |b| are found exactly (approximate division, then
+// an exact fma remainder that corrects q by one either way), and numpy's
+// result is then s*q, minus one when r != 0 and the signs differ (s < 0),
+// with numpy's signed zero when q == 0.  In that range numpy's own f32
+// steps (fmod, (a - mod) / b, floor, snap) land exactly on that integer: the
+// rounding of (a - mod) / b stays within q * 2^-23 < 1/8 of it.  Everything
+// else takes f_floor_divide.
+__device__ __forceinline__ float f_floor_divide_fast(float a, float b) {
+  const float ab = fabsf(a), bb = fabsf(b);
+  if (ab < bb * 1048576.0f && bb >= 1.17549435e-38f && bb < 8.50705917e37f) {
+    float q = truncf(__fdividef(ab, bb));
+    float r = fmaf(-q, bb, ab);
+    if (r < 0.0f) {
+      q -= 1.0f;
+      r = fmaf(-q, bb, ab);
+    } else if (r >= bb) {
+      q += 1.0f;
+      r = fmaf(-q, bb, ab);
+    }
+    const bool neg = (__float_as_uint(a) ^ __float_as_uint(b)) >> 31;
+    if (q == 0.0f) {
+      if (r == 0.0f) return neg ? -0.0f : 0.0f;
+      return neg ? -1.0f : 0.0f;
+    }
+    return neg ? -(q + (r != 0.0f ? 1.0f : 0.0f)) : q;
+  }
+  return f_floor_divide<float>(a, b);
+}
+template <class R> __device__ __forceinline__ R floor_divide_f(R a, R b) { return f_floor_divide<R>(a, b); }
+template <> __device__ __forceinline__ float floor_divide_f<float>(float a, float b) {
+  return f_floor_divide_fast(a, b);
+}
+
 template <class R>
 __device__ __forceinline__ R f_remainder(R a, R b) {
   R mod = m_fmod(a, b);
@@ -194,7 +229,7 @@ __device__ __forceinline__ I i_remainder(I a, I b) {
 // This is not np.remainder for floats; it is what the reference returns.
 template <class T, class R>
 __device__ __forceinline__ R ref_mod_f(R a, R b) {
-  R fd = mmpd::cvt<R>(mmpd::cvt<T>(f_floor_divide<R>(a, b)));
+  R fd = mmpd::cvt<R>(mmpd::cvt<T>(floor_divide_f<R>(a, b)));
   R t = mmpd::cvt<R>(mmpd::cvt<T>(fd * b));
   return a - t;
 }

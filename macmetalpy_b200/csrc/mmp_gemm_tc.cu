@@ -16,9 +16,10 @@
 // and every TMA box is fully in bounds.
 //
 // Kernel: one CTA per 128 x 256 output tile (grouped rasterisation for L2
-// reuse), 6 warps: warp 0 issues TMA loads (one elected lane), warp 1
-// allocates TMEM and issues MMAs (one elected lane), warps 2-5 drain TMEM
-// and store C.  Stages are handed over with mbarriers; tcgen05.commit frees
+// reuse): warp 0 issues TMA loads (one elected lane), warp 1 allocates TMEM
+// and issues MMAs (one elected lane), the epilogue warps drain TMEM and
+// store C (8 warps accumulating every CHUNK k-tiles for the TF32 modes, see
+// Cfg::FLUSH; 4 warps for float16).  Stages are handed over with mbarriers; tcgen05.commit frees
 // a stage when the MMAs reading it have completed.  Every wait is bounded
 // (2 s on %globaltimer): a wait that runs out sets the device error word and
 // the CTA finishes (draining its own TMA loads, freeing TMEM) instead of
@@ -38,7 +39,6 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int NTHREADS = 192;
 constexpr int GROUP_M = 16;  // m-blocks per rasterisation group
 
 enum { MODE_3XTF32 = 0, MODE_TF32 = 1, MODE_F16 = 2 };
@@ -54,6 +54,16 @@ template <int MODE> struct Cfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int UMMA_K_BYTES = 32;  // K of one MMA: 8 tf32 or 16 f16
   static constexpr int KSTEPS = 128 / UMMA_K_BYTES;
+  // TF32 modes drain the TMEM accumulator every CHUNK k-tiles into
+  // round-to-nearest float32 registers (two TMEM buffers alternate, so the
+  // MMAs never wait): the tensor core's float32 accumulation then only spans
+  // CHUNK * BK terms, which keeps the 3xTF32 result at float32 accuracy for
+  // any K.  float16 keeps one accumulator for the whole K.
+  static constexpr bool FLUSH = (MODE != MODE_F16);
+  static constexpr int CHUNK = 4;
+  static constexpr int EPI_WARPS = FLUSH ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int TMEM_COLS = FLUSH ? 2 * BN : BN;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -165,7 +175,44 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__device__ __forceinline__ void store_chunk32(char *crow, long long col0, long long N, const float *v) {
+  if (MODE == MODE_F16) {
+    __half *p = (__half *)crow + col0;
+    if (col0 + 32 <= N && ((uintptr_t)p & 15) == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        __half2 h0 = __floats2half2_rn(v[q * 8 + 0], v[q * 8 + 1]);
+        __half2 h1 = __floats2half2_rn(v[q * 8 + 2], v[q * 8 + 3]);
+        __half2 h2 = __floats2half2_rn(v[q * 8 + 4], v[q * 8 + 5]);
+        __half2 h3 = __floats2half2_rn(v[q * 8 + 6], v[q * 8 + 7]);
+        w.x = *reinterpret_cast<uint32_t *>(&h0);
+        w.y = *reinterpret_cast<uint32_t *>(&h1);
+        w.z = *reinterpret_cast<uint32_t *>(&h2);
+        w.w = *reinterpret_cast<uint32_t *>(&h3);
+        reinterpret_cast<uint4 *>(p)[q] = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) p[j] = __float2half_rn(v[j]);
+    }
+  } else {
+    float *p = (float *)crow + col0;
+    if (col0 + 32 <= N && ((uintptr_t)p & 15) == 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4 *>(p)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) p[j] = v[j];
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1, void *C,
                    long long M, long long N, long long ldc, long long sC, int m_blocks, int n_blocks,
@@ -175,8 +222,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = (uint64_t *)(smem + G::STAGES * G::STAGE_BYTES);
   uint64_t *empty = full + G::STAGES;
-  uint64_t *accum = empty + G::STAGES;
-  uint32_t *tmem_holder = (uint32_t *)(accum + 1);
+  uint64_t *acc_full = empty + G::STAGES;  // [2]
+  uint64_t *acc_empty = acc_full + 2;      // [2]
+  uint32_t *tmem_holder = (uint32_t *)(acc_empty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   // grouped rasterisation: GROUP_M m-blocks share the n sweep (L2 reuse)
@@ -187,18 +235,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int m_blk = first_m + (pid % per_group) % gsize;
   const int n_blk = (pid % per_group) / gsize;
   const int bz = blockIdx.y;
+  const int chunk_kt = G::FLUSH ? G::CHUNK : k_tiles;
+  const int nchunks = (k_tiles + chunk_kt - 1) / chunk_kt;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], G::EPI_WARPS);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
-                 "r"(BN)
+                 "r"(G::TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -231,11 +284,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t ID = make_idesc(MODE == MODE_F16 ? 0u : 2u, BM, BN);
-      for (int kt = 0; kt < k_tiles; ++kt) {
+      bool ok = true;
+      for (int kt = 0; kt < k_tiles && ok; ++kt) {
+        const int chunk = kt / chunk_kt;
+        const int buf = chunk & 1;
+        const bool first_of_chunk = (kt % chunk_kt) == 0;
+        if (first_of_chunk && chunk >= 2) {  // buffer drained by the epilogue?
+          if (!mbar_wait(&acc_empty[buf], (uint32_t)((chunk >> 1) - 1) & 1u, err)) break;
+          tc_fence_after();
+        }
         const int s = kt % G::STAGES;
         const uint32_t ph = (uint32_t)(kt / G::STAGES) & 1u;
         if (!mbar_wait(&full[s], ph, err)) break;
         tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
         const uint32_t base = smem_u32(smem + s * G::STAGE_BYTES);
         const uint32_t b0 = base + G::NOPS * G::A_BYTES;
 #pragma unroll
@@ -243,72 +305,72 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t off = kk * G::UMMA_K_BYTES;
           const uint64_t da0 = sw128_desc(base + off);
           const uint64_t db0 = sw128_desc(b0 + off);
-          const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+          const uint32_t acc = (!first_of_chunk || kk > 0) ? 1u : 0u;
           if (MODE == MODE_3XTF32) {
             const uint64_t da1 = sw128_desc(base + G::A_BYTES + off);
             const uint64_t db1 = sw128_desc(b0 + G::B_BYTES + off);
-            umma<MODE>(tmem, da1, db0, ID, acc);  // small * big
-            umma<MODE>(tmem, da0, db1, ID, 1u);   // big * small
-            umma<MODE>(tmem, da0, db0, ID, 1u);   // big * big
+            umma<MODE>(d, da1, db0, ID, acc);  // small * big
+            umma<MODE>(d, da0, db1, ID, 1u);   // big * small
+            umma<MODE>(d, da0, db0, ID, 1u);   // big * big
           } else {
-            umma<MODE>(tmem, da0, db0, ID, acc);
+            umma<MODE>(d, da0, db0, ID, acc);
           }
         }
         umma_commit(&empty[s]);  // stage reusable once these MMAs are done
+        if ((kt % chunk_kt) == chunk_kt - 1 || kt == k_tiles - 1) umma_commit(&acc_full[buf]);
       }
-      umma_commit(accum);  // accumulator complete
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its quadrant)
-    const bool ok = mbar_wait(accum, 0u, err);
-    tc_fence_after();
+    // epilogue warps: lane quadrant q = warp % 4 (TMEM access rule), column
+    // half h when there are 8 of them
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int h = (G::EPI_WARPS == 8) ? (ew >> 2) : 0;
+    constexpr int COLS = BN / (G::EPI_WARPS / 4);  // columns per warp
     const int row = q * 32 + lane;
     const long long gm = (long long)m_blk * BM + row;
-    const long long n0 = (long long)n_blk * BN;
-    const bool row_ok = ok && gm < M;
+    const long long n0 = (long long)n_blk * BN + h * COLS;
     char *crow = (char *)C + ((long long)bz * sC + gm * ldc) * (MODE == MODE_F16 ? 2 : 4);
+    bool ok = true;
+    if (G::FLUSH) {
+      float acc[COLS];
+#pragma unroll
+      for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
+      for (int chunk = 0; chunk < nchunks; ++chunk) {
+        const int buf = chunk & 1;
+        if (ok) ok = mbar_wait(&acc_full[buf], (uint32_t)(chunk >> 1) & 1u, err);
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < COLS / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + h * COLS + c * 32), r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c * 32 + j] += __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[buf]))
+                                    : "memory");
+      }
+      if (ok && gm < M) {
+#pragma unroll
+        for (int c = 0; c < COLS / 32; ++c) {
+          const long long col0 = n0 + c * 32;
+          if (col0 < N) store_chunk32<MODE>(crow, col0, N, acc + c * 32);
+        }
+      }
+    } else {
+      ok = mbar_wait(&acc_full[0], 0u, err);
+      tc_fence_after();
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
-      if (!row_ok) continue;
-      const long long col0 = n0 + c * 32;
-      if (col0 >= N) continue;
-      if (MODE == MODE_F16) {
-        __half *p = (__half *)crow + col0;
-        if (col0 + 32 <= N && ((uintptr_t)p & 15) == 0) {
+      for (int c = 0; c < COLS / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * COLS + c * 32), r);
+        float v[32];
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            __half2 h0 = __floats2half2_rn(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-            __half2 h1 = __floats2half2_rn(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-            __half2 h2 = __floats2half2_rn(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-            __half2 h3 = __floats2half2_rn(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-            w.x = *reinterpret_cast<uint32_t *>(&h0);
-            w.y = *reinterpret_cast<uint32_t *>(&h1);
-            w.z = *reinterpret_cast<uint32_t *>(&h2);
-            w.w = *reinterpret_cast<uint32_t *>(&h3);
-            reinterpret_cast<uint4 *>(p)[v] = w;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < N) p[j] = __float2half_rn(__uint_as_float(r[j]));
-        }
-      } else {
-        float *p = (float *)crow + col0;
-        if (col0 + 32 <= N && ((uintptr_t)p & 15) == 0) {
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            reinterpret_cast<float4 *>(p)[v] =
-                make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
-                            __uint_as_float(r[4 * v + 3]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < N) p[j] = __uint_as_float(r[j]);
-        }
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const long long col0 = n0 + c * 32;
+        if (ok && gm < M && col0 < N) store_chunk32<MODE>(crow, col0, N, v);
       }
     }
   }
@@ -316,7 +378,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TMEM_COLS) : "memory");
   }
 }
 
@@ -454,7 +516,7 @@ static int run(long long batch, long long m, long long n, long long k, const voi
     attr = true;
   }
   dim3 grid((unsigned)(m_blocks * n_blocks), (unsigned)batch, 1);
-  gemm_tc_kernel<MODE><<<grid, NTHREADS, G::SMEM, st>>>(mA0, mA1, mB0, mB1, c, m, n, ldc, sc, (int)m_blocks,
+  gemm_tc_kernel<MODE><<<grid, G::THREADS, G::SMEM, st>>>(mA0, mA1, mB0, mB1, c, m, n, ldc, sc, (int)m_blocks,
                                                         (int)n_blocks, (int)k_tiles, a_bc, b_bc,
                                                         mmp::device_error_word());
   cudaError_t e = cudaGetLastError();

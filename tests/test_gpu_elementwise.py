@@ -46,8 +46,8 @@ def test_binary_sweep_bit_exact(cp, n, dtype):
         scale = np.maximum(np.abs(ref64), np.maximum(np.abs(a), np.abs(b)).astype(np.float64))
         err = np.abs(got.astype(np.float64) - ref64) / np.spacing(scale.astype(np.float32)).astype(np.float64)
         assert err.max(initial=0) <= 2
-        refnp = O.logaddexp(a, b)
-        assert (np.abs(got.astype(np.float64) - refnp) <= 2 * np.spacing(np.abs(refnp))).all()
+        refnp = O.logaddexp(a, b).astype(np.float64)
+        assert (np.abs(got.astype(np.float64) - refnp) <= 2 * np.spacing(scale.astype(np.float32))).all()
 
 
 @pytest.mark.parametrize("dtype", [np.int16, np.uint16, np.int64, np.uint32, np.float16, np.float64])
@@ -178,3 +178,30 @@ def test_shared_subexpression(cp):
     sn = np.sin(x.astype(np.float64))
     # absolute bar: the sum cancels near s = -1 and s = 0
     assert np.max(np.abs(r.get() - (sn * sn + sn))) <= 4 * np.spacing(np.float32(2))
+
+
+def test_floor_divide_mod_magnitude_sweep(cp):
+    """Bit-exact float32 floor_divide / mod across quotient magnitudes (both
+    sides of the 2^20 fast-path bound), tiny and huge divisors, subnormals,
+    signed zeros, infinities and NaN."""
+    rng = np.random.default_rng(11)
+    n = 1 << 18
+    ea = rng.uniform(-40, 40, n)
+    eb = rng.uniform(-40, 40, n)
+    a = (rng.choice([-1, 1], n) * rng.uniform(1, 2, n) * 2.0 ** ea).astype(np.float32)
+    b = (rng.choice([-1, 1], n) * rng.uniform(1, 2, n) * 2.0 ** eb).astype(np.float32)
+    special = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 3.4e38, 1.0, -1.0, 2 ** 20, 2 ** 21],
+                       np.float32)
+    a[:144] = np.repeat(special, 12)
+    b[:144] = np.tile(special, 12)
+    A, B = cp.array(a), cp.array(b)
+    np.testing.assert_array_equal(cp.floor_divide(A, B).get(), O.floor_divide(a, b))
+    np.testing.assert_array_equal((A % B).get(), O.mod(a, b))
+    ai = rng.integers(-2 ** 31, 2 ** 31, n).astype(np.int32)
+    bi = rng.integers(-2 ** 31, 2 ** 31, n).astype(np.int32)
+    bi[:100] = rng.integers(-3, 4, 100)
+    ai[:8] = [-2 ** 31, -2 ** 31, 2 ** 31 - 1, 0, 7, -7, 5, -5]
+    bi[:8] = [-1, 1, -1, 0, 0, 0, -1, 1]
+    Ai, Bi = cp.array(ai), cp.array(bi)
+    np.testing.assert_array_equal(cp.floor_divide(Ai, Bi).get(), O.floor_divide(ai, bi))
+    np.testing.assert_array_equal((Ai % Bi).get(), O.mod(ai, bi))
