@@ -322,9 +322,13 @@ def main():
     ap.add_argument("--no-suite", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--case", default=None, help="time one op only (for profiling): " + ", ".join(CASES))
+    ap.add_argument("--elements", type=int, default=1 << 26, help="--case size (matmul: n of n^3)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.case:
+        return run_case(args)
     rank, world, local = _env()
     dist = None
     if world > 1:
@@ -422,6 +426,70 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+CASES = ("add_f32", "floor_divide_f32", "mod_f32", "logaddexp_f32", "add_i32", "floor_divide_i32", "mod_i32",
+         "bcast_add_f32", "c1_fused_sum", "sum_f32", "var_f32", "argmax_f32", "sum_axis0_f32", "sum_axis1_f32",
+         "cumsum_i32", "cumsum_f32", "cumsum_axis1_f32", "matmul_f32", "matmul_f16")
+
+
+def run_case(args):
+    """One op at one size, `--steps` timed launches after `--warmup` (for ncu)."""
+    import macmetalpy_b200 as cp
+
+    gen = Gen(cp)
+    n = args.elements
+    c = args.case
+    if c.endswith("_i32") and c[:-4] in I32_OPS:
+        a, b = gen.integers((n,), -1000, 1000, 3), gen.integers((n,), 1, 50, 4, signed=True)
+        o = cp.empty((n,), dtype=np.int32)
+        f = getattr(cp, c[:-4])
+        fn, nb = (lambda: f(a, b, out=o)), 12 * n
+    elif c.endswith("_f32") and c[:-4] in F32_OPS:
+        a, b = gen.uniform((n,), -1000, 1000, 1), gen.signed_uniform((n,), 1, 50, 2)
+        o = cp.empty((n,), dtype=np.float32)
+        f = getattr(cp, c[:-4])
+        fn, nb = (lambda: f(a, b, out=o)), 12 * n
+    elif c == "bcast_add_f32":
+        rows = max(1, n // BC_COLS)
+        r, cc = gen.normal((rows, 1), 5), gen.normal((1, BC_COLS), 6)
+        o = cp.empty((rows, BC_COLS), dtype=np.float32)
+        fn, nb = (lambda: cp.add(r, cc, out=o)), 4 * rows * BC_COLS + 4 * (rows + BC_COLS)
+    elif c == "c1_fused_sum":
+        x = gen.normal((n,), 11)
+        fn, nb = (lambda: cp.sum(cp.sqrt(cp.abs(x)) + cp.exp(-x ** 2))), 4 * n
+    elif c in ("sum_f32", "var_f32", "argmax_f32"):
+        x = gen.normal((n,), 21)
+        f = {"sum_f32": cp.sum, "var_f32": cp.var, "argmax_f32": cp.argmax}[c]
+        fn, nb = (lambda: f(x)), 4 * n
+    elif c in ("sum_axis0_f32", "sum_axis1_f32"):
+        side = int(math.isqrt(n))
+        x = gen.normal((side, side), 21)
+        ax = 0 if c == "sum_axis0_f32" else 1
+        fn, nb = (lambda: cp.sum(x, axis=ax)), 4 * side * side
+    elif c == "cumsum_i32":
+        x = gen.integers((n,), -100, 101, 31)
+        fn, nb = (lambda: cp.cumsum(x)), 12 * n
+    elif c == "cumsum_f32":
+        x = gen.uniform((n,), 0, 1, 32)
+        fn, nb = (lambda: cp.cumsum(x)), 8 * n
+    elif c == "cumsum_axis1_f32":
+        x = gen.normal((max(1, n // 65536), 65536), 33)
+        fn, nb = (lambda: cp.cumsum(x, axis=1)), 8 * x.size
+    elif c in ("matmul_f32", "matmul_f16"):
+        x = gen.normal((n, n), 41) * np.float32(1 / math.sqrt(n))
+        y = gen.normal((n, n), 42) * np.float32(1 / math.sqrt(n))
+        if c == "matmul_f16":
+            x, y = x.astype(np.float16), y.astype(np.float16)
+        x, y = x.copy(), y.copy()
+        fn, nb = (lambda: cp.matmul(x, y)), 2 * n ** 3
+    else:
+        raise SystemExit(f"unknown case {c}; one of {CASES}")
+    ms = _time(cp, fn, iters=max(args.steps, 1), warm=max(args.warmup, 1))
+    unit = "TFLOP/s" if c.startswith("matmul") else "GB/s"
+    val = nb / (ms / 1e3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"case": c, "elements": n, "ms": round(ms, 4), "value": round(val, 2), "unit": unit}))
     return 0
 
 
