@@ -147,6 +147,22 @@ int mmp_reduce_axis(int op, int dtype, const void *x, int64_t outer, int64_t k,
 int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y,
              int64_t outer, int64_t k, int64_t inner, const void *carry_in);
 
+/* Allocation-free form of mmp_scan, for callers that cannot have this
+ * library allocate device memory during a call -- a host framework that owns
+ * nearly all of HBM through its own pool and passes only its input and output
+ * buffers, or code holding that framework's allocator lock.  Same arguments
+ * and results as mmp_scan.  No counterpart in the reference (it has no such
+ * callers).  The look-back state lives in a fixed device array of this
+ * library (about 4 MiB per GPU that loads it, kept until exit), so scans
+ * longer than MMP_NOALLOC_SCAN_TILES tiles of 4096 elements per row-set
+ * (outer * ceil(k / 4096)) are rejected with MMP_E_ARG.  Calls share the
+ * array: calls that may overlap on the GPU race and must be serialised by
+ * the caller.  Requires mmp_init on the device; the first call on a device
+ * looks up the array's address (make it before any stream capture). */
+#define MMP_NOALLOC_SCAN_TILES 209715
+int mmp_scan_noalloc(int op, int dtype, const void *x, int out_dtype, void *y,
+                     int64_t outer, int64_t k, int64_t inner, const void *carry_in);
+
 /* Row-major C[b] = A[b] @ B[b] for b < batch (ndarray.__matmul__,
  * ndarray.py:1398-1450; linalg_top.matmul, linalg_top.py:94-111).
  * Leading dimensions and batch strides are in elements. */

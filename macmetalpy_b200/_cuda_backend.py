@@ -78,6 +78,7 @@ SIGNATURES = {
                           ctypes.POINTER(MmpPartial)]),
     "mmp_reduce_axis": (_int, [_int, _int, _vp, _i64, _i64, _i64, _int, _vp, ctypes.c_double]),
     "mmp_scan": (_int, [_int, _int, _vp, _int, _vp, _i64, _i64, _i64, _vp]),
+    "mmp_scan_noalloc": (_int, [_int, _int, _vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "mmp_gemm": (_int, [_int, _int, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp,
                         _i64, _i64]),
 }

@@ -23,6 +23,8 @@ int sm_count();
 int scratch(size_t bytes, void **ptr, unsigned **tickets);
 // Device-side error word (bounded waits set it instead of hanging).
 int *device_error_word();
+// True once mmp_init has set up the current device (no side effects).
+bool is_ready();
 
 }  // namespace mmp
 

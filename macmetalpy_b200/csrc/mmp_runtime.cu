@@ -168,6 +168,11 @@ int scratch(size_t bytes, void **ptr, unsigned **tickets) {
   return MMP_OK;
 }
 
+bool is_ready() {
+  DevState *s = cur();
+  return s && s->ready;
+}
+
 int *device_error_word() {
   DevState *s = cur();
   if (!s || !s->ready) {

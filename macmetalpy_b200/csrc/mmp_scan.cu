@@ -5,6 +5,8 @@
 #include "mmp_dispatch.h"
 #include "mmp_scan.cuh"
 
+#include <cstdio>
+
 using namespace mmpd;
 
 namespace mmp {
@@ -124,5 +126,114 @@ extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y
                                                                   (long long)k, (long long)inner, carry_in);
   if (op == MMP_S_PROD) return mmp::dispatch_dtype<mmp::ScanRun, 1>(dtype, x, out_dtype, y, (long long)outer,
                                                                    (long long)k, (long long)inner, carry_in);
+  return mmp::set_error(MMP_E_ARG, "unsupported scan op");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free scan.
+//
+// Some callers cannot let this library allocate device memory during a
+// call: a host framework that owns the GPU's memory (it reserves almost all
+// of HBM for its own pool and hands us only its input and output buffers,
+// so a hidden cudaMalloc could fail or fragment its pool), or code that
+// runs while that framework holds its allocator lock, where re-entering an
+// allocator would deadlock.  mmp_scan_noalloc gives them the same scan as
+// mmp_scan with its look-back state in a fixed device array that is part of
+// this library, so the call itself allocates nothing.
+//
+// The array holds the state of at most MMP_NOALLOC_SCAN_TILES tiles of
+// 4096 elements; larger scans are rejected with MMP_E_ARG.  Every GPU that
+// loads the library keeps the array (about 4 MiB) until the process exits.
+// All calls share it: calls that can overlap on the GPU (different streams
+// or devices sharing nothing else) race on it and must be serialised by the
+// caller.  The first call on each device looks up the array's address with
+// cudaGetSymbolAddress; make that first call before any stream capture.
+// The caller must have called mmp_init on the device.
+// ---------------------------------------------------------------------------
+// Look-back state of mmp_scan_noalloc: tile aggregates (8 B each), inclusive
+// prefixes (8 B each), flags (4 B each), then the tile counter.
+static __device__ __align__(256) unsigned char g_noalloc_scan[(size_t)MMP_NOALLOC_SCAN_TILES * 20 + 256];
+
+namespace mmp {
+namespace {
+
+constexpr size_t kNoallocTiles = MMP_NOALLOC_SCAN_TILES;
+
+unsigned char *g_noalloc_addr[64];  // device address of g_noalloc_scan, per device
+
+int noalloc_state(unsigned char **base) {
+  int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
+  if (!g_noalloc_addr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scan);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_scan)");
+    g_noalloc_addr[dev] = (unsigned char *)p;
+  }
+  *base = g_noalloc_addr[dev];
+  return MMP_OK;
+}
+
+template <int PRODI, class T>
+struct ScanNoallocRun {
+  static int run(const void *xv, int out_dt, void *yv, long long outer, long long k, long long inner,
+                 const void *carry) {
+    typedef typename ScanOut<T>::type O;
+    typedef typename ScanTypes<T>::carry_t C;
+    constexpr bool PROD = PRODI != 0;
+    if (out_dt != ScanOut<T>::code)
+      return set_error(MMP_E_ARG, "scan output dtype must be the numpy accumulation type");
+    if (inner > 1 || k < STILE / 4)  // these shapes need no scratch at all
+      return ScanRun<PRODI, T>::run(xv, out_dt, yv, outer, k, inner, carry);
+    const long long tpr = (k + STILE - 1) / STILE;
+    const long long total = outer * tpr;
+    if (total > (long long)kNoallocTiles) {
+      char msg[200];
+      snprintf(msg, sizeof msg,
+               "mmp_scan_noalloc: %lld tiles of %d elements exceed the fixed scratch of %zu tiles; "
+               "use mmp_scan",
+               total, STILE, kNoallocTiles);
+      return set_error(MMP_E_ARG, msg);
+    }
+    unsigned char *base = nullptr;
+    int rc = noalloc_state(&base);
+    if (rc) return rc;
+    cudaStream_t st = stream();
+    C *agg = (C *)base;
+    C *incl = (C *)(base + kNoallocTiles * 8);
+    unsigned *flags = (unsigned *)(base + kNoallocTiles * 16);
+    unsigned *counter = (unsigned *)(base + kNoallocTiles * 20);
+    // the previous call's flags and counter must not be read as this call's
+    MMP_CUDA_TRY(cudaMemsetAsync(flags, 0, (size_t)total * sizeof(unsigned), st));
+    MMP_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(unsigned), st));
+    TileState<C> ts;
+    ts.agg = agg;
+    ts.incl = incl;
+    ts.flag = flags;
+    const T *x = (const T *)xv;
+    O *y = (O *)yv;
+    int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
+    scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, 0, st>>>(
+        x, y, outer, k, tpr, total, ts, counter, 1u, device_error_word(), (const C *)carry, vec_ok);
+    MMP_LAUNCH_CHECK("scan_tiles_kernel (noalloc)");
+    return MMP_OK;
+  }
+};
+
+}  // namespace
+}  // namespace mmp
+
+extern "C" int mmp_scan_noalloc(int op, int dtype, const void *x, int out_dtype, void *y, int64_t outer,
+                                int64_t k, int64_t inner, const void *carry_in) {
+  if (outer < 0 || k < 0 || inner < 0) return mmp::set_error(MMP_E_ARG, "negative extent");
+  if (outer == 0 || k == 0 || inner == 0) return MMP_OK;
+  if (!x || !y) return mmp::set_error(MMP_E_ARG, "null pointer");
+  if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "mmp_scan_noalloc: call mmp_init on this device first");
+  if (op == MMP_S_SUM)
+    return mmp::dispatch_dtype<mmp::ScanNoallocRun, 0>(dtype, x, out_dtype, y, (long long)outer, (long long)k,
+                                                      (long long)inner, carry_in);
+  if (op == MMP_S_PROD)
+    return mmp::dispatch_dtype<mmp::ScanNoallocRun, 1>(dtype, x, out_dtype, y, (long long)outer, (long long)k,
+                                                      (long long)inner, carry_in);
   return mmp::set_error(MMP_E_ARG, "unsupported scan op");
 }
