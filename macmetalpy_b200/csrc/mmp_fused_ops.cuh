@@ -205,7 +205,8 @@ __device__ __forceinline__ I i_floor_divide(I a, I b) {
   if (mmpd::IsSigned<I>::value) {
     if (b == I(-1)) return (I)(I(0) - a);  // wraps INT_MIN to INT_MIN
     I q = a / b;
-    if ((a % b != I(0)) && ((a < I(0)) != (b < I(0)))) q -= I(1);
+    I r = (I)(a - q * b);  // one division: the remainder from the quotient
+    if (r != I(0) && ((r < I(0)) != (b < I(0)))) q -= I(1);
     return q;
   }
   return a / b;
@@ -273,12 +274,19 @@ template <class R>
 __device__ __forceinline__ R fmin_(R a, R b) { return (a <= b || isnan_(b)) ? a : b; }
 
 // ---- logaddexp (numpy npy_logaddexp / npy_logaddexp2)
+// log1p(t) for t = exp(-|x - y|) in (0, 1].  Below 2^-12 the series
+// t - t^2/2 is exact to t^3/3 < t * 2^-24 / 3 (under a sixth of an ulp of
+// t), so the library log1p is only needed for |x - y| < 12 ln 2.
+template <class R>
+__device__ __forceinline__ R log1p_of_exp(R t) {
+  return (t < R(2.44140625e-4)) ? (t - R(0.5) * t * t) : m_log1p(t);
+}
 template <class R>
 __device__ __forceinline__ R logaddexp(R x, R y) {
   if (x == y) return x + Consts<R>::loge2();  // equal infinities without nan
   R tmp = x - y;
-  if (tmp > R(0)) return x + m_log1p(m_exp(-tmp));
-  if (tmp <= R(0)) return y + m_log1p(m_exp(tmp));
+  if (tmp > R(0)) return x + log1p_of_exp(m_exp(-tmp));
+  if (tmp <= R(0)) return y + log1p_of_exp(m_exp(tmp));
   return tmp;  // nan
 }
 template <class R>

@@ -326,11 +326,16 @@ struct ArgOp {
     }
     return (b.i < a.i) ? b : a;
   }
+  // One accumulator sees its indices in increasing order in every kernel
+  // here, so a strict comparison keeps the first occurrence, and a NaN,
+  // once held, is never replaced (the first NaN wins).
   __device__ static void one(Acc &a, T v, long long idx) {
-    Acc b;
-    b.v = ar(v);
-    b.i = idx;
-    a = pick(a, b);
+    const V_ x = ar(v);
+    const bool take = (a.i < 0) || (!isnan_(a.v) && (isnan_(x) || (MAX ? (x > a.v) : (x < a.v))));
+    if (take) {
+      a.v = x;
+      a.i = idx;
+    }
   }
   template <int V>
   __device__ static void vec(Acc &a, const T (&v)[V], long long base) {
@@ -654,7 +659,26 @@ __device__ __forceinline__ void reduce_cols_body(const L &ld, long long outer, l
 #pragma unroll
   for (int j = 0; j < CV; ++j) acc0[j] = acc[j];
   const bool full = (c0 + CV <= inner);
-  for (long long r = r0 + ty; r < r1; r += 8) {
+  long long r = r0 + ty;
+  if (CV > 1 && full) {
+    // four rows of loads in flight per thread, consumed in row order
+    for (; r + 24 < r1; r += 32) {
+      T v0[CV], v1[CV], v2[CV], v3[CV];
+      const long long off = obase + r * inner + c0;
+      ld.template vec<CV>(off, v0);
+      ld.template vec<CV>(off + 8 * inner, v1);
+      ld.template vec<CV>(off + 16 * inner, v2);
+      ld.template vec<CV>(off + 24 * inner, v3);
+#pragma unroll
+      for (int j = 0; j < CV; ++j) {
+        Op::one(acc[j], v0[j], r);
+        Op::one(acc[j], v1[j], r + 8);
+        Op::one(acc[j], v2[j], r + 16);
+        Op::one(acc[j], v3[j], r + 24);
+      }
+    }
+  }
+  for (; r < r1; r += 8) {
     long long off = obase + r * inner + c0;
     if (CV > 1 && full) {
       T v[CV];

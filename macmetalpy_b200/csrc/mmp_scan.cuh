@@ -87,6 +87,16 @@ __device__ __forceinline__ unsigned wait_flag(const unsigned *flag, long long t,
   return 0;
 }
 
+// Shared-memory index with one padding element per 128 bytes.
+template <class E>
+__device__ __forceinline__ int spad(int i) {
+  return i + i / (int)(128 / sizeof(E));
+}
+template <class E>
+struct StageBytes {
+  static constexpr int value = (STILE + STILE / (128 / sizeof(E))) * sizeof(E);
+};
+
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tiles_per_row,
@@ -98,6 +108,8 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
   __shared__ long long s_tile;
   __shared__ A s_warp[SBLOCK / 32];
   __shared__ C s_excl;
+  constexpr int STAGE = StageBytes<T>::value > StageBytes<O>::value ? StageBytes<T>::value : StageBytes<O>::value;
+  __shared__ __align__(16) unsigned char s_stage[STAGE];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   if (tid == 0) s_tile = (long long)atomicAdd(tile_counter, 1u);
   __syncthreads();
@@ -111,17 +123,25 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
   if (count > STILE) count = STILE;
   const unsigned ep = epoch & 0x3fffffffu;
 
-  // ---- load SITEMS consecutive elements per thread and scan them
+  // ---- load the tile: coalesced 16-byte vectors into shared memory (one
+  // padding element per 128 bytes keeps both access patterns free of bank
+  // conflicts), then SITEMS consecutive elements per thread
   A v[SITEMS];
   const long long my0 = (long long)tid * SITEMS;
-  if (vec_ok && count == STILE) {
+  const bool full_vec = vec_ok && count == STILE;
+  if (full_vec) {
+    T *smT = reinterpret_cast<T *>(s_stage);
     constexpr int VE = (16 / sizeof(T)) < SITEMS ? (16 / sizeof(T)) : SITEMS;
 #pragma unroll
     for (int q = 0; q < SITEMS / VE; ++q) {
-      Vec<T, VE> t = ldvec_stream<T, VE>(x + start + my0 + q * VE);
+      const int i0 = (q * SBLOCK + tid) * VE;
+      Vec<T, VE> t = ldvec_stream<T, VE>(x + start + i0);
 #pragma unroll
-      for (int e = 0; e < VE; ++e) v[q * VE + e] = to_local<A, T>(t.v[e]);
+      for (int e = 0; e < VE; ++e) smT[spad<T>(i0 + e)] = t.v[e];
     }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) v[e] = to_local<A, T>(smT[spad<T>(tid * SITEMS + e)]);
   } else {
 #pragma unroll
     for (int e = 0; e < SITEMS; ++e) {
@@ -223,14 +243,21 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     A loc = Op::op(thread_excl, v[e]);
     res[e] = cvt<O>(Op::op(excl, (C)loc));
   }
-  if (vec_ok && count == STILE) {
+  if (full_vec) {
+    // stage the outputs through shared memory, write 16-byte vectors
+    O *smO = reinterpret_cast<O *>(s_stage);
+    __syncthreads();  // every thread has finished reading its inputs
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) smO[spad<O>(tid * SITEMS + e)] = res[e];
+    __syncthreads();
     constexpr int VO = (16 / sizeof(O)) < SITEMS ? (16 / sizeof(O)) : SITEMS;
 #pragma unroll
     for (int q = 0; q < SITEMS / VO; ++q) {
+      const int i0 = (q * SBLOCK + tid) * VO;
       Vec<O, VO> t;
 #pragma unroll
-      for (int e = 0; e < VO; ++e) t.v[e] = res[q * VO + e];
-      stvec_stream<O, VO>(y + start + my0 + q * VO, t);
+      for (int e = 0; e < VO; ++e) t.v[e] = smO[spad<O>(i0 + e)];
+      stvec_stream<O, VO>(y + start + i0, t);
     }
   } else {
 #pragma unroll
