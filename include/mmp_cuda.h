@@ -122,6 +122,9 @@ int mmp_compile(const char *source, const char *name, const char *options,
                 void **func, char *log, size_t log_size);
 int mmp_launch(void *func, const unsigned grid[3], const unsigned block[3],
                unsigned shared_bytes, void **args);
+/* Blocks of `block_threads` threads that fit on one SM at once (grid sizing
+ * for the compiled function; runFunction picks its own in the reference). */
+int mmp_occupancy(void *func, int block_threads, unsigned shared_bytes, int *blocks_per_sm);
 
 /* ---- typed hot-path kernels */
 

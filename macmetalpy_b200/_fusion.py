@@ -252,7 +252,7 @@ def _binary_expr(op: str, dt, a: str, b: str) -> str:
     if op == "floor_divide_op":
         if isbool:
             return f"({a} && {b})"
-        return f"mmpf::floor_divide_f<{R}>({a}, {b})" if f else f"mmpf::i_floor_divide<{R}>({a}, {b})"
+        return f"mmpf::floor_divide_f<{R}>({a}, {b})" if f else f"mmpf::floor_divide_i<{R}>({a}, {b})"
     if op == "mod_op":  # the reference's composite a - floor_divide(a, b) * b
         if isbool:
             return f"(({a}) && !({b}))"
@@ -558,33 +558,36 @@ def _emit_loader(plan: _Plan) -> tuple[str, list[str]]:
     op_scalar = offsets_code("i", strided_in)
 
     V = plan.vec
-    vec_pre = []
+    raw_members, load_lines, apply_args = [], [], []
     for k, kd in enumerate(plan.kinds):
         t = _ct(plan.inputs[k]._dtype)
-        if kd == "ct":
-            vec_pre.append(f"    const mmpd::Vec<{t}, V> v{k} = mmpd::ldvec<{t}, V>(in{k} + i);")
-        elif kd == "bc":
-            vec_pre.append(f"    const {t} b{k} = in{k}[0];")
-        elif kd == "sv":
-            vec_pre.append(f"    const mmpd::Vec<{t}, V> v{k} = mmpd::ldvec<{t}, V>(in{k} + o{k});")
-        elif kd == "sb":
-            vec_pre.append(f"    const {t} b{k} = in{k}[o{k}];")
-    vec_args = []
-    for k, kd in enumerate(plan.kinds):
         if kd in ("ct", "sv"):
-            vec_args.append(f"v{k}.v[j]")
+            raw_members.append(f"    mmpd::Vec<{t}, V> v{k};")
+            src_ = f"in{k} + i" if kd == "ct" else f"in{k} + o{k}"
+            load_lines.append(f"    r.v{k} = mmpd::ldvec<{t}, V>({src_});")
+            apply_args.append(f"r.v{k}.v[j]")
         elif kd in ("bc", "sb"):
-            vec_args.append(f"b{k}")
-        elif kd == "sg":
-            vec_args.append(f"in{k}[o{k} + ({I})j * st{k}[{nd - 1}]]")
-        else:  # ctu never reaches the vector path
-            vec_args.append(f"in{k}[i + j]")
+            raw_members.append(f"    {t} b{k};")
+            load_lines.append(f"    r.b{k} = in{k}[{'0' if kd == 'bc' else f'o{k}'}];")
+            apply_args.append(f"r.b{k}")
+        else:  # sg (gather) / ctu (unaligned contiguous)
+            raw_members.append(f"    {t} g{k}[V];")
+            if kd == "sg":
+                load_lines.append(f"#pragma unroll\n    for (int j = 0; j < V; ++j) r.g{k}[j] = in{k}[o{k} + ({I})j * st{k}[{nd - 1}]];")
+            else:
+                load_lines.append(f"#pragma unroll\n    for (int j = 0; j < V; ++j) r.g{k}[j] = in{k}[i + j];")
+            apply_args.append(f"r.g{k}[j]")
     op_vec = offsets_code("i", strided_in)
+    raw_body = "\n".join(raw_members) if raw_members else "    int unused;"
 
     src = f"""
 struct Loader {{
   typedef {out_t} value_type;
 {chr(10).join(members)}
+  template <int V>
+  struct Raw {{
+{raw_body}
+  }};
   __device__ __forceinline__ {out_t} eval({args}) const {{
 {body}
     return {root};
@@ -593,12 +596,23 @@ struct Loader {{
 {op_scalar}
     return eval({", ".join(scalar_loads)});
   }}
+  // raw loads of V elements at i (no arithmetic, so several vectors of
+  // loads can be in flight before any evaluation)
+  template <int V>
+  __device__ __forceinline__ void load(long long i, Raw<V> &r) const {{
+{op_vec}
+{chr(10).join(load_lines)}
+  }}
+  template <int V>
+  __device__ __forceinline__ void apply(const Raw<V> &r, {out_t} (&out)[V]) const {{
+#pragma unroll
+    for (int j = 0; j < V; ++j) out[j] = eval({", ".join(apply_args)});
+  }}
   template <int V>
   __device__ __forceinline__ void vec(long long i, {out_t} (&out)[V]) const {{
-{op_vec}
-{chr(10).join(vec_pre)}
-#pragma unroll
-    for (int j = 0; j < V; ++j) out[j] = eval({", ".join(vec_args)});
+    Raw<V> r;
+    load<V>(i, r);
+    apply<V>(r, out);
   }}
 }};
 """
@@ -653,16 +667,28 @@ def _ew_source(plan: _Plan, out_strided: bool) -> str:
     else:
         body = f"""  if (L.aligned) {{
     const long long nv = n / {V};
-    for (long long v = t; v < nv; v += 2 * nth) {{
-      {out_t} r0[{V}], r1[{V}];
-      const long long v1 = v + nth;
-      L.vec<{V}>(v * {V}, r0);
-      if (v1 < nv) L.vec<{V}>(v1 * {V}, r1);
-      mmpd::Vec<{out_t}, {V}> w0, w1;
-#pragma unroll
-      for (int j = 0; j < {V}; ++j) {{ w0.v[j] = r0[j]; w1.v[j] = r1[j]; }}
+    long long v = t;
+    // four vectors per thread per iteration: all loads first, then math
+    for (; v + 3 * nth < nv; v += 4 * nth) {{
+      Loader::Raw<{V}> r0, r1, r2, r3;
+      L.load<{V}>(v * {V}, r0);
+      L.load<{V}>((v + nth) * {V}, r1);
+      L.load<{V}>((v + 2 * nth) * {V}, r2);
+      L.load<{V}>((v + 3 * nth) * {V}, r3);
+      mmpd::Vec<{out_t}, {V}> w0, w1, w2, w3;
+      L.apply<{V}>(r0, w0.v);
+      L.apply<{V}>(r1, w1.v);
+      L.apply<{V}>(r2, w2.v);
+      L.apply<{V}>(r3, w3.v);
       mmpd::stvec<{out_t}, {V}>(out + v * {V}, w0);
-      if (v1 < nv) mmpd::stvec<{out_t}, {V}>(out + v1 * {V}, w1);
+      mmpd::stvec<{out_t}, {V}>(out + (v + nth) * {V}, w1);
+      mmpd::stvec<{out_t}, {V}>(out + (v + 2 * nth) * {V}, w2);
+      mmpd::stvec<{out_t}, {V}>(out + (v + 3 * nth) * {V}, w3);
+    }}
+    for (; v < nv; v += nth) {{
+      mmpd::Vec<{out_t}, {V}> w0;
+      L.vec<{V}>(v * {V}, w0.v);
+      mmpd::stvec<{out_t}, {V}>(out + v * {V}, w0);
     }}
     for (long long i = nv * {V} + t; i < n; i += nth) out[i] = L(i);
   }} else {{
@@ -797,6 +823,20 @@ def _launch(fn, grid, args, block=_BLOCK):
     _cb.check(_cb.lib.mmp_launch(ctypes.c_void_p(fn), g, b, 0, arr), "fused kernel launch")
 
 
+_occ: dict = {}
+
+
+def _resident_blocks(fn) -> int:
+    """Blocks of _BLOCK threads that fit on the whole GPU at once."""
+    r = _occ.get(fn)
+    if r is None:
+        per_sm = ctypes.c_int(0)
+        _cb.check(_cb.lib.mmp_occupancy(ctypes.c_void_p(fn), _BLOCK, 0, ctypes.byref(per_sm)), "occupancy")
+        r = max(1, per_sm.value) * _cb.CudaBackend().sm_count
+        _occ[fn] = r
+    return r
+
+
 def _vec_width(dtypes) -> int:
     mx = max((np.dtype(d).itemsize for d in dtypes), default=4)
     return 8 if mx <= 2 else 4
@@ -829,9 +869,8 @@ def run_elementwise(node, out_ptr: int, out_shape, out_strides=None) -> None:
     args = _loader_args(plan) + [ctypes.c_void_p(out_ptr), ctypes.c_longlong(plan.n)]
     if out_strided:
         args += [ctypes.c_longlong(int(s)) for s in out_strides]
-    sms = _cb.CudaBackend().sm_count
-    per = _BLOCK * V * 2
-    grid = max(1, min((plan.n + per - 1) // per, sms * 8))
+    per = _BLOCK * V * 4
+    grid = max(1, min((plan.n + per - 1) // per, _resident_blocks(fn)))
     _launch(fn, (grid,), args)
 
 
@@ -878,7 +917,7 @@ def run_reduce(node, shape, opc: int, out_ptr: int, out_dt, ddof: float = 0.0,
 
         fn = _get(key, src, "mmp_fused_reduce")
         per = _BLOCK * V * 4
-        grid = max(1, min((n + per - 1) // per, be.sm_count * 4))
+        grid = max(1, min((n + per - 1) // per, _resident_blocks(fn)))
         acc_bytes = 64 * grid
         scr = ctypes.c_void_p()
         tick = ctypes.c_void_p()

@@ -212,6 +212,32 @@ __device__ __forceinline__ I i_floor_divide(I a, I b) {
   return a / b;
 }
 
+// int32 floor division for |a| < 2^21, |b| < 2^24 through float: both
+// convert exactly, |a/b| < 2^21 so the 2-ulp approximate quotient is within
+// 1/2 of a/b, its truncation q0 is within {-1, 0, +1, +2} of the floor, and
+// the exact integer remainder a - q*b steers q onto the floor quotient in
+// at most two steps.  Everything else takes the integer division.
+__device__ __forceinline__ int i32_floor_divide(int a, int b) {
+  const unsigned ua = (unsigned)(a < 0 ? -a : a), ub = (unsigned)(b < 0 ? -b : b);
+  if (b != 0 && ua < (1u << 21) && ub < (1u << 24)) {
+    int q = (int)truncf(__fdividef((float)a, (float)b));
+    int r = a - q * b;
+    if (b > 0) {
+      if (r < 0) { q -= 1; r += b; }
+      if (r < 0) { q -= 1; r += b; }
+      if (r >= b) { q += 1; }
+    } else {
+      if (r > 0) { q -= 1; r += b; }
+      if (r > 0) { q -= 1; r += b; }
+      if (r <= b) { q += 1; }
+    }
+    return q;
+  }
+  return i_floor_divide<int>(a, b);
+}
+template <class I> __device__ __forceinline__ I floor_divide_i(I a, I b) { return i_floor_divide<I>(a, b); }
+template <> __device__ __forceinline__ int floor_divide_i<int>(int a, int b) { return i32_floor_divide(a, b); }
+
 template <class I>
 __device__ __forceinline__ I i_remainder(I a, I b) {
   if (b == I(0)) return I(0);
@@ -236,7 +262,7 @@ __device__ __forceinline__ R ref_mod_f(R a, R b) {
 }
 template <class I>
 __device__ __forceinline__ I ref_mod_i(I a, I b) {
-  I fd = i_floor_divide<I>(a, b);
+  I fd = floor_divide_i<I>(a, b);
   I t = (I)(fd * b);
   return (I)(a - t);
 }

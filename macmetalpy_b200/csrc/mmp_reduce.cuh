@@ -452,10 +452,21 @@ struct ContigLoader {
   int aligned;
   __device__ __forceinline__ T operator()(long long i) const { return x[i]; }
   template <int V>
-  __device__ __forceinline__ void vec(long long i, T (&v)[V]) const {
-    Vec<T, V> t = ldvec_stream<T, V>(x + i);
+  using Raw = Vec<T, V>;
+  template <int V>
+  __device__ __forceinline__ void load(long long i, Raw<V> &r) const {
+    r = ldvec_stream<T, V>(x + i);
+  }
+  template <int V>
+  __device__ __forceinline__ void apply(const Raw<V> &r, T (&v)[V]) const {
 #pragma unroll
-    for (int j = 0; j < V; ++j) v[j] = t.v[j];
+    for (int j = 0; j < V; ++j) v[j] = r.v[j];
+  }
+  template <int V>
+  __device__ __forceinline__ void vec(long long i, T (&v)[V]) const {
+    Raw<V> r;
+    load<V>(i, r);
+    apply<V>(r, v);
   }
 };
 
@@ -509,11 +520,16 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
     long long nv = n / V;
     long long i = tid;
     for (; i + 3 * nth < nv; i += 4 * nth) {
+      typename L::template Raw<V> r0, r1, r2, r3;
+      ld.template load<V>(i * V, r0);
+      ld.template load<V>((i + nth) * V, r1);
+      ld.template load<V>((i + 2 * nth) * V, r2);
+      ld.template load<V>((i + 3 * nth) * V, r3);
       T a0[V], a1[V], a2[V], a3[V];
-      ld.template vec<V>(i * V, a0);
-      ld.template vec<V>((i + nth) * V, a1);
-      ld.template vec<V>((i + 2 * nth) * V, a2);
-      ld.template vec<V>((i + 3 * nth) * V, a3);
+      ld.template apply<V>(r0, a0);
+      ld.template apply<V>(r1, a1);
+      ld.template apply<V>(r2, a2);
+      ld.template apply<V>(r3, a3);
       Op::template vec<V>(acc, a0, i * V);
       Op::template vec<V>(acc, a1, (i + nth) * V);
       Op::template vec<V>(acc, a2, (i + 2 * nth) * V);

@@ -64,6 +64,7 @@ typedef CUresult (*PFN_Launch)(CUfunction, unsigned, unsigned, unsigned,
                                CUstream, void **, void **);
 typedef CUresult (*PFN_FuncSetAttr)(CUfunction, CUfunction_attribute, int);
 typedef CUresult (*PFN_GetErrorString)(CUresult, const char **);
+typedef CUresult (*PFN_Occupancy)(int *, CUfunction, int, size_t);
 
 struct Driver {
   PFN_LoadData load_data = nullptr;
@@ -71,6 +72,7 @@ struct Driver {
   PFN_Launch launch = nullptr;
   PFN_FuncSetAttr set_attr = nullptr;
   PFN_GetErrorString err_string = nullptr;
+  PFN_Occupancy occupancy = nullptr;
   bool ok = false;
 };
 Driver g_drv;
@@ -122,6 +124,7 @@ static int load_driver() {
   g_drv.launch = (PFN_Launch)driver_fn("cuLaunchKernel");
   g_drv.set_attr = (PFN_FuncSetAttr)driver_fn("cuFuncSetAttribute");
   g_drv.err_string = (PFN_GetErrorString)driver_fn("cuGetErrorString");
+  g_drv.occupancy = (PFN_Occupancy)driver_fn("cuOccupancyMaxActiveBlocksPerMultiprocessor");
   if (!g_drv.load_data || !g_drv.get_function || !g_drv.launch || !g_drv.set_attr)
     return set_error(MMP_E_CUDA, "CUDA driver entry points unavailable");
   g_drv.ok = true;
@@ -481,6 +484,16 @@ int mmp_launch(void *func, const unsigned grid[3], const unsigned block[3],
   CUresult r = g_drv.launch((CUfunction)func, grid[0], grid[1], grid[2], block[0], block[1],
                             block[2], shared_bytes, (CUstream)cur()->stream, args, nullptr);
   if (r != CUDA_SUCCESS) return driver_error(r, "cuLaunchKernel");
+  return MMP_OK;
+}
+
+int mmp_occupancy(void *func, int block_threads, unsigned shared_bytes, int *blocks_per_sm) {
+  if (!func || !blocks_per_sm || block_threads <= 0) return set_error(MMP_E_ARG, "bad argument to mmp_occupancy");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  if (!g_drv.occupancy) return set_error(MMP_E_CUDA, "occupancy query unavailable");
+  CUresult r = g_drv.occupancy(blocks_per_sm, (CUfunction)func, block_threads, shared_bytes);
+  if (r != CUDA_SUCCESS) return driver_error(r, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
   return MMP_OK;
 }
 

@@ -22,8 +22,7 @@ struct ScanState {
 };
 ScanState g_scan[64];
 
-int scan_state(long long tiles, void **agg, void **incl, unsigned **flags, unsigned **counter,
-               unsigned *epoch) {
+int scan_state(long long tiles, void **desc, unsigned **counter, unsigned *epoch) {
   int dev = current_device();
   ScanState &s = g_scan[dev];
   cudaStream_t st = stream();
@@ -32,7 +31,7 @@ int scan_state(long long tiles, void **agg, void **incl, unsigned **flags, unsig
     if (s.buf) MMP_CUDA_TRY(cudaFreeAsync(s.buf, st));
     s.buf = nullptr;
     s.tiles = 0;
-    size_t bytes = want * (8 + 8 + 4) + 256;
+    size_t bytes = want * 16 + 256;
     MMP_CUDA_TRY(cudaMallocAsync(&s.buf, bytes, st));
     MMP_CUDA_TRY(cudaMemsetAsync(s.buf, 0, bytes, st));
     s.tiles = want;
@@ -40,14 +39,12 @@ int scan_state(long long tiles, void **agg, void **incl, unsigned **flags, unsig
   }
   s.epoch = (s.epoch + 1) & 0x3fffffffu;
   if (s.epoch == 0) {  // wrapped: clear stale flags once
-    MMP_CUDA_TRY(cudaMemsetAsync(s.buf, 0, s.tiles * 20 + 256, st));
+    MMP_CUDA_TRY(cudaMemsetAsync(s.buf, 0, s.tiles * 16 + 256, st));
     s.epoch = 1;
   }
   char *b = (char *)s.buf;
-  *agg = b;
-  *incl = b + s.tiles * 8;
-  *flags = (unsigned *)(b + s.tiles * 16);
-  *counter = (unsigned *)(b + s.tiles * 20);
+  *desc = b;
+  *counter = (unsigned *)(b + s.tiles * 16);
   *epoch = s.epoch;
   return MMP_OK;
 }
@@ -98,15 +95,13 @@ struct ScanRun {
     long long tpr = (k + STILE - 1) / STILE;
     long long total = rows * tpr;
     if (total > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
-    void *agg, *incl;
-    unsigned *flags, *counter, epoch;
-    int rc = scan_state(total, &agg, &incl, &flags, &counter, &epoch);
+    void *desc;
+    unsigned *counter, epoch;
+    int rc = scan_state(total, &desc, &counter, &epoch);
     if (rc) return rc;
     typedef typename ScanTypes<T>::carry_t C;
     TileState<C> ts;
-    ts.agg = (C *)agg;
-    ts.incl = (C *)incl;
-    ts.flag = flags;
+    ts.desc = (TileDesc<C> *)desc;
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
     scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, 0, st>>>(
         x, y, rows, k, tpr, total, ts, counter, epoch, device_error_word(), cin, vec_ok);
@@ -150,8 +145,8 @@ extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y
 // cudaGetSymbolAddress; make that first call before any stream capture.
 // The caller must have called mmp_init on the device.
 // ---------------------------------------------------------------------------
-// Look-back state of mmp_scan_noalloc: tile aggregates (8 B each), inclusive
-// prefixes (8 B each), flags (4 B each), then the tile counter.
+// Look-back state of mmp_scan_noalloc: 16-byte tile descriptors, then the
+// tile counter.
 static __device__ __align__(256) unsigned char g_noalloc_scan[(size_t)MMP_NOALLOC_SCAN_TILES * 20 + 256];
 
 namespace mmp {
@@ -199,17 +194,13 @@ struct ScanNoallocRun {
     int rc = noalloc_state(&base);
     if (rc) return rc;
     cudaStream_t st = stream();
-    C *agg = (C *)base;
-    C *incl = (C *)(base + kNoallocTiles * 8);
-    unsigned *flags = (unsigned *)(base + kNoallocTiles * 16);
-    unsigned *counter = (unsigned *)(base + kNoallocTiles * 20);
-    // the previous call's flags and counter must not be read as this call's
-    MMP_CUDA_TRY(cudaMemsetAsync(flags, 0, (size_t)total * sizeof(unsigned), st));
+    TileDesc<C> *desc = (TileDesc<C> *)base;
+    unsigned *counter = (unsigned *)(base + kNoallocTiles * 16);
+    // the previous call's descriptors and counter must not be read as this call's
+    MMP_CUDA_TRY(cudaMemsetAsync(desc, 0, (size_t)total * sizeof(TileDesc<C>), st));
     MMP_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(unsigned), st));
     TileState<C> ts;
-    ts.agg = agg;
-    ts.incl = incl;
-    ts.flag = flags;
+    ts.desc = desc;
     const T *x = (const T *)xv;
     O *y = (O *)yv;
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);

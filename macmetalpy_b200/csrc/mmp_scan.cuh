@@ -54,34 +54,49 @@ __device__ __forceinline__ float to_local<float, __half>(__half v) { return __ha
 template <>
 __device__ __forceinline__ long long to_local<long long, bool>(bool v) { return v ? 1 : 0; }
 
-// Per-launch tile state; flag = (epoch << 2) | state, state 1 = aggregate,
-// 2 = inclusive prefix.  A flag from an older launch reads as "not ready",
-// so the state never needs clearing between launches.
+// Per-tile state: the value and its flag in one 16-byte descriptor, written
+// and read with single 16-byte accesses, so a reader never sees a flag
+// without its value and no memory fence is needed between them.  flag =
+// (epoch << 2) | state, state 1 = aggregate, 2 = inclusive prefix; a flag
+// from an older launch reads as "not ready", so descriptors are never
+// cleared between launches.
+template <class C>
+struct __align__(16) TileDesc {
+  C value;
+  unsigned long long flag;
+};
 template <class C>
 struct TileState {
-  C *agg;
-  C *incl;
-  unsigned *flag;
+  TileDesc<C> *desc;
 };
 
-__device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
-  return *reinterpret_cast<const volatile unsigned *>(p);
+template <class C>
+__device__ __forceinline__ void desc_store(TileDesc<C> *d, C v, unsigned long long flag) {
+  unsigned long long bits;
+  memcpy(&bits, &v, 8);
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(d), "l"(bits), "l"(flag) : "memory");
 }
 template <class C>
-__device__ __forceinline__ C ld_volatile_c(const C *p) {
-  return *reinterpret_cast<const volatile C *>(p);
+__device__ __forceinline__ void desc_load(const TileDesc<C> *d, C &v, unsigned long long &flag) {
+  unsigned long long bits;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(bits), "=l"(flag) : "l"(d) : "memory");
+  memcpy(&v, &bits, 8);
 }
 
-// Wait for the state of tile `t` in this launch; bounded.
-__device__ __forceinline__ unsigned wait_flag(const unsigned *flag, long long t, unsigned epoch,
-                                              int *err) {
-  unsigned f = 0;
-  unsigned ns = 8;
+// Wait for tile `t`'s descriptor of this launch; spins, then backs off;
+// bounded.  Returns the state (1 or 2) and the value, or 0 on time-out.
+template <class C>
+__device__ __forceinline__ unsigned wait_desc(const TileDesc<C> *desc, long long t, unsigned epoch, int *err,
+                                              C &val) {
+  unsigned long long f = 0;
+  unsigned ns = 32;
   for (long long it = 0; it < (1ll << 22); ++it) {
-    f = ld_volatile(flag + t);
-    if ((f >> 2) == (epoch & 0x3fffffffu) && (f & 3u)) return f & 3u;
-    __nanosleep(ns);
-    if (ns < 256) ns <<= 1;
+    desc_load(desc + t, val, f);
+    if ((unsigned)(f >> 2) == (epoch & 0x3fffffffu) && (f & 3ull)) return (unsigned)(f & 3ull);
+    if (it >= 64) {
+      __nanosleep(ns);
+      if (ns < 512) ns <<= 1;
+    }
   }
   atomicExch(err, 2);  // look-back wait ran out
   return 0;
@@ -185,19 +200,12 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
   // ---- decoupled look-back over earlier tiles of the same row
   if (w == 0) {
     C excl = Op::template id<C>();
+    const unsigned long long ep2 = (unsigned long long)ep << 2;
     if (j == 0) {
       if (carry_in && rows == 1) excl = (C)(*carry_in);
-      if (lane == 0) {
-        st.incl[tile] = Op::op(excl, (C)tile_agg);
-        __threadfence();
-        atomicExch(st.flag + tile, (ep << 2) | 2u);
-      }
+      if (lane == 0) desc_store(st.desc + tile, Op::op(excl, (C)tile_agg), ep2 | 2ull);
     } else {
-      if (lane == 0) {
-        st.agg[tile] = (C)tile_agg;
-        __threadfence();
-        atomicExch(st.flag + tile, (ep << 2) | 1u);
-      }
+      if (lane == 0) desc_store(st.desc + tile, (C)tile_agg, ep2 | 1ull);
       const long long row_first = row * tiles_per_row;
       long long look = tile - 1;  // highest tile id still to fold in
       bool done = false;
@@ -206,30 +214,23 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
         unsigned f;
         C val = Op::template id<C>();
         if (t >= row_first) {
-          f = wait_flag(st.flag, t, ep, err);
-          __threadfence();
-          if (f == 2) val = ld_volatile_c(st.incl + t);
-          else if (f == 1) val = ld_volatile_c(st.agg + t);
+          f = wait_desc(st.desc, t, ep, err, val);
+          if (f == 0) val = Op::template id<C>();
         } else {
           f = 2;  // before the row start: acts as an inclusive prefix of identity
           if (carry_in && rows == 1 && t == row_first - 1) val = (C)(*carry_in);
         }
         unsigned incl_mask = __ballot_sync(0xffffffffu, f == 2);
         int stop = incl_mask ? (__ffs(incl_mask) - 1) : 31;
-        // fold lanes 0..stop (closest tile first) -- order: tile-1, tile-2, ...
+        // fold lanes 0..stop (tile-1, tile-2, ..., the nearest inclusive prefix)
         C part = (lane <= stop) ? val : Op::template id<C>();
-        // combine with the lane order reversed so the fold is deterministic
 #pragma unroll
         for (int d = 16; d >= 1; d >>= 1) part = Op::op(part, __shfl_down_sync(0xffffffffu, part, d));
         excl = Op::op(excl, part);
         if (incl_mask) done = true;
         else look -= 32;
       }
-      if (lane == 0) {
-        st.incl[tile] = Op::op(excl, (C)tile_agg);
-        __threadfence();
-        atomicExch(st.flag + tile, (ep << 2) | 2u);
-      }
+      if (lane == 0) desc_store(st.desc + tile, Op::op(excl, (C)tile_agg), ep2 | 2ull);
     }
     if (lane == 0) s_excl = excl;
   }

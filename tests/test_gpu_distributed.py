@@ -1,0 +1,103 @@
+"""Block-distributed arrays on 2 GPUs over NCCL, against the oracle on the
+whole array: sum / mean / var / argmax / argmin / max / nansum / nanmean
+(all-reduce and all-gather merges), 1-D cumsum with carries (int32 exact,
+float32 within 1e-4), axis-1 reductions and scans (shard-local), matmul
+with B broadcast from rank 0.  Needs two visible GPUs; skipped otherwise.
+Ranks are child processes with a short process-group timeout; NVLS is off
+(plain NCCL rings), as this test only checks results."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        from macmetalpy_b200 import distributed as D
+        from macmetalpy_b200.creation import array, zeros
+
+        dist = D.init(backend="nccl", timeout_s=60)
+        rng = np.random.default_rng(7)
+        x = rng.standard_normal(1_000_003).astype(np.float32) + 0.25
+        X = D.DistArray.from_global(x)
+        x64 = x.astype(np.float64)
+        assert abs(X.sum() - x64.sum()) <= 1e-4 * np.abs(x64).sum()
+        assert abs(X.mean() - x64.mean()) <= 1e-4 * abs(x64.mean())
+        assert abs(X.var() - x64.var()) <= 1e-4 * x64.var()
+        assert X.argmax() == O.argmax(x)
+        assert X.argmin() == int(np.argmin(x))
+        assert X.max() == float(x.max())
+        xn = x.copy()
+        xn[rng.choice(x.size, 1000, replace=False)] = np.nan
+        XN = D.DistArray.from_global(xn)
+        assert abs(XN.nansum() - np.nansum(xn.astype(np.float64))) <= 1e-4 * np.nansum(np.abs(xn))
+        assert abs(XN.nanmean() - np.nanmean(xn.astype(np.float64))) <= 1e-4 * abs(np.nanmean(xn))
+        xi = rng.integers(-100, 101, 3_000_017).astype(np.int32)
+        XI = D.DistArray.from_global(xi)
+        assert XI.sum() == int(xi.sum(dtype=np.int64))
+        np.testing.assert_array_equal(XI.cumsum().gather(), O.cumsum(xi))
+        xf = rng.uniform(0, 1, 2_000_001).astype(np.float32)
+        got = XF = D.DistArray.from_global(xf).cumsum().gather()
+        ref = O.cumsum_f64(xf)
+        assert np.max(np.abs(got - ref) / ref) <= 1e-4
+        m = rng.standard_normal((1001, 515)).astype(np.float32)
+        M = D.DistArray.from_global(m)
+        s1 = M.sum(axis=1).gather()
+        assert np.max(np.abs(s1 - m.astype(np.float64).sum(axis=1))) <= 1e-4 * np.abs(m).sum(axis=1).max()
+        s0 = M.sum(axis=0).get()
+        assert np.max(np.abs(s0 - m.astype(np.float64).sum(axis=0))) <= 1e-4 * np.abs(m).sum(axis=0).max()
+        c1 = M.cumsum(axis=1).gather()
+        assert np.max(np.abs(c1 - np.cumsum(m.astype(np.float64), axis=1))) <= 1e-3
+        a = (rng.standard_normal((512, 384)) / 20).astype(np.float32)
+        b = (rng.standard_normal((384, 640)) / 20).astype(np.float32)
+        A = D.DistArray.from_global(a)
+        Bl = array(b) if rank == 0 else zeros(b.shape, dtype=np.float32)
+        C = A.matmul(Bl).gather()
+        r = O.matmul_f64(a, b)
+        assert np.linalg.norm(C - r) / np.linalg.norm(r) <= 1e-5
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_two_gpu_distributed_ops():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+    for r, msg in res:
+        assert msg == "ok", f"rank {r}:\n{msg}"

@@ -205,3 +205,22 @@ def test_floor_divide_mod_magnitude_sweep(cp):
     Ai, Bi = cp.array(ai), cp.array(bi)
     np.testing.assert_array_equal(cp.floor_divide(Ai, Bi).get(), O.floor_divide(ai, bi))
     np.testing.assert_array_equal((Ai % Bi).get(), O.mod(ai, bi))
+
+
+def test_int32_floor_divide_fast_path_boundaries(cp):
+    """int32 floor_divide / % around the float fast path's bounds (|a| < 2^21,
+    |b| < 2^24): bit-exact against numpy on both sides."""
+    rng = np.random.default_rng(12)
+    n = 1 << 20
+    mags = np.array([1, 7, 1000, (1 << 21) - 1, 1 << 21, (1 << 24) - 1, 1 << 24, (1 << 31) - 1], np.int64)
+    a = (rng.choice(mags, n) - rng.integers(0, 3, n)) * rng.choice([-1, 1], n)
+    b = (rng.choice(mags, n) - rng.integers(0, 3, n)) * rng.choice([-1, 1], n)
+    a = np.clip(a, -(1 << 31), (1 << 31) - 1).astype(np.int32)
+    b = np.clip(b, -(1 << 31), (1 << 31) - 1).astype(np.int32)
+    b[b == 0] = 3
+    A, B = cp.array(a), cp.array(b)
+    np.testing.assert_array_equal(cp.floor_divide(A, B).get(), O.floor_divide(a, b))
+    np.testing.assert_array_equal((A % B).get(), O.mod(a, b))
+    small = rng.integers(-(1 << 21) + 1, 1 << 21, n).astype(np.int32)
+    sb = rng.integers(1, 1 << 24, n).astype(np.int32) * rng.choice(np.array([-1, 1], np.int32), n)
+    np.testing.assert_array_equal(cp.floor_divide(cp.array(small), cp.array(sb)).get(), O.floor_divide(small, sb))

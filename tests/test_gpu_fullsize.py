@@ -102,10 +102,11 @@ def test_c4_scans_2pow30(cp):
     x2 = rng.standard_normal((4096, 65536), dtype=np.float32)
     Y2 = cp.cumsum(cp.array(x2), axis=1)
     for r in (0, 1, 2047, 4095):
+        # normwise: an N(0,1) row's prefix crosses zero, where an elementwise
+        # relative error is not defined by the data
         ref = np.cumsum(x2[r].astype(np.float64))
-        scale = np.cumsum(np.abs(x2[r].astype(np.float64))) * 1e-7 + 1e-30
         got = Y2[r].get()
-        assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), scale)) <= 1e-4
+        assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) <= 1e-4
 
 
 def test_c5_matmul_baseline_shapes(cp):
