@@ -97,7 +97,21 @@ __device__ __forceinline__ void store_acc_value(void *out, long long idx, int dt
   store_scalar(out, idx, dt, false, 0, 0, (double)v, false);
 }
 
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float min_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 // ---------------------------------------------------------------- ops
+// four(acc, v0..v3, idx) folds four successive values of one reduction
+// (consecutive rows of the column kernel); ops without a cheaper form
+// apply one() four times.
 // Every op provides: Acc, init(), start(first_value), one(acc, v, idx),
 // vec<V>(acc, v[], base), combine(a, b), finish(acc, n, out, idx, dt, ddof, part).
 
@@ -124,6 +138,16 @@ struct SumLike {
     } else {
 #pragma unroll
       for (int j = 0; j < V; ++j) a += (Acc)ar(v[j]);
+    }
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long) {
+    if (IsFloat<T>::value && sizeof(T) < 8) {
+      a += (Acc)((AsF<T>::f(v0) + AsF<T>::f(v1)) + (AsF<T>::f(v2) + AsF<T>::f(v3)));
+    } else {
+      a += (Acc)ar(v0);
+      a += (Acc)ar(v1);
+      a += (Acc)ar(v2);
+      a += (Acc)ar(v3);
     }
   }
   __device__ static Acc combine(Acc a, Acc b) { return a + b; }
@@ -155,6 +179,12 @@ struct RedOp<MMP_R_PROD, T> {
   __device__ static void vec(Acc &a, const T (&v)[V], long long) {
 #pragma unroll
     for (int j = 0; j < V; ++j) a *= (Acc)ar(v[j]);
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    one(a, v0, i);
+    one(a, v1, i);
+    one(a, v2, i);
+    one(a, v3, i);
   }
   __device__ static Acc combine(Acc a, Acc b) { return a * b; }
   __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
@@ -208,6 +238,12 @@ struct ExtremeOp {
   __device__ static void vec(Acc &a, const T (&v)[V], long long) {
 #pragma unroll
     for (int j = 0; j < V; ++j) one(a, v[j], 0);
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    one(a, v0, i);
+    one(a, v1, i);
+    one(a, v2, i);
+    one(a, v3, i);
   }
   __device__ static Acc combine(Acc a, Acc b) { return pick(a, b); }
   __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
@@ -265,6 +301,20 @@ struct VarOp {
     } else {
 #pragma unroll
       for (int j = 0; j < V; ++j) one(a, v[j], 0);
+    }
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    if (IsFloat<T>::value && sizeof(T) < 8) {
+      const float kf = (float)a.k;
+      const float d0 = AsF<T>::f(v0) - kf, d1 = AsF<T>::f(v1) - kf, d2 = AsF<T>::f(v2) - kf,
+                  d3 = AsF<T>::f(v3) - kf;
+      a.s1 += (double)((d0 + d1) + (d2 + d3));
+      a.s2 += (double)((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3));
+    } else {
+      one(a, v0, i);
+      one(a, v1, i);
+      one(a, v2, i);
+      one(a, v3, i);
     }
   }
   __device__ static Acc combine(Acc a, Acc b) {
@@ -337,10 +387,37 @@ struct ArgOp {
       a.i = idx;
     }
   }
+  // float / half vectors: the NaN-propagating vector extreme first; the
+  // position of its first occurrence is only searched when it beats the
+  // running value (rare once a few vectors are in).
   template <int V>
   __device__ static void vec(Acc &a, const T (&v)[V], long long base) {
+    if constexpr (IsFloat<T>::value && sizeof(T) <= 4) {
+      float m = AsF<T>::f(v[0]);
 #pragma unroll
-    for (int j = 0; j < V; ++j) one(a, v[j], base + j);
+      for (int j = 1; j < V; ++j) m = MAX ? max_nan(m, AsF<T>::f(v[j])) : min_nan(m, AsF<T>::f(v[j]));
+      const bool mn = isnan_(m);
+      const bool take = (a.i < 0) || (!isnan_(a.v) && (mn || (MAX ? (m > a.v) : (m < a.v))));
+      if (take) {
+        int jj = V - 1;
+#pragma unroll
+        for (int j = V - 1; j >= 0; --j) {
+          const float x = AsF<T>::f(v[j]);
+          if (mn ? isnan_(x) : (x == m)) jj = j;
+        }
+        a.v = m;
+        a.i = base + jj;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) one(a, v[j], base + j);
+    }
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    one(a, v0, i);
+    one(a, v1, i + 8);
+    one(a, v2, i + 16);
+    one(a, v3, i + 24);
   }
   __device__ static Acc combine(Acc a, Acc b) { return pick(a, b); }
   __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
@@ -397,6 +474,12 @@ struct NanSumOp {
       for (int j = 0; j < V; ++j) one(a, v[j], 0);
     }
   }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    one(a, v0, i);
+    one(a, v1, i);
+    one(a, v2, i);
+    one(a, v3, i);
+  }
   __device__ static Acc combine(Acc a, Acc b) {
     a.s += b.s;
     a.c += b.c;
@@ -429,6 +512,12 @@ struct BoolOp {
   __device__ static void vec(Acc &a, const T (&v)[V], long long) {
 #pragma unroll
     for (int j = 0; j < V; ++j) one(a, v[j], 0);
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    one(a, v0, i);
+    one(a, v1, i);
+    one(a, v2, i);
+    one(a, v3, i);
   }
   __device__ static Acc combine(Acc a, Acc b) { return ANY ? (a | b) : (a & b); }
   __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
@@ -686,12 +775,7 @@ __device__ __forceinline__ void reduce_cols_body(const L &ld, long long outer, l
       ld.template vec<CV>(off + 16 * inner, v2);
       ld.template vec<CV>(off + 24 * inner, v3);
 #pragma unroll
-      for (int j = 0; j < CV; ++j) {
-        Op::one(acc[j], v0[j], r);
-        Op::one(acc[j], v1[j], r + 8);
-        Op::one(acc[j], v2[j], r + 16);
-        Op::one(acc[j], v3[j], r + 24);
-      }
+      for (int j = 0; j < CV; ++j) Op::four(acc[j], v0[j], v1[j], v2[j], v3[j], r);
     }
   }
   for (; r < r1; r += 8) {

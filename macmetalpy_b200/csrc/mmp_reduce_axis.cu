@@ -74,10 +74,18 @@ struct AxisRun {
       const long long ctiles = (inner + 32 * cv - 1) / (32 * cv);
       const long long gx = outer * ctiles;
       if (gx > 0x7fffffffll) return set_error(MMP_E_ARG, "reduction too large");
-      long long target = (long long)sms * 6;
+      // split the reduced axis so that the grid is one full wave
+      int occ = 0;
+      if (vec) {
+        MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reduce_cols_kernel<OPC, T, L, CV>, RBLOCK, 0));
+      } else {
+        MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reduce_cols_kernel<OPC, T, L, 1>, RBLOCK, 0));
+      }
+      if (occ < 1) occ = 1;
+      long long target = (long long)sms * occ;
       long long S = 1;
       if (gx <= 4096 && gx < target) {
-        S = (target + gx - 1) / gx;
+        S = target / gx;
         long long maxS = (k + 63) / 64;  // at least 64 rows per chunk
         if (S > maxS) S = maxS;
         if (S > 65535) S = 65535;

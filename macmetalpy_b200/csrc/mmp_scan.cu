@@ -57,6 +57,19 @@ template <> struct ScanOut<__half> { typedef __half type; static constexpr int c
 template <> struct ScanOut<float> { typedef float type; static constexpr int code = MMP_FLOAT32; };
 template <> struct ScanOut<double> { typedef double type; static constexpr int code = MMP_FLOAT64; };
 
+// The tile kernel stages a tile through dynamic shared memory (more than
+// the 48 KB default for 8-byte outputs); raise the limit once per kernel.
+template <class T, class O, bool PROD>
+int set_stage_smem() {
+  static bool done = false;
+  if (!done) {
+    MMP_CUDA_TRY(cudaFuncSetAttribute(scan_tiles_kernel<T, O, PROD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      StageSize<T, O>()));
+    done = true;
+  }
+  return MMP_OK;
+}
+
 }  // namespace
 
 template <int PRODI, class T>
@@ -103,7 +116,9 @@ struct ScanRun {
     TileState<C> ts;
     ts.desc = (TileDesc<C> *)desc;
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
-    scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, 0, st>>>(
+    rc = set_stage_smem<T, O, PROD>();
+    if (rc) return rc;
+    scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, StageSize<T, O>(), st>>>(
         x, y, rows, k, tpr, total, ts, counter, epoch, device_error_word(), cin, vec_ok);
     MMP_LAUNCH_CHECK("scan_tiles_kernel");
     return MMP_OK;
@@ -137,7 +152,7 @@ extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y
 // this library, so the call itself allocates nothing.
 //
 // The array holds the state of at most MMP_NOALLOC_SCAN_TILES tiles of
-// 4096 elements; larger scans are rejected with MMP_E_ARG.  Every GPU that
+// 8192 elements; larger scans are rejected with MMP_E_ARG.  Every GPU that
 // loads the library keeps the array (about 4 MiB) until the process exits.
 // All calls share it: calls that can overlap on the GPU (different streams
 // or devices sharing nothing else) race on it and must be serialised by the
@@ -204,7 +219,9 @@ struct ScanNoallocRun {
     const T *x = (const T *)xv;
     O *y = (O *)yv;
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
-    scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, 0, st>>>(
+    rc = set_stage_smem<T, O, PROD>();
+    if (rc) return rc;
+    scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, StageSize<T, O>(), st>>>(
         x, y, outer, k, tpr, total, ts, counter, 1u, device_error_word(), (const C *)carry, vec_ok);
     MMP_LAUNCH_CHECK("scan_tiles_kernel (noalloc)");
     return MMP_OK;

@@ -9,7 +9,8 @@
 // accumulates and returns 64-bit integers, float cumsum returns the input
 // float type.
 //
-// Rows of a (rows, k) view are cut into tiles of TILE elements.  Each block
+// Rows of a (rows, k) view are cut into tiles of STILE = 8192 elements
+// (512 threads x 16).  Each block
 // takes the next tile id from a global counter (so every lower tile is
 // already running), scans its tile in registers and shared memory, publishes
 // the tile aggregate, looks back over its predecessors within the same row
@@ -27,7 +28,7 @@
 
 namespace mmpd {
 
-constexpr int SBLOCK = 256;
+constexpr int SBLOCK = 512;
 constexpr int SITEMS = 16;
 constexpr int STILE = SBLOCK * SITEMS;
 
@@ -112,6 +113,11 @@ struct StageBytes {
   static constexpr int value = (STILE + STILE / (128 / sizeof(E))) * sizeof(E);
 };
 
+template <class T, class O>
+constexpr int StageSize() {
+  return StageBytes<T>::value > StageBytes<O>::value ? StageBytes<T>::value : StageBytes<O>::value;
+}
+
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tiles_per_row,
@@ -123,8 +129,7 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
   __shared__ long long s_tile;
   __shared__ A s_warp[SBLOCK / 32];
   __shared__ C s_excl;
-  constexpr int STAGE = StageBytes<T>::value > StageBytes<O>::value ? StageBytes<T>::value : StageBytes<O>::value;
-  __shared__ __align__(16) unsigned char s_stage[STAGE];
+  extern __shared__ __align__(16) unsigned char s_stage[];  // StageSize<T, O>() bytes
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   if (tid == 0) s_tile = (long long)atomicAdd(tile_counter, 1u);
   __syncthreads();

@@ -67,7 +67,7 @@ def test_noalloc_scan_rejects_more_than_its_array(cp):
 
     x = cp.zeros((16,), dtype=np.int32)
     y = cp.zeros((16,), dtype=np.int64)
-    too_long = 209715 * 4096 + 1  # MMP_NOALLOC_SCAN_TILES tiles of 4096, plus one element
+    too_long = 1 << 40  # far more tiles than MMP_NOALLOC_SCAN_TILES, whatever the tile size
     # refused on the host before any launch, so the small buffers are never read
     rc = cb.lib.mmp_scan_noalloc(0, MMP_INT32, ctypes.c_void_p(x.data_ptr), MMP_INT64, ctypes.c_void_p(y.data_ptr),
                                  1, too_long, 1, None)
