@@ -157,8 +157,8 @@ int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y,
  * and results as mmp_scan.  No counterpart in the reference (it has no such
  * callers).  The look-back state lives in a fixed device array of this
  * library (about 4 MiB per GPU that loads it, kept until exit), so scans
- * longer than MMP_NOALLOC_SCAN_TILES tiles of 8192 elements per row-set
- * (outer * ceil(k / 8192)) are rejected with MMP_E_ARG.  Calls share the
+ * longer than MMP_NOALLOC_SCAN_TILES tiles of 4096 elements per row-set
+ * (outer * ceil(k / 4096)) are rejected with MMP_E_ARG.  Calls share the
  * array: calls that may overlap on the GPU race and must be serialised by
  * the caller.  Requires mmp_init on the device; the first call on a device
  * looks up the array's address (make it before any stream capture). */

@@ -45,22 +45,27 @@ enum { MODE_3XTF32 = 0, MODE_TF32 = 1, MODE_F16 = 2 };
 
 template <int MODE> struct Cfg {
   static constexpr int ELEM = (MODE == MODE_F16) ? 2 : 4;
-  static constexpr int BK = 128 / ELEM;          // one 128-byte swizzle row of K
+  // bytes of K per tile row: 3xTF32 reads four operand tiles per stage, so
+  // it uses 64-byte rows (64-byte swizzle) to fit four stages; the others
+  // use 128-byte rows (128-byte swizzle)
+  static constexpr int ROW_BYTES = (MODE == MODE_3XTF32) ? 64 : 128;
+  static constexpr int BK = ROW_BYTES / ELEM;
   static constexpr int NOPS = (MODE == MODE_3XTF32) ? 2 : 1;  // tiles per operand
-  static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int A_BYTES = BM * ROW_BYTES;
+  static constexpr int B_BYTES = BN * ROW_BYTES;
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = (MODE == MODE_3XTF32) ? 2 : 4;
+  static constexpr int STAGES = 4;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int UMMA_K_BYTES = 32;  // K of one MMA: 8 tf32 or 16 f16
-  static constexpr int KSTEPS = 128 / UMMA_K_BYTES;
+  static constexpr int KSTEPS = ROW_BYTES / UMMA_K_BYTES;
+  static constexpr uint32_t SWIZZLE = (ROW_BYTES == 128) ? 2u : 4u;  // descriptor layout type
   // TF32 modes drain the TMEM accumulator every CHUNK k-tiles into
   // round-to-nearest float32 registers (two TMEM buffers alternate, so the
   // MMAs never wait): the tensor core's float32 accumulation then only spans
   // CHUNK * BK terms, which keeps the 3xTF32 result at float32 accuracy for
   // any K.  float16 keeps one accumulator for the whole K.
   static constexpr bool FLUSH = (MODE != MODE_F16);
-  static constexpr int CHUNK = 4;
+  static constexpr int CHUNK = 512 / ROW_BYTES;  // k-tiles per TMEM chunk: K = 128
   static constexpr int EPI_WARPS = FLUSH ? 8 : 4;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TMEM_COLS = FLUSH ? 2 * BN : BN;
@@ -119,15 +124,17 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major tile written by TMA with 128-byte
-// swizzle (8-row x 128-byte atoms, 1024 bytes apart), sm100 version field.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// Shared-memory matrix descriptor: K-major tile written by TMA with a
+// ROW-byte swizzle (8-row x ROW-byte atoms, 8*ROW bytes apart; layout type 2
+// = 128-byte swizzle, 4 = 64-byte swizzle), sm100 version field.
+template <int ROW>
+__device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused with swizzle)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset between 8-row groups
-  d |= (uint64_t)1 << 46;             // descriptor version
-  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused with swizzle)
+  d |= (uint64_t)((8 * ROW) >> 4) << 32;    // stride byte offset between 8-row groups
+  d |= (uint64_t)1 << 46;                   // descriptor version
+  d |= (uint64_t)(ROW == 128 ? 2 : 4) << 61;
   return d;
 }
 
@@ -303,12 +310,12 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < G::KSTEPS; ++kk) {
           const uint32_t off = kk * G::UMMA_K_BYTES;
-          const uint64_t da0 = sw128_desc(base + off);
-          const uint64_t db0 = sw128_desc(b0 + off);
+          const uint64_t da0 = sw_desc<G::ROW_BYTES>(base + off);
+          const uint64_t db0 = sw_desc<G::ROW_BYTES>(b0 + off);
           const uint32_t acc = (!first_of_chunk || kk > 0) ? 1u : 0u;
           if (MODE == MODE_3XTF32) {
-            const uint64_t da1 = sw128_desc(base + G::A_BYTES + off);
-            const uint64_t db1 = sw128_desc(b0 + G::B_BYTES + off);
+            const uint64_t da1 = sw_desc<G::ROW_BYTES>(base + G::A_BYTES + off);
+            const uint64_t db1 = sw_desc<G::ROW_BYTES>(b0 + G::B_BYTES + off);
             umma<MODE>(d, da1, db0, ID, acc);  // small * big
             umma<MODE>(d, da0, db1, ID, 1u);   // big * small
             umma<MODE>(d, da0, db0, ID, 1u);   // big * big
@@ -451,7 +458,7 @@ typedef CUresult (*PFN_Encode)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, v
                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static int make_map(CUtensorMap *map, const void *base, bool f16, long long kp, long long rows, long long batch,
-                    int box_k, int box_rows) {
+                    int box_k, int box_rows, int row_bytes) {
   static PFN_Encode enc = nullptr;
   if (!enc) enc = (PFN_Encode)mmp::driver_fn("cuTensorMapEncodeTiled");
   if (!enc) return mmp::set_error(MMP_E_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -462,7 +469,8 @@ static int make_map(CUtensorMap *map, const void *base, bool f16, long long kp, 
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return mmp::set_error(MMP_E_CUDA, "cuTensorMapEncodeTiled failed");
   return MMP_OK;
@@ -502,10 +510,11 @@ static int run(long long batch, long long m, long long n, long long k, const voi
   }
   CUtensorMap mA0, mA1, mB0, mB1;
   const bool f16 = MODE == MODE_F16;
-  int rc = make_map(&mA0, A0, f16, Kp, Mp, ba, G::BK, BM);
-  if (!rc) rc = make_map(&mA1, G::NOPS == 2 ? (const void *)A1 : (const void *)A0, f16, Kp, Mp, ba, G::BK, BM);
-  if (!rc) rc = make_map(&mB0, B0, f16, Kp, Np, bb, G::BK, BN);
-  if (!rc) rc = make_map(&mB1, G::NOPS == 2 ? (const void *)B1 : (const void *)B0, f16, Kp, Np, bb, G::BK, BN);
+  const int RB = G::ROW_BYTES;
+  int rc = make_map(&mA0, A0, f16, Kp, Mp, ba, G::BK, BM, RB);
+  if (!rc) rc = make_map(&mA1, G::NOPS == 2 ? (const void *)A1 : (const void *)A0, f16, Kp, Mp, ba, G::BK, BM, RB);
+  if (!rc) rc = make_map(&mB0, B0, f16, Kp, Np, bb, G::BK, BN, RB);
+  if (!rc) rc = make_map(&mB1, G::NOPS == 2 ? (const void *)B1 : (const void *)B0, f16, Kp, Np, bb, G::BK, BN, RB);
   if (rc) {
     cudaFreeAsync(ws, st);
     return rc;

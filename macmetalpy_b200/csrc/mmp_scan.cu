@@ -152,7 +152,7 @@ extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y
 // this library, so the call itself allocates nothing.
 //
 // The array holds the state of at most MMP_NOALLOC_SCAN_TILES tiles of
-// 8192 elements; larger scans are rejected with MMP_E_ARG.  Every GPU that
+// 4096 elements; larger scans are rejected with MMP_E_ARG.  Every GPU that
 // loads the library keeps the array (about 4 MiB) until the process exits.
 // All calls share it: calls that can overlap on the GPU (different streams
 // or devices sharing nothing else) race on it and must be serialised by the

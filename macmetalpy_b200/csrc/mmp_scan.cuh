@@ -9,8 +9,8 @@
 // accumulates and returns 64-bit integers, float cumsum returns the input
 // float type.
 //
-// Rows of a (rows, k) view are cut into tiles of STILE = 8192 elements
-// (512 threads x 16).  Each block
+// Rows of a (rows, k) view are cut into tiles of STILE = 4096 elements
+// (256 threads x 16).  Each block
 // takes the next tile id from a global counter (so every lower tile is
 // already running), scans its tile in registers and shared memory, publishes
 // the tile aggregate, looks back over its predecessors within the same row
@@ -28,7 +28,7 @@
 
 namespace mmpd {
 
-constexpr int SBLOCK = 512;
+constexpr int SBLOCK = 256;
 constexpr int SITEMS = 16;
 constexpr int STILE = SBLOCK * SITEMS;
 
@@ -84,23 +84,29 @@ __device__ __forceinline__ void desc_load(const TileDesc<C> *d, C &v, unsigned l
   memcpy(&v, &bits, 8);
 }
 
-// Wait for tile `t`'s descriptor of this launch; spins, then backs off;
-// bounded.  Returns the state (1 or 2) and the value, or 0 on time-out.
+__device__ __forceinline__ bool desc_ready(unsigned long long f, unsigned epoch) {
+  return (unsigned)(f >> 2) == (epoch & 0x3fffffffu) && (f & 3ull);
+}
+
+// Wait for tile `t`'s descriptor of this launch (given its first read);
+// spins, then backs off; bounded.  Returns the state (1 or 2), or 0 when
+// the wait ran out (the device error word is set).
 template <class C>
 __device__ __forceinline__ unsigned wait_desc(const TileDesc<C> *desc, long long t, unsigned epoch, int *err,
-                                              C &val) {
-  unsigned long long f = 0;
+                                              C &val, unsigned long long f) {
   unsigned ns = 32;
-  for (long long it = 0; it < (1ll << 22); ++it) {
-    desc_load(desc + t, val, f);
-    if ((unsigned)(f >> 2) == (epoch & 0x3fffffffu) && (f & 3ull)) return (unsigned)(f & 3ull);
+  for (long long it = 0; !desc_ready(f, epoch); ++it) {
+    if (it >= (1ll << 22)) {
+      atomicExch(err, 2);  // look-back wait ran out
+      return 0;
+    }
     if (it >= 64) {
       __nanosleep(ns);
       if (ns < 512) ns <<= 1;
     }
+    desc_load(desc + t, val, f);
   }
-  atomicExch(err, 2);  // look-back wait ran out
-  return 0;
+  return (unsigned)(f & 3ull);
 }
 
 // Shared-memory index with one padding element per 128 bytes.
@@ -214,26 +220,50 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
       const long long row_first = row * tiles_per_row;
       long long look = tile - 1;  // highest tile id still to fold in
       bool done = false;
+      // each round covers LB = 4 x 32 predecessors: lane l, slot q looks at
+      // tile look - (32 q + l); the four reads of a lane are issued together
+      constexpr int LB = 4;
       while (!done) {
-        long long t = look - lane;
-        unsigned f;
-        C val = Op::template id<C>();
-        if (t >= row_first) {
-          f = wait_desc(st.desc, t, ep, err, val);
-          if (f == 0) val = Op::template id<C>();
-        } else {
-          f = 2;  // before the row start: acts as an inclusive prefix of identity
-          if (carry_in && rows == 1 && t == row_first - 1) val = (C)(*carry_in);
+        C val[LB];
+        unsigned long long fl[LB];
+#pragma unroll
+        for (int q = 0; q < LB; ++q) {
+          const long long t = look - (32 * q + lane);
+          val[q] = Op::template id<C>();
+          fl[q] = 0;
+          if (t >= row_first) desc_load(st.desc + t, val[q], fl[q]);
         }
-        unsigned incl_mask = __ballot_sync(0xffffffffu, f == 2);
-        int stop = incl_mask ? (__ffs(incl_mask) - 1) : 31;
-        // fold lanes 0..stop (tile-1, tile-2, ..., the nearest inclusive prefix)
-        C part = (lane <= stop) ? val : Op::template id<C>();
+        unsigned state[LB];
+#pragma unroll
+        for (int q = 0; q < LB; ++q) {
+          const long long t = look - (32 * q + lane);
+          if (t >= row_first) {
+            state[q] = wait_desc(st.desc, t, ep, err, val[q], fl[q]);
+            if (state[q] == 0) val[q] = Op::template id<C>();
+          } else {
+            state[q] = 2;  // before the row start: an inclusive prefix of identity
+            val[q] = (carry_in && rows == 1 && t == row_first - 1) ? (C)(*carry_in) : Op::template id<C>();
+          }
+        }
+        // the nearest inclusive prefix: lowest slot q, then lowest lane
+        int qs = LB, stop = 31;
+#pragma unroll
+        for (int q = LB - 1; q >= 0; --q) {
+          const unsigned m = __ballot_sync(0xffffffffu, state[q] == 2);
+          if (m) {
+            qs = q;
+            stop = __ffs(m) - 1;
+          }
+        }
+        C part = Op::template id<C>();
+#pragma unroll
+        for (int q = 0; q < LB; ++q)
+          if (q < qs || (q == qs && lane <= stop)) part = Op::op(part, val[q]);
 #pragma unroll
         for (int d = 16; d >= 1; d >>= 1) part = Op::op(part, __shfl_down_sync(0xffffffffu, part, d));
-        excl = Op::op(excl, part);
-        if (incl_mask) done = true;
-        else look -= 32;
+        excl = Op::op(excl, __shfl_sync(0xffffffffu, part, 0));
+        if (qs < LB) done = true;
+        else look -= 32 * LB;
       }
       if (lane == 0) desc_store(st.desc + tile, Op::op(excl, (C)tile_agg), ep2 | 2ull);
     }
