@@ -45,16 +45,17 @@ enum { MODE_3XTF32 = 0, MODE_TF32 = 1, MODE_F16 = 2 };
 
 template <int MODE> struct Cfg {
   static constexpr int ELEM = (MODE == MODE_F16) ? 2 : 4;
-  // bytes of K per tile row: 3xTF32 reads four operand tiles per stage, so
-  // it uses 64-byte rows (64-byte swizzle) to fit four stages; the others
-  // use 128-byte rows (128-byte swizzle)
-  static constexpr int ROW_BYTES = (MODE == MODE_3XTF32) ? 64 : 128;
+  // bytes of K per tile row (128: 128-byte swizzle; 64-byte rows with the
+  // 64-byte swizzle are supported too).  3xTF32 keeps 128-byte rows and two
+  // stages: measured faster than 64-byte rows with four stages, as the
+  // kernel is bound by L2->SM operand bandwidth, not by TMA latency
+  static constexpr int ROW_BYTES = 128;
   static constexpr int BK = ROW_BYTES / ELEM;
   static constexpr int NOPS = (MODE == MODE_3XTF32) ? 2 : 1;  // tiles per operand
   static constexpr int A_BYTES = BM * ROW_BYTES;
   static constexpr int B_BYTES = BN * ROW_BYTES;
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = 4;
+  static constexpr int STAGES = (MODE == MODE_3XTF32) ? 2 : 4;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int UMMA_K_BYTES = 32;  // K of one MMA: 8 tf32 or 16 f16
   static constexpr int KSTEPS = ROW_BYTES / UMMA_K_BYTES;
@@ -428,7 +429,7 @@ template <class T, int MODE>
 __global__ void __launch_bounds__(256) prep_cols_kernel(const T *__restrict__ B, long long ldb, long long sB,
                                                         long long K, long long N, long long Np, long long Kp,
                                                         T *__restrict__ out0, T *__restrict__ out1) {
-  __shared__ T tile[32][33];
+  __shared__ T tile[32][33];  // grid.y = ceil(Kp / 32): Kp need not be a multiple of 32
   const long long b = blockIdx.z;
   const long long n0 = (long long)blockIdx.x * 32, k0 = (long long)blockIdx.y * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
@@ -439,6 +440,7 @@ __global__ void __launch_bounds__(256) prep_cols_kernel(const T *__restrict__ B,
   __syncthreads();
   for (int r = ty; r < 32; r += 8) {
     const long long n = n0 + r, k = k0 + tx;
+    if (k >= Kp) continue;
     const long long o = (b * Np + n) * Kp + k;
     T v = tile[tx][r];
     if constexpr (MODE == MODE_3XTF32) {
@@ -505,7 +507,7 @@ static int run(long long batch, long long m, long long n, long long k, const voi
     long long blocks = (tot + 255) / 256;
     if (blocks > (long long)mmp::sm_count() * 16) blocks = (long long)mmp::sm_count() * 16;
     prep_rows_kernel<T, MODE><<<(unsigned)blocks, 256, 0, st>>>((const T *)a, lda, sa, m, k, Mp, Kp, ba, A0, A1);
-    dim3 g2((unsigned)(Np / 32), (unsigned)(Kp / 32), (unsigned)bb);
+    dim3 g2((unsigned)(Np / 32), (unsigned)((Kp + 31) / 32), (unsigned)bb);
     prep_cols_kernel<T, MODE><<<g2, 256, 0, st>>>((const T *)b, ldb, sb, k, n, Np, Kp, B0, B1);
   }
   CUtensorMap mA0, mA1, mB0, mB1;
