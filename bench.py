@@ -411,16 +411,20 @@ def main():
         "clocks": clocks,
         "gpu_launches": args.steps * len(ops),
     }
-    if rank == 0 and not args.no_e2e:
-        line["e2e"] = e2e_c2(cp, d, steps=2)
-    if rank == 0 and not args.no_cpu:
+    if not args.no_e2e:
+        line["e2e"] = e2e_c2(cp, d, steps=2, dist=dist, local=local)
+    if rank == 0 and not args.no_cpu and world == 1:
         line["cpu_baseline"] = cpu_baseline()
-    if rank == 0 and not args.no_suite and world == 1:
+    if not args.no_suite:
         del d, ops
         import gc
 
         gc.collect()
-        line["suite"] = run_suite(cp, gen)
+        if world == 1:
+            if rank == 0:
+                line["suite"] = run_suite(cp, gen)
+        else:
+            line["dist_suite"] = dist_suite(cp, gen, dist, local)
     if rank == 0:
         print(json.dumps(line))
     if dist is not None:
@@ -510,9 +514,68 @@ def _traffic(opname):
     return None
 
 
-def e2e_c2(cp, d, steps=2):
+def dist_suite(cp, gen, dist, local):
+    """Block-distributed ops over all ranks (NCCL exchange steps included),
+    weak-scaled: every rank holds the single-GPU C3 / C4 operand, so the
+    global array is world x that.  Matmul is strong-scaled: A (16384,16384)
+    row-sharded, B broadcast from rank 0.  Device time (events on the
+    library stream, which is also torch's current stream), max over ranks;
+    values count every rank's bytes / FLOPs."""
+    import torch
+
+    from macmetalpy_b200 import distributed as D
+    from macmetalpy_b200._cuda_backend import Event
+
+    D.init()
+    W, R = D.world(), D.rank()
+
+    def timed(fn, iters=3, warm=2):
+        for _ in range(warm):
+            fn()
+        cp.synchronize()
+        dist.barrier()
+        s, e = Event(), Event()
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        ms = s.elapsed_ms(e) / iters
+        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    out = {}
+    n = 1 << 28
+    x = gen.normal((n,), 21 + 100 * R)
+    X = D.DistArray.from_local(x, W * n)
+    for name, f in (("sum_f32", X.sum), ("var_f32", X.var), ("argmax_f32", X.argmax)):
+        ms = timed(f)
+        out[f"dist_{name}"] = {"gbs": round(W * 4 * n / ms / 1e6, 1), "ms": round(ms, 4)}
+    M = D.DistArray.from_local(x.reshape(16384, 16384), W * 16384)
+    ms = timed(lambda: M.sum(axis=0))
+    out["dist_sum_axis0_f32"] = {"gbs": round(W * 4 * n / ms / 1e6, 1), "ms": round(ms, 4)}
+    del X, M, x
+    xi = gen.integers((n,), -100, 101, 31 + 100 * R)
+    XI = D.DistArray.from_local(xi, W * n)
+    ms = timed(lambda: XI.cumsum())
+    out["dist_cumsum_i32"] = {"gbs": round(W * 12 * n / ms / 1e6, 1), "ms": round(ms, 4)}
+    del XI, xi
+    m = 16384
+    s0, e0 = D.row_partition(m, W)[R]
+    a = gen.normal((e0 - s0, m), 41 + 100 * R) * np.float32(1 / 128)
+    b = gen.normal((m, m), 42) * np.float32(1 / 128)
+    A = D.DistArray.from_local(a, m)
+    ms = timed(lambda: A.matmul(b), iters=2, warm=1)
+    out["dist_matmul_f32_16384_bcastB"] = {"tflops": round(2 * m ** 3 / ms / 1e9, 2), "ms": round(ms, 3)}
+    out["world"] = W
+    return out
+
+
+def e2e_c2(cp, d, steps=2, dist=None, local=0):
     """Same op set through the public API with host buffers: every step
-    copies its inputs from pinned host memory and its results back."""
+    copies its inputs from pinned host memory and its results back.  With
+    several ranks every rank runs it on its own GPU and shard; the time is
+    the maximum over ranks and the value counts every rank's bytes."""
     from macmetalpy_b200 import _cuda_backend as cb
     from macmetalpy_b200._cuda_backend import Event
 
@@ -545,16 +608,26 @@ def e2e_c2(cp, d, steps=2):
     one_step()
     s, e = Event(), Event()
     cp.synchronize()
+    world = 1
+    if dist is not None:
+        dist.barrier()
+        world = dist.get_world_size()
     s.record()
     for _ in range(steps):
         one_step()
     e.record()
     ms = s.elapsed_ms(e)
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     for k in names:
         cb.lib.mmp_host_free(host[k][0])
     for k in outs:
         cb.lib.mmp_host_free(outs[k])
-    return {"value": round(step_bytes() * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+    return {"value": round(world * step_bytes() * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
             "ms_per_step": round(ms / steps, 2)}
 

@@ -220,50 +220,28 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
       const long long row_first = row * tiles_per_row;
       long long look = tile - 1;  // highest tile id still to fold in
       bool done = false;
-      // each round covers LB = 4 x 32 predecessors: lane l, slot q looks at
-      // tile look - (32 q + l); the four reads of a lane are issued together
-      constexpr int LB = 4;
+      // each round looks at 32 predecessors: lane l at tile look - l
       while (!done) {
-        C val[LB];
-        unsigned long long fl[LB];
-#pragma unroll
-        for (int q = 0; q < LB; ++q) {
-          const long long t = look - (32 * q + lane);
-          val[q] = Op::template id<C>();
-          fl[q] = 0;
-          if (t >= row_first) desc_load(st.desc + t, val[q], fl[q]);
+        const long long t = look - lane;
+        C val = Op::template id<C>();
+        unsigned state = 2;  // before the row start: an inclusive prefix of identity
+        if (t >= row_first) {
+          unsigned long long f;
+          desc_load(st.desc + t, val, f);
+          state = wait_desc(st.desc, t, ep, err, val, f);
+          if (state == 0) val = Op::template id<C>();
+        } else if (carry_in && rows == 1 && t == row_first - 1) {
+          val = (C)(*carry_in);
         }
-        unsigned state[LB];
-#pragma unroll
-        for (int q = 0; q < LB; ++q) {
-          const long long t = look - (32 * q + lane);
-          if (t >= row_first) {
-            state[q] = wait_desc(st.desc, t, ep, err, val[q], fl[q]);
-            if (state[q] == 0) val[q] = Op::template id<C>();
-          } else {
-            state[q] = 2;  // before the row start: an inclusive prefix of identity
-            val[q] = (carry_in && rows == 1 && t == row_first - 1) ? (C)(*carry_in) : Op::template id<C>();
-          }
-        }
-        // the nearest inclusive prefix: lowest slot q, then lowest lane
-        int qs = LB, stop = 31;
-#pragma unroll
-        for (int q = LB - 1; q >= 0; --q) {
-          const unsigned m = __ballot_sync(0xffffffffu, state[q] == 2);
-          if (m) {
-            qs = q;
-            stop = __ffs(m) - 1;
-          }
-        }
-        C part = Op::template id<C>();
-#pragma unroll
-        for (int q = 0; q < LB; ++q)
-          if (q < qs || (q == qs && lane <= stop)) part = Op::op(part, val[q]);
+        const unsigned m = __ballot_sync(0xffffffffu, state == 2);
+        const int stop = m ? (__ffs(m) - 1) : 31;
+        // fold lanes 0..stop (tile-1, tile-2, ..., the nearest inclusive prefix)
+        C part = (lane <= stop) ? val : Op::template id<C>();
 #pragma unroll
         for (int d = 16; d >= 1; d >>= 1) part = Op::op(part, __shfl_down_sync(0xffffffffu, part, d));
         excl = Op::op(excl, __shfl_sync(0xffffffffu, part, 0));
-        if (qs < LB) done = true;
-        else look -= 32 * LB;
+        if (m) done = true;
+        else look -= 32;
       }
       if (lane == 0) desc_store(st.desc + tile, Op::op(excl, (C)tile_agg), ep2 | 2ull);
     }

@@ -23,7 +23,7 @@ NVLink, one communicator per process group):
 * matmul: A row-sharded, B broadcast from rank 0 (``broadcast``), C
   row-sharded.
 
-The library's stream is set to torch's current stream, so kernels and NCCL
+The library and torch share one current stream, so kernels and NCCL
 collectives are ordered on the device without host synchronisation.  The
 merge helpers (``merge_moments``, ``pick_arg``, ``exclusive_prefix``,
 ``row_partition``) are pure functions, tested on CPU with ``gloo`` ranks.
@@ -69,7 +69,15 @@ def init(backend: str | None = None, timeout_s: float = 120.0):
         from . import _cuda_backend as cb
 
         cb.CudaBackend()
-        cb.check(cb.lib.mmp_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "set stream")
+        cur = torch.cuda.current_stream()
+        if cur.cuda_stream == 0:
+            # torch is on the legacy default stream: make the library's own
+            # (non-blocking) stream torch's current stream instead
+            h = ctypes.c_void_p()
+            cb.check(cb.lib.mmp_get_stream(ctypes.byref(h)), "get stream")
+            torch.cuda.set_stream(torch.cuda.ExternalStream(h.value, device=torch.cuda.current_device()))
+        else:
+            cb.check(cb.lib.mmp_set_stream(ctypes.c_void_p(cur.cuda_stream)), "set stream")
     return dist
 
 

@@ -65,10 +65,18 @@ def test_dtypes(cp):
         want = np.cumsum(x)
         assert got.dtype == want.dtype, dt
         np.testing.assert_array_equal(got.get(), want)
-    x = np.random.default_rng(5).uniform(0.999, 1.001, 5000).astype(np.float32)
-    got = cp.cumprod(cp.array(x)).get()
-    ref = np.cumprod(x.astype(np.float64))
-    assert np.max(np.abs(got - ref) / ref) <= 1e-4
+    # 5000: rows not a multiple of 16 elements (unaligned tile kernel);
+    # 12400: 16-byte aligned, ragged last tile (pipelined tile kernel)
+    for n in (5000, 12400):
+        x = np.random.default_rng(5).uniform(0.999, 1.001, n).astype(np.float32)
+        got = cp.cumprod(cp.array(x)).get()
+        ref = np.cumprod(x.astype(np.float64))
+        assert np.max(np.abs(got - ref) / ref) <= 1e-4
+    x = np.random.default_rng(6).standard_normal(3 * 4096 + 48)
+    got = cp.cumsum(cp.array(x)).get()
+    assert got.dtype == np.float64
+    ref = np.cumsum(x)
+    assert np.max(np.abs(got - ref)) <= 1e-9 * np.abs(x).sum()
 
 
 def test_repeated_calls_reuse_state(cp):
