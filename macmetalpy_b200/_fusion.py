@@ -92,11 +92,15 @@ class ScalarNode(FusionNode):
 
 
 class UnaryOpNode(FusionNode):
-    __slots__ = ("_op_name", "_input")
+    """``_in_dtype`` is the loop dtype the operand is cast to (equal to
+    ``_dtype`` except for predicates such as isnan, whose result is bool)."""
 
-    def __init__(self, op_name, input_node, shape, dtype):
+    __slots__ = ("_op_name", "_input", "_in_dtype")
+
+    def __init__(self, op_name, input_node, shape, dtype, in_dtype=None):
         self._op_name = op_name
         self._input = input_node
+        self._in_dtype = np.dtype(in_dtype) if in_dtype is not None else np.dtype(dtype)
         self._shape = tuple(shape)
         self._dtype = np.dtype(dtype)
         self._depth = input_node._depth + 1
@@ -157,6 +161,8 @@ _UNARY_UFUNC = {
     "asinh_op": np.arcsinh, "acosh_op": np.arccosh, "atanh_op": np.arctanh,
     "degrees_op": np.degrees, "radians_op": np.radians, "sign_op": np.sign,
     "floor_op": np.floor, "ceil_op": np.ceil, "square_op": np.square,
+    "isnan_op": np.isnan, "isinf_op": np.isinf, "isfinite_op": np.isfinite,
+    "signbit_op": np.signbit, "logical_not_op": np.logical_not, "invert_op": np.invert,
 }
 
 _BINARY_UFUNC = {
@@ -168,6 +174,10 @@ _BINARY_UFUNC = {
     "logaddexp2_op": np.logaddexp2, "heaviside_op": np.heaviside,
     "lt_op": np.less, "le_op": np.less_equal, "gt_op": np.greater, "ge_op": np.greater_equal,
     "eq_op": np.equal, "ne_op": np.not_equal,
+    "logical_and_op": np.logical_and, "logical_or_op": np.logical_or,
+    "logical_xor_op": np.logical_xor, "bitwise_and_op": np.bitwise_and,
+    "bitwise_or_op": np.bitwise_or, "bitwise_xor_op": np.bitwise_xor,
+    "left_shift_op": np.left_shift, "right_shift_op": np.right_shift,
 }
 
 _FUSEABLE_UNARY_OPS = frozenset(_UNARY_UFUNC)
@@ -190,6 +200,12 @@ _MATH2 = {
 }
 
 _CMP = {"lt_op": "<", "le_op": "<=", "gt_op": ">", "ge_op": ">=", "eq_op": "==", "ne_op": "!="}
+
+# bool predicates on the loop value (numpy: NaN is true, only zero is false)
+_LOGIC = {"logical_and_op": "&&", "logical_or_op": "||", "logical_xor_op": "!="}
+_BITS = {"bitwise_and_op": "&", "bitwise_or_op": "|", "bitwise_xor_op": "^"}
+_PRED = {"isnan_op": "mmpd::isnan_", "isinf_op": "mmpf::isinf_", "isfinite_op": "mmpf::isfinite_",
+         "signbit_op": "mmpf::signbit_"}
 
 
 def _is_float(dt) -> bool:
@@ -230,6 +246,16 @@ def _unary_expr(op: str, dt, x: str) -> str:
         return f"({x} * {_float_literal(float(c), dt if dt != np.float16 else np.dtype(np.float32))})"
     if op == "cast":
         return x
+    if op in _PRED:
+        return f"{_PRED[op]}({x})"
+    if op == "logical_not_op":
+        return f"(({x}) == {R}(0))"
+    if op == "invert_op":
+        if dt == np.bool_:
+            return f"(!{x})"
+        if f:
+            raise TypeError(f"invert needs an integer or bool loop dtype, got {dt}")
+        return f"({R})(~{x})"
     if op in _MATH1:
         if not f:
             raise TypeError(f"{op} needs a float loop dtype, got {dt}")
@@ -274,6 +300,16 @@ def _binary_expr(op: str, dt, a: str, b: str) -> str:
         return f"mmpf::fmin_<{R}>({a}, {b})"
     if op in _CMP:
         return f"({a} {_CMP[op]} {b})"
+    if op in _LOGIC:
+        return f"((({a}) != {R}(0)) {_LOGIC[op]} (({b}) != {R}(0)))"
+    if op in _BITS:
+        if f:
+            raise TypeError(f"{op} needs an integer or bool loop dtype, got {dt}")
+        return f"({a} {_BITS[op]} {b})"
+    if op in ("left_shift_op", "right_shift_op"):
+        if f or isbool:
+            raise TypeError(f"{op} needs an integer loop dtype, got {dt}")
+        return f"mmpf::{'shl_' if op == 'left_shift_op' else 'shr_'}<{R}>({a}, {b})"
     if op in _MATH2:
         if not f:
             raise TypeError(f"{op} needs a float loop dtype, got {dt}")
@@ -430,7 +466,8 @@ class _Plan:
             elif isinstance(node, ScalarNode):
                 topo.append(("sc", self.scalars.index(node), node._dtype.str))
             elif isinstance(node, UnaryOpNode):
-                topo.append(("un", node._op_name, node._dtype.str, self.ids[id(node._input)]))
+                topo.append(("un", node._op_name, node._dtype.str, node._in_dtype.str,
+                             self.ids[id(node._input)]))
             elif isinstance(node, CastNode):
                 topo.append(("cast", node._dtype.str, self.ids[id(node._input)]))
             elif isinstance(node, SelectNode):
@@ -502,10 +539,11 @@ def _emit_loader(plan: _Plan) -> tuple[str, list[str]]:
             if isinstance(node, CastNode):
                 lines.append(f"    const {t} {nm} = mmpd::cvt<{t}>({x});")
             else:
-                R = _arith_name(node._dtype)
-                xv = f"mmpd::cvt<{R}>(mmpd::cvt<{t}>({x}))"
+                ldt = node._in_dtype
+                R = _arith_name(ldt)
+                xv = f"mmpd::cvt<{R}>(mmpd::cvt<{_ct(ldt)}>({x}))"
                 lines.append(f"    const {R} x{i} = {xv};")
-                lines.append(f"    const {t} {nm} = mmpd::cvt<{t}>({_unary_expr(node._op_name, node._dtype, 'x' + str(i))});")
+                lines.append(f"    const {t} {nm} = mmpd::cvt<{t}>({_unary_expr(node._op_name, ldt, 'x' + str(i))});")
         elif isinstance(node, SelectNode):
             c_, x_, y_ = names[id(node._cond)], names[id(node._x)], names[id(node._y)]
             lines.append(f"    const {t} {nm} = mmpd::cvt<bool>({c_}) ? mmpd::cvt<{t}>({x_}) : mmpd::cvt<{t}>({y_});")

@@ -290,6 +290,42 @@ __device__ __forceinline__ I i_power(I a, I b) {
 }
 
 // ---- max/min with numpy's NaN rules
+// isinf / isfinite / signbit on the bit pattern (not folded under
+// fast-math); integers and bool are finite, and signbit of an integer is
+// its sign (numpy computes it through a float loop, same answer).
+template <class R>
+__device__ __forceinline__ bool isinf_(R) { return false; }
+__device__ __forceinline__ bool isinf_(float x) { return (__float_as_uint(x) & 0x7fffffffu) == 0x7f800000u; }
+__device__ __forceinline__ bool isinf_(double x) {
+  return ((unsigned long long)__double_as_longlong(x) & 0x7fffffffffffffffull) == 0x7ff0000000000000ull;
+}
+template <class R>
+__device__ __forceinline__ bool isfinite_(R) { return true; }
+__device__ __forceinline__ bool isfinite_(float x) { return (__float_as_uint(x) & 0x7fffffffu) < 0x7f800000u; }
+__device__ __forceinline__ bool isfinite_(double x) {
+  return ((unsigned long long)__double_as_longlong(x) & 0x7fffffffffffffffull) < 0x7ff0000000000000ull;
+}
+template <class R>
+__device__ __forceinline__ bool signbit_(R x) { return x < R(0); }
+__device__ __forceinline__ bool signbit_(float x) { return (__float_as_uint(x) >> 31) != 0u; }
+__device__ __forceinline__ bool signbit_(double x) {
+  return ((unsigned long long)__double_as_longlong(x) >> 63) != 0ull;
+}
+
+// numpy's shifts (npy_lshift / npy_rshift): a shift count outside
+// [0, bits) gives 0 (left) or the sign fill (right); the count is compared
+// as an unsigned value, so a negative count is out of range.
+template <class R>
+__device__ __forceinline__ R shl_(R a, R b) {
+  return ((unsigned long long)(long long)b < sizeof(R) * 8ull) ? (R)((unsigned long long)(long long)a << (int)b)
+                                                              : R(0);
+}
+template <class R>
+__device__ __forceinline__ R shr_(R a, R b) {
+  if ((unsigned long long)(long long)b < sizeof(R) * 8ull) return (R)(a >> (int)b);
+  return (a < R(0)) ? (R)(~R(0)) : R(0);
+}
+
 template <class R>
 __device__ __forceinline__ R maximum(R a, R b) { return (a >= b || isnan_(a)) ? a : b; }
 template <class R>

@@ -559,7 +559,7 @@ class ndarray:
                 o._materialize_if_lazy()
                 nodes[i] = ndarray._to_node(o, loop)
         if len(nodes) == 1:
-            node = _fu.UnaryOpNode(op_name, nodes[0], shape, out)
+            node = _fu.UnaryOpNode(op_name, nodes[0], shape, out, in_dtype=loop)
         else:
             node = _fu.BinaryOpNode(op_name, nodes[0], nodes[1], shape, out, in_dtype=loop)
         return ndarray._lazy(node)
@@ -635,6 +635,68 @@ class ndarray:
         self._materialize_if_lazy()
         _fu.run_elementwise(node, self._ptr, self._shape, out_strides=self._strides)
         return self
+
+    def _inplace_result(self, r):
+        """Write the (lazy) result ``r`` into this array, cast to its dtype."""
+        node = r._node()
+        if node._dtype != self._dtype:
+            node = _fu.CastNode(node, self._dtype)
+        self._materialize_if_lazy()
+        _fu.run_elementwise(node, self._ptr, self._shape, out_strides=self._strides)
+        return self
+
+    # boolean / bitwise operators, dispatched as the reference does
+    # (ndarray.py:1670-1700, 2549-2645): on integer arrays &, |, ^, ~ are the
+    # int32 bitwise ops of bitwise_ops; on bool and float arrays &, |, ^ are
+    # numpy's logical ops (the other operand taken as bool) and ~ is logical
+    # not (of the int32 cast, for floats); << and >> are always the int32
+    # shifts.  In-place forms cast the result back to this array's dtype.
+    def _logic_bits(self, o, bits, logic, rev=False):
+        from . import bitwise_ops, logic_ops
+        if self._dtype.kind in "iu":
+            f = getattr(bitwise_ops, bits)
+        else:
+            f = getattr(logic_ops, logic)
+            if not isinstance(o, ndarray):
+                o = np.asarray(o).astype(np.bool_)[()]
+        return f(o, self) if rev else f(self, o)
+
+    def __and__(self, o): return self._logic_bits(o, "bitwise_and", "logical_and")
+    def __rand__(self, o): return self._logic_bits(o, "bitwise_and", "logical_and", True)
+    def __or__(self, o): return self._logic_bits(o, "bitwise_or", "logical_or")
+    def __ror__(self, o): return self._logic_bits(o, "bitwise_or", "logical_or", True)
+    def __xor__(self, o): return self._logic_bits(o, "bitwise_xor", "logical_xor")
+    def __rxor__(self, o): return self._logic_bits(o, "bitwise_xor", "logical_xor", True)
+
+    def __invert__(self):
+        from . import bitwise_ops, logic_ops
+        if self._dtype.kind in "iu":
+            return bitwise_ops.invert(self)
+        if self._dtype == np.bool_:
+            return logic_ops.logical_not(self)
+        return logic_ops.logical_not(self.astype(np.int32))
+
+    def __lshift__(self, o):
+        from . import bitwise_ops
+        return bitwise_ops.left_shift(self, o)
+
+    def __rlshift__(self, o):
+        from . import bitwise_ops
+        return bitwise_ops.left_shift(o, self)
+
+    def __rshift__(self, o):
+        from . import bitwise_ops
+        return bitwise_ops.right_shift(self, o)
+
+    def __rrshift__(self, o):
+        from . import bitwise_ops
+        return bitwise_ops.right_shift(o, self)
+
+    def __iand__(self, o): return self._inplace_result(self & o)
+    def __ior__(self, o): return self._inplace_result(self | o)
+    def __ixor__(self, o): return self._inplace_result(self ^ o)
+    def __ilshift__(self, o): return self._inplace_result(self << o)
+    def __irshift__(self, o): return self._inplace_result(self >> o)
 
     def __iadd__(self, o): return self._inplace(o, "add_op")
     def __isub__(self, o): return self._inplace(o, "sub_op")

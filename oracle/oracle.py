@@ -26,6 +26,9 @@ __all__ = [
     "resolve_dtype", "c1_expression", "add", "floor_divide", "mod", "logaddexp", "broadcast_add",
     "reduce_sum", "reduce_mean", "reduce_var", "argmax", "argmax_axis", "nansum", "nanmean",
     "cumsum", "matmul", "sum_f64", "mean_f64", "var_f64", "cumsum_f64", "matmul_f64", "ulp_error",
+    "logical", "logical_not", "predicate", "isclose", "allclose", "array_equal", "count_nonzero",
+    "nan_to_num", "bitwise", "invert", "op_and", "op_or", "op_xor", "op_invert", "op_shift",
+    "nanprod", "nancumsum", "nancumprod", "nanvar", "nanstd", "nanargmax", "nanargmin",
 ]
 
 
@@ -180,3 +183,175 @@ def ulp_error(got, ref64) -> np.ndarray:
     same_inf = np.isinf(got) & np.isinf(ref32) & (np.sign(got) == np.sign(ref32))
     err[both_nan | same_inf] = 0.0
     return err
+
+
+# ------------------------------------------- comparison / logic / bitwise
+
+
+def logical(name, a, b):
+    """``logic_ops.logical_and/or/xor`` (logic_ops.py:45-66): the CPU branch
+    of ``_logical_binary`` calls ``np.logical_*`` on the operands as they are
+    (logic_ops.py:32-37)."""
+    return getattr(np, name)(a, b)
+
+
+def logical_not(a):
+    """``logic_ops.logical_not`` (logic_ops.py:53-61) -> ``np.logical_not``."""
+    return np.logical_not(a)
+
+
+def predicate(name, a):
+    """``isnan/isinf/isfinite`` (math_ops.py:558-577) and ``signbit``
+    (ufunc_ops.py:352-354): ``_unary_predicate_op``'s CPU branch
+    (ndarray.py:1255-1273) calls the numpy predicate."""
+    return getattr(np, name)(a)
+
+
+def isclose(a, b, rtol=1e-5, atol=1e-8, equal_nan=False):
+    """``math_ops.isclose`` CPU branch (math_ops.py:646-648) -> ``np.isclose``."""
+    return np.isclose(a, b, rtol=rtol, atol=atol, equal_nan=equal_nan)
+
+
+def allclose(a, b, rtol=1e-5, atol=1e-8, equal_nan=False):
+    """``math_ops.allclose`` (math_ops.py:663-673): Python bool."""
+    return bool(np.allclose(a, b, rtol=rtol, atol=atol, equal_nan=equal_nan))
+
+
+def array_equal(a, b, equal_nan=False):
+    """``math_ops.array_equal`` (math_ops.py:676-690): False on a shape
+    mismatch, else ``np.array_equal``; Python bool."""
+    a, b = np.asarray(a), np.asarray(b)
+    if a.shape != b.shape:
+        return False
+    return bool(np.array_equal(a, b, equal_nan=equal_nan))
+
+
+def count_nonzero(a, axis=None, keepdims=False):
+    """``math_ops.count_nonzero`` (math_ops.py:693-705): Python int without
+    an axis, else an intp array."""
+    r = np.count_nonzero(a, axis=axis, keepdims=keepdims)
+    if axis is None and not keepdims:
+        return int(r)
+    return np.asarray(r)
+
+
+def nan_to_num(x, nan=0.0, posinf=None, neginf=None):
+    """``math_ops.nan_to_num`` (math_ops.py:580-636): numpy's replacement,
+    posinf/neginf defaulting to the dtype's finite extremes."""
+    x = np.asarray(x)
+    if x.dtype.kind != "f":
+        return x.copy()
+    fi = np.finfo(x.dtype)
+    return np.nan_to_num(x, copy=True, nan=nan, posinf=fi.max if posinf is None else posinf,
+                         neginf=fi.min if neginf is None else neginf)
+
+
+def bitwise(name, a, b):
+    """``bitwise_ops.bitwise_and/or/xor/left_shift/right_shift``
+    (bitwise_ops.py:35-56, 58-95): both operands cast to int32, then the
+    numpy function (CPU branch :37-45); int32 result."""
+    return getattr(np, name)(np.asarray(a).astype(np.int32), np.asarray(b).astype(np.int32))
+
+
+def invert(a):
+    """``bitwise_ops.invert`` (bitwise_ops.py:70-82): ``~int32(a)``."""
+    return np.invert(np.asarray(a).astype(np.int32))
+
+
+def _bool_other(o):
+    return o if isinstance(o, np.ndarray) else np.asarray(o).astype(np.bool_)
+
+
+def op_and(a, b):
+    """``ndarray.__and__`` (ndarray.py:1670-1674): int32 bitwise for integer
+    arrays, else ``_boolean_op``'s CPU branch ``np.logical_and``
+    (ndarray.py:1588-1600) with a non-array operand taken as bool."""
+    a = np.asarray(a)
+    return bitwise("bitwise_and", a, b) if a.dtype.kind in "iu" else np.logical_and(a, _bool_other(b))
+
+
+def op_or(a, b):
+    """``ndarray.__or__`` (ndarray.py:1676-1680)."""
+    a = np.asarray(a)
+    return bitwise("bitwise_or", a, b) if a.dtype.kind in "iu" else np.logical_or(a, _bool_other(b))
+
+
+def op_xor(a, b):
+    """``ndarray.__xor__`` (ndarray.py:2578-2583)."""
+    a = np.asarray(a)
+    return bitwise("bitwise_xor", a, b) if a.dtype.kind in "iu" else np.logical_xor(a, _bool_other(b))
+
+
+def op_invert(a):
+    """``ndarray.__invert__`` (ndarray.py:1682-1703): integers ->
+    ``bitwise_ops.invert``; bool -> the ``bool_not_op`` kernel (logical not,
+    ``_kernels.py:968-972``); other dtypes -> ``not_op`` on the int32 cast,
+    read back as bool (``_kernels.py:889-894``, ``ndarray.py:1696-1703``).
+    The bool and float cases have no CPU branch in the reference; this is
+    what those kernels compute."""
+    a = np.asarray(a)
+    if a.dtype.kind in "iu":
+        return invert(a)
+    if a.dtype == np.bool_:
+        return np.logical_not(a)
+    return np.logical_not(a.astype(np.int32))
+
+
+def op_shift(name, a, b):
+    """``ndarray.__lshift__/__rshift__`` (ndarray.py:2549-2565) ->
+    ``bitwise_ops.left_shift/right_shift``."""
+    return bitwise(name, a, b)
+
+
+# ------------------------------------------------- remaining NaN-aware ops
+
+
+def _isfloat(a):
+    return np.asarray(a).dtype.kind == "f"
+
+
+def nanprod(a, axis=None):
+    """``nan_ops.nanprod`` (nan_ops.py:171-214): float -> ``np.nanprod``
+    (CPU branch :191-199); integers -> ``reductions.prod`` (``np.prod``)."""
+    return np.nanprod(a, axis=axis) if _isfloat(a) else np.prod(a, axis=axis)
+
+
+def nancumsum(a, axis=None):
+    """``nan_ops.nancumsum`` (nan_ops.py:215-241): float -> ``np.nancumsum``;
+    integers -> ``reductions.cumsum`` (int32 -> int64)."""
+    return np.nancumsum(a, axis=axis) if _isfloat(a) else np.cumsum(a, axis=axis)
+
+
+def nancumprod(a, axis=None):
+    """``nan_ops.nancumprod`` (nan_ops.py:244-270)."""
+    return np.nancumprod(a, axis=axis) if _isfloat(a) else np.cumprod(a, axis=axis)
+
+
+def nanvar(a, axis=None, ddof=0):
+    """``nan_ops.nanvar`` (nan_ops.py:484-559): float -> ``np.nanvar`` (CPU
+    branch :503-509); integers -> ``reductions.var`` (``np.var``)."""
+    return np.nanvar(a, axis=axis, ddof=ddof) if _isfloat(a) else np.var(a, axis=axis, ddof=ddof)
+
+
+def nanstd(a, axis=None, ddof=0):
+    """``nan_ops.nanstd`` (nan_ops.py:444-481): ``np.nanstd``."""
+    return np.nanstd(a, axis=axis, ddof=ddof) if _isfloat(a) else np.std(a, axis=axis, ddof=ddof)
+
+
+def _nanarg(fn_nan, fn_int, a, axis):
+    if not _isfloat(a):
+        return int(fn_int(a)) if axis is None else np.asarray(fn_int(a, axis=axis), dtype=np.int32)
+    r = fn_nan(a, axis=axis)
+    return int(r) if axis is None else np.asarray(r)
+
+
+def nanargmax(a, axis=None):
+    """``nan_ops.nanargmax`` (nan_ops.py:562-584): float -> ``np.nanargmax``
+    (Python int without an axis, numpy's int64 with one; ValueError on an
+    all-NaN slice); integers -> ``reductions.argmax`` (int32 with an axis)."""
+    return _nanarg(np.nanargmax, np.argmax, a, axis)
+
+
+def nanargmin(a, axis=None):
+    """``nan_ops.nanargmin`` (nan_ops.py:587-612)."""
+    return _nanarg(np.nanargmin, np.argmin, a, axis)

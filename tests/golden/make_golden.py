@@ -144,6 +144,129 @@ def main():
     out = os.path.join(HERE, "golden_v1.npz")
     np.savez_compressed(out, **g)
     print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
+    logic_golden(mp)
+    nan_golden(mp)
+
+
+def nan_golden(mp):
+    """The remaining NaN-aware reductions and scans (``nan_ops.py:171-612``)
+    on small float32 / int32 inputs with ~10% NaN, one all-NaN row and one
+    all-NaN column; every call takes the reference's CPU branch."""
+    g = {}
+    rng = np.random.default_rng(6)
+    m = rng.standard_normal((24, 40)).astype(np.float32)
+    m[rng.random(m.shape) < 0.1] = np.nan
+    m[5, :] = np.nan
+    m[:, 7] = np.nan
+    p = rng.uniform(0.9, 1.1, (24, 40)).astype(np.float32)
+    p[rng.random(p.shape) < 0.1] = np.nan
+    v = rng.standard_normal(1000).astype(np.float32)
+    v[rng.random(1000) < 0.1] = np.nan
+    mi = rng.integers(-5, 6, (24, 40)).astype(np.int32)
+    g.update(m=m, p=p, v=v, mi=mi)
+    M, P, V, MI = mp.array(m), mp.array(p), mp.array(v), mp.array(mi)
+    g["nanprod"] = np.asarray(mp.nanprod(P).get())
+    g["nanprod_ax0"] = mp.nanprod(P, axis=0).get()
+    g["nanprod_ax1"] = mp.nanprod(P, axis=1).get()
+    g["nancumsum"] = mp.nancumsum(V).get()
+    g["nancumsum_ax1"] = mp.nancumsum(M, axis=1).get()
+    g["nancumprod_ax0"] = mp.nancumprod(P, axis=0).get()
+    g["nancumsum_i"] = mp.nancumsum(MI).get()
+    for ddof in (0, 1):
+        g[f"nanvar_d{ddof}"] = np.asarray(mp.nanvar(M, ddof=ddof).get())
+        g[f"nanvar_ax0_d{ddof}"] = mp.nanvar(M, axis=0, ddof=ddof).get()
+        g[f"nanvar_ax1_d{ddof}"] = mp.nanvar(M, axis=1, ddof=ddof).get()
+        g[f"nanstd_ax1_d{ddof}"] = mp.nanstd(M, axis=1, ddof=ddof).get()
+    g["nanvar_i"] = np.asarray(mp.nanvar(MI).get())
+    g["nanargmax"] = np.asarray(mp.nanargmax(V))
+    g["nanargmin"] = np.asarray(mp.nanargmin(V))
+    mm = np.where(np.isnan(m), np.float32(0), m)
+    mm[3, ::2] = np.nan  # rows with NaN but no all-NaN slice
+    g["mm"] = mm
+    MM = mp.array(mm)
+    g["nanargmax_ax1"] = mp.nanargmax(MM, axis=1).get()
+    g["nanargmin_ax0"] = mp.nanargmin(MM, axis=0).get()
+    g["nanargmax_i_ax0"] = mp.nanargmax(MI, axis=0).get()
+    out = os.path.join(HERE, "golden_nan_v1.npz")
+    np.savez_compressed(out, **g)
+    print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
+
+
+def logic_golden(mp):
+    """Comparison / logical / bitwise / predicate ops (the next row after the
+    C1-C5 path) through the reference's own functions and operators; sizes
+    stay below its 4,194,304 CPU threshold (``bitwise_ops.py:32``;
+    ``logic_ops`` and ``math_ops.py:647`` use the same literal), so every
+    call takes its CPU branch.  ``~`` of a bool array has no CPU branch
+    (``ndarray.py:1687-1695`` runs the Metal ``bool_not_op``) and is not
+    recorded."""
+    g = {}
+    rng = np.random.default_rng(5)
+    fe = np.array([0.0, -0.0, 1.5, -2.5, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 3e38, 0.5, -0.5],
+                  np.float32)
+    f = np.concatenate([fe, rng.standard_normal(244).astype(np.float32)])
+    f2 = f.copy()
+    f2[::3] += np.float32(1e-6) * f2[::3]
+    f2[5::7] = np.nan
+    i = rng.integers(-1000, 1000, 256).astype(np.int32)
+    i[:8] = [0, 1, -1, 2147483647, -2147483648, 7, -7, 12345]
+    j = rng.integers(-40, 41, 256).astype(np.int32)
+    j[:8] = [0, 1, 31, 32, 33, -1, 100, 5]
+    bl = rng.random(256) < 0.5
+    bl2 = rng.random(256) < 0.5
+    w = rng.integers(-(1 << 40), 1 << 40, 64).astype(np.int64)
+    w2 = rng.integers(-(1 << 40), 1 << 40, 64).astype(np.int64)
+    g.update(f=f, f2=f2, i=i, j=j, bl=bl, bl2=bl2, w=w, w2=w2)
+    F, F2, I, J, BL, BL2, W, W2 = (mp.array(v) for v in (f, f2, i, j, bl, bl2, w, w2))
+    for nm in ("logical_and", "logical_or", "logical_xor"):
+        fn = getattr(mp, nm)
+        g[f"{nm}_ff"] = fn(F, F2).get()
+        g[f"{nm}_ii"] = fn(I, J).get()
+        g[f"{nm}_bb"] = fn(BL, BL2).get()
+    g["logical_not_f"] = mp.logical_not(F).get()
+    g["logical_not_i"] = mp.logical_not(I).get()
+    for nm in ("isnan", "isinf", "isfinite", "signbit"):
+        g[f"{nm}_f"] = getattr(mp, nm)(F).get()
+    g["signbit_i"] = mp.signbit(I).get()
+    g["isclose"] = mp.isclose(F, F2).get()
+    g["isclose_nan"] = mp.isclose(F, F2, equal_nan=True).get()
+    g["isclose_tol"] = mp.isclose(F, F2, rtol=1e-3, atol=1e-2).get()
+    g["allclose"] = np.asarray(mp.allclose(F, F2))
+    g["allclose_self_nan"] = np.asarray(mp.allclose(F, F, equal_nan=True))
+    g["array_equal"] = np.asarray(mp.array_equal(F, F))
+    g["array_equal_nan"] = np.asarray(mp.array_equal(F, F, equal_nan=True))
+    g["array_equal_i"] = np.asarray(mp.array_equal(I, I))
+    m2 = rng.integers(-2, 3, (16, 24)).astype(np.int32)
+    g["cnz_m"] = m2
+    g["cnz"] = np.asarray(mp.count_nonzero(mp.array(m2)))
+    g["cnz_ax0"] = mp.count_nonzero(mp.array(m2), axis=0).get()
+    g["cnz_ax1"] = mp.count_nonzero(mp.array(m2), axis=1).get()
+    g["cnz_f"] = np.asarray(mp.count_nonzero(F))
+    g["nan_to_num"] = mp.nan_to_num(F).get()
+    g["nan_to_num_v"] = mp.nan_to_num(F, nan=-1.0, posinf=9.0, neginf=-9.0).get()
+    for nm in ("bitwise_and", "bitwise_or", "bitwise_xor", "left_shift", "right_shift"):
+        fn = getattr(mp, nm)
+        g[f"{nm}_ii"] = fn(I, J).get()
+        g[f"{nm}_ww"] = fn(W, W2 if not nm.endswith("shift") else mp.array(w2 % 40)).get()
+        g[f"{nm}_bb"] = fn(BL, BL2).get()
+    g["invert_i"] = mp.invert(I).get()
+    g["invert_w"] = mp.invert(W).get()
+    g["invert_b"] = mp.invert(BL).get()
+    g["op_and_ii"] = (I & J).get()
+    g["op_or_ii"] = (I | J).get()
+    g["op_xor_ii"] = (I ^ J).get()
+    g["op_and_bb"] = (BL & BL2).get()
+    g["op_or_bb"] = (BL | BL2).get()
+    g["op_xor_bb"] = (BL ^ BL2).get()
+    g["op_and_ff"] = (F & F2).get()
+    g["op_inv_i"] = (~I).get()
+    g["op_lshift_ii"] = (I << J).get()
+    g["op_rshift_ii"] = (I >> J).get()
+    g["op_and_scalar"] = (I & 0xFF).get()
+    g["op_rand_scalar"] = (0xF0 & I).get()
+    out = os.path.join(HERE, "golden_logic_v1.npz")
+    np.savez_compressed(out, **g)
+    print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
 
 
 if __name__ == "__main__":

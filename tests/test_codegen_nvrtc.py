@@ -76,12 +76,19 @@ CASES = {
                            (1 << 16, 1 << 16)),
     "all_unary": lambda: (_unary_chain(), (256,)),
     "all_binary": lambda: (_binary_chain(), (256,)),
+    "int_bits_i32": lambda: (_int_bits_chain(np.int32), (256,)),
+    "int_bits_u8": lambda: (_int_bits_chain(np.uint8), (256,)),
+    "int_bits_i64": lambda: (_int_bits_chain(np.int64), (256,)),
+    "predicates_logic": lambda: (_predicates(), (256,)),
 }
+
+
+_INT_ONLY = {"invert_op", "bitwise_and_op", "bitwise_or_op", "bitwise_xor_op", "left_shift_op", "right_shift_op"}
 
 
 def _unary_chain():
     node = _inp((256,), np.float32)
-    for op in sorted(fu._FUSEABLE_UNARY_OPS):
+    for op in sorted(fu._FUSEABLE_UNARY_OPS - _INT_ONLY):
         node = fu.UnaryOpNode(op, node, (256,), np.float32)
     return node
 
@@ -89,11 +96,31 @@ def _unary_chain():
 def _binary_chain():
     a = _inp((256,), np.float64)
     node = a
-    for op in sorted(fu._FUSEABLE_BINARY_OPS):
+    for op in sorted(fu._FUSEABLE_BINARY_OPS - _INT_ONLY):
         if op in fu._CMP:
             continue
         node = fu.BinaryOpNode(op, node, a, (256,), np.float64)
     return node
+
+
+def _int_bits_chain(dt=np.int32):
+    a = _inp((256,), dt)
+    b = _inp((256,), dt)
+    node = a
+    for op in sorted(_INT_ONLY - {"invert_op"}):
+        node = fu.BinaryOpNode(op, node, b, (256,), dt)
+    return fu.UnaryOpNode("invert_op", node, (256,), dt)
+
+
+def _predicates():
+    x = _inp((256,), np.float32)
+    n = (256,)
+    p = [fu.UnaryOpNode(op, x, n, np.bool_, in_dtype=np.float32)
+         for op in ("isnan_op", "isinf_op", "isfinite_op", "signbit_op", "logical_not_op")]
+    node = p[0]
+    for q, op in zip(p[1:], ("logical_and_op", "logical_or_op", "logical_xor_op", "logical_and_op")):
+        node = fu.BinaryOpNode(op, node, q, n, np.bool_, in_dtype=np.bool_)
+    return fu.BinaryOpNode("logical_or_op", node, x, n, np.bool_, in_dtype=np.float32)
 
 
 @pytest.mark.parametrize("case", sorted(CASES))

@@ -88,3 +88,87 @@ def test_resolve_dtype_rules():
     assert O.resolve_dtype(np.int8) == np.int16
     assert O.resolve_dtype(np.uint8) == np.uint16
     assert O.resolve_dtype(None) == np.float32
+
+
+L = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_logic_v1.npz"))
+
+
+def test_logic_predicates():
+    f, f2, i, j, bl, bl2 = L["f"], L["f2"], L["i"], L["j"], L["bl"], L["bl2"]
+    for nm in ("logical_and", "logical_or", "logical_xor"):
+        eq(O.logical(nm, f, f2), L[f"{nm}_ff"])
+        eq(O.logical(nm, i, j), L[f"{nm}_ii"])
+        eq(O.logical(nm, bl, bl2), L[f"{nm}_bb"])
+    eq(O.logical_not(f), L["logical_not_f"])
+    eq(O.logical_not(i), L["logical_not_i"])
+    for nm in ("isnan", "isinf", "isfinite", "signbit"):
+        eq(O.predicate(nm, f), L[f"{nm}_f"])
+    eq(O.predicate("signbit", i), L["signbit_i"])
+    eq(O.isclose(f, f2), L["isclose"])
+    eq(O.isclose(f, f2, equal_nan=True), L["isclose_nan"])
+    eq(O.isclose(f, f2, rtol=1e-3, atol=1e-2), L["isclose_tol"])
+    assert O.allclose(f, f2) == bool(L["allclose"])
+    assert O.allclose(f, f, equal_nan=True) == bool(L["allclose_self_nan"])
+    assert O.array_equal(f, f) == bool(L["array_equal"]) is False  # NaN != NaN
+    assert O.array_equal(f, f, equal_nan=True) == bool(L["array_equal_nan"])
+    assert O.array_equal(i, i) == bool(L["array_equal_i"])
+    m = L["cnz_m"]
+    assert O.count_nonzero(m) == int(L["cnz"])
+    eq(O.count_nonzero(m, axis=0), L["cnz_ax0"])
+    eq(O.count_nonzero(m, axis=1), L["cnz_ax1"])
+    assert O.count_nonzero(f) == int(L["cnz_f"])
+    eq(O.nan_to_num(f), L["nan_to_num"])
+    eq(O.nan_to_num(f, nan=-1.0, posinf=9.0, neginf=-9.0), L["nan_to_num_v"])
+
+
+def test_bitwise_and_operators():
+    i, j, bl, bl2, w, w2, f, f2 = (L[k] for k in ("i", "j", "bl", "bl2", "w", "w2", "f", "f2"))
+    for nm in ("bitwise_and", "bitwise_or", "bitwise_xor", "left_shift", "right_shift"):
+        eq(O.bitwise(nm, i, j), L[f"{nm}_ii"])
+        eq(O.bitwise(nm, w, w2 if not nm.endswith("shift") else w2 % 40), L[f"{nm}_ww"])
+        eq(O.bitwise(nm, bl, bl2), L[f"{nm}_bb"])
+    eq(O.invert(i), L["invert_i"])
+    eq(O.invert(w), L["invert_w"])
+    eq(O.invert(bl), L["invert_b"])
+    eq(O.op_and(i, j), L["op_and_ii"])
+    eq(O.op_or(i, j), L["op_or_ii"])
+    eq(O.op_xor(i, j), L["op_xor_ii"])
+    eq(O.op_and(bl, bl2), L["op_and_bb"])
+    eq(O.op_or(bl, bl2), L["op_or_bb"])
+    eq(O.op_xor(bl, bl2), L["op_xor_bb"])
+    eq(O.op_and(f, f2), L["op_and_ff"])
+    eq(O.op_invert(i), L["op_inv_i"])
+    eq(O.op_shift("left_shift", i, j), L["op_lshift_ii"])
+    eq(O.op_shift("right_shift", i, j), L["op_rshift_ii"])
+    eq(O.op_and(i, 0xFF), L["op_and_scalar"])
+    eq(O.bitwise("bitwise_and", 0xF0, i), L["op_rand_scalar"])
+
+
+N = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_nan_v1.npz"))
+
+
+def test_nan_reductions_and_scans():
+    import warnings
+
+    warnings.simplefilter("ignore", RuntimeWarning)
+    m, p, v, mi, mm = N["m"], N["p"], N["v"], N["mi"], N["mm"]
+    eq(O.nanprod(p), N["nanprod"])
+    eq(O.nanprod(p, axis=0), N["nanprod_ax0"])
+    eq(O.nanprod(p, axis=1), N["nanprod_ax1"])
+    eq(O.nancumsum(v), N["nancumsum"])
+    eq(O.nancumsum(m, axis=1), N["nancumsum_ax1"])
+    eq(O.nancumprod(p, axis=0), N["nancumprod_ax0"])
+    eq(O.nancumsum(mi), N["nancumsum_i"])
+    for ddof in (0, 1):
+        eq(O.nanvar(m, ddof=ddof), N[f"nanvar_d{ddof}"])
+        eq(O.nanvar(m, axis=0, ddof=ddof), N[f"nanvar_ax0_d{ddof}"])
+        eq(O.nanvar(m, axis=1, ddof=ddof), N[f"nanvar_ax1_d{ddof}"])
+        eq(O.nanstd(m, axis=1, ddof=ddof), N[f"nanstd_ax1_d{ddof}"])
+    eq(O.nanvar(mi), N["nanvar_i"])
+    assert O.nanargmax(v) == int(N["nanargmax"])
+    assert O.nanargmin(v) == int(N["nanargmin"])
+    eq(O.nanargmax(mm, axis=1), N["nanargmax_ax1"])
+    eq(O.nanargmin(mm, axis=0), N["nanargmin_ax0"])
+    eq(O.nanargmax(mi, axis=0), N["nanargmax_i_ax0"])
+    with pytest.raises(ValueError):
+        O.nanargmax(m, axis=1)
