@@ -436,7 +436,8 @@ def main():
 CASES = ("add_f32", "floor_divide_f32", "mod_f32", "logaddexp_f32", "add_i32", "floor_divide_i32", "mod_i32",
          "bcast_add_f32", "c1_fused_sum", "sum_f32", "var_f32", "argmax_f32", "sum_axis0_f32", "sum_axis1_f32",
          "var_axis0_f32",
-         "cumsum_i32", "cumsum_f32", "cumsum_axis1_f32", "matmul_f32", "matmul_f16")
+         "cumsum_i32", "cumsum_f32", "cumsum_axis1_f32", "matmul_f32", "matmul_f16", "sort_f32", "argsort_f32",
+         "searchsorted_f32")
 
 
 def run_case(args):
@@ -490,10 +491,18 @@ def run_case(args):
             x, y = x.astype(np.float16), y.astype(np.float16)
         x, y = x.copy(), y.copy()
         fn, nb = (lambda: cp.matmul(x, y)), 2 * n ** 3
+    elif c in ("sort_f32", "argsort_f32"):
+        x = gen.normal((n,), 21)
+        f = cp.sort if c == "sort_f32" else cp.argsort
+        fn, nb = (lambda: f(x)), n
+    elif c == "searchsorted_f32":
+        a = cp.sort(gen.normal((1 << 20,), 22))
+        x = gen.normal((n,), 21)
+        fn, nb = (lambda: cp.searchsorted(a, x)), n
     else:
         raise SystemExit(f"unknown case {c}; one of {CASES}")
     ms = _time(cp, fn, iters=max(args.steps, 1), warm=max(args.warmup, 1))
-    unit = "TFLOP/s" if c.startswith("matmul") else "GB/s"
+    unit = "TFLOP/s" if c.startswith("matmul") else "Gkeys/s" if "sort" in c else "GB/s"
     val = nb / (ms / 1e3) / (1e12 if unit == "TFLOP/s" else 1e9)
     print(json.dumps({"case": c, "elements": n, "ms": round(ms, 4), "value": round(val, 2), "unit": unit}))
     return 0
@@ -706,6 +715,25 @@ def run_suite(cp, gen):
     Ha = (gen.normal((8192, 8192), 45) * np.float32(1 / 90.5)).astype(np.float16)
     Hb = (gen.normal((8192, 8192), 46) * np.float32(1 / 90.5)).astype(np.float16)
     out["c5_f16_8192"] = tflops(2 * 8192 ** 3, _time(cp, lambda: cp.matmul(Ha, Hb), iters=3))
+    del Ha, Hb
+    # next rows: logic (fused predicate + reduction), nan-ops, sort / searchsorted
+    x = gen.normal((1 << 28,), 21)
+    y = (x + np.float32(1e-7)).copy()
+    out["f1_allclose_2^28"] = gbs(8 * x.size, _time(cp, lambda: cp.allclose(x, y), iters=3))
+    out["f1_count_nonzero_gt_2^28"] = gbs(4 * x.size, _time(cp, lambda: cp.count_nonzero(x > 0), iters=3))
+    out["f4_nanvar_2^28"] = gbs(4 * x.size, _time(cp, lambda: cp.nanvar(x), iters=3))
+    del y
+    for n, tag in ((1 << 24, "2^24"), (1 << 28, "2^28")):
+        xs = x[:n].copy()
+        ms = _time(cp, lambda: cp.sort(xs), iters=3, warm=1)
+        out[f"f3_sort_f32_{tag}"] = {"gkeys_s": round(n / ms / 1e6, 3), "ms": round(ms, 3)}
+        ms = _time(cp, lambda: cp.argsort(xs), iters=3, warm=1)
+        out[f"f3_argsort_f32_{tag}"] = {"gkeys_s": round(n / ms / 1e6, 3), "ms": round(ms, 3)}
+        del xs
+    srt = cp.sort(x[: 1 << 20].copy())
+    q = x[: 1 << 24].copy()
+    ms = _time(cp, lambda: cp.searchsorted(srt, q), iters=3)
+    out["f3_searchsorted_2^20_x_2^24q"] = {"gq_s": round((1 << 24) / ms / 1e6, 3), "ms": round(ms, 3)}
     return out
 
 

@@ -106,7 +106,9 @@ int mmp_scratch(size_t bytes, void **ptr, void **tickets);
 /* ---- synchronisation (synchronize, _metal_backend.py:359-372) */
 int mmp_synchronize(void);
 /* Synchronise, then read and clear the device-side error word that kernels
- * with bounded waits set instead of hanging (0 = no error). */
+ * set instead of hanging or writing out of bounds: 0 = no error, 2 = scan
+ * look-back wait ran out, 3 = GEMM pipeline wait ran out, 4 = sort scatter
+ * offset out of range. */
 int mmp_check_device_error(int *code);
 
 /* ---- timing */
@@ -173,6 +175,23 @@ int mmp_gemm(int dtype, int mode, int64_t batch, int64_t m, int64_t n,
              int64_t k, const void *a, int64_t lda, int64_t stride_a,
              const void *b, int64_t ldb, int64_t stride_b, void *c,
              int64_t ldc, int64_t stride_c);
+
+/* Stable ascending sort of each row of a C-contiguous (rows, cols) array
+ * (sorting.sort / argsort, sorting.py:22-54, whose GPU branch is the bitonic
+ * network of :57-190).  Writes the sorted values to `y` and/or, when
+ * `indices` is not NULL, each sorted element's column index (int64, numpy's
+ * argsort).  numpy order: NaN last; with indices, -0.0 and +0.0 tie (and a
+ * -0.0 comes back as +0.0 in `y`).  rows * cols < 2^32.  Synchronises the
+ * stream once (to skip radix passes that would not move anything). */
+int mmp_sort(int dtype, const void *x, void *y, int64_t *indices, int64_t rows,
+             int64_t cols);
+
+/* out[q] = insertion point of v[q] in the ascending array a[0..n)
+ * (sorting.searchsorted, sorting.py:218-272).  side 0 = left, 1 = right;
+ * `sorter` (NULL or n int64 indices, already validated) reads a[sorter[i]].
+ * numpy's order: NaN sorts last.  a and v share `dtype`; out is int64. */
+int mmp_searchsorted(int dtype, const void *a, int64_t n, const void *v,
+                     int64_t m, int side, const int64_t *sorter, int64_t *out);
 
 #ifdef __cplusplus
 }

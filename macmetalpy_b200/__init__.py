@@ -23,6 +23,7 @@ from .nan_ops import *  # noqa: F401,F403
 from .ndarray import ndarray
 from .raw_kernel import RawKernel
 from .reductions import *  # noqa: F401,F403
+from .sorting import *  # noqa: F401,F403
 from .ufunc_ops import *  # noqa: F401,F403
 from .ufunc import maximum, minimum  # ufunc objects (ufunc.py:10-49)
 

@@ -82,6 +82,8 @@ SIGNATURES = {
     "mmp_scan_noalloc": (_int, [_int, _int, _vp, _int, _vp, _i64, _i64, _i64, _vp]),
     "mmp_gemm": (_int, [_int, _int, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp,
                         _i64, _i64]),
+    "mmp_sort": (_int, [_int, _vp, _vp, _vp, _i64, _i64]),
+    "mmp_searchsorted": (_int, [_int, _vp, _i64, _vp, _i64, _int, _vp, _vp]),
 }
 
 

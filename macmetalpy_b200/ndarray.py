@@ -143,7 +143,7 @@ class ndarray:
         """Upload a host array (after dtype resolution) into a new buffer."""
         arr = np.asarray(arr)
         target = resolve_dtype(dtype if dtype is not None else arr.dtype)
-        host = np.ascontiguousarray(arr, dtype=target)
+        host = np.asarray(arr, dtype=target, order="C")  # keeps 0-d shapes (ascontiguousarray makes them 1-d)
         out = cls._empty(host.shape, target)
         if host.nbytes:
             _cb.check(_cb.lib.mmp_h2d(ctypes.c_void_p(out._buffer.ptr), host.ctypes.data_as(ctypes.c_void_p),
@@ -272,7 +272,7 @@ class ndarray:
     def set(self, arr, stream=None) -> None:
         """Copy host data into this array (broadcast to its shape)."""
         self._materialize_if_lazy()
-        host = np.ascontiguousarray(np.broadcast_to(np.asarray(arr, dtype=self._dtype), self._shape))
+        host = np.asarray(np.broadcast_to(np.asarray(arr, dtype=self._dtype), self._shape), order="C")
         if self._is_c_contiguous():
             if host.nbytes:
                 _cb.check(_cb.lib.mmp_h2d(ctypes.c_void_p(self._ptr), host.ctypes.data_as(ctypes.c_void_p),
@@ -697,6 +697,20 @@ class ndarray:
     def __ixor__(self, o): return self._inplace_result(self ^ o)
     def __ilshift__(self, o): return self._inplace_result(self << o)
     def __irshift__(self, o): return self._inplace_result(self >> o)
+
+    # sorting (ndarray.py:2393-2412)
+    def sort(self, axis=-1):
+        """Sort in place."""
+        from . import sorting
+        self._inplace_result(sorting.sort(self, axis=axis))
+
+    def argsort(self, axis=-1):
+        from . import sorting
+        return sorting.argsort(self, axis=axis)
+
+    def searchsorted(self, v, side="left"):
+        from . import sorting
+        return sorting.searchsorted(self, v, side=side)
 
     def __iadd__(self, o): return self._inplace(o, "add_op")
     def __isub__(self, o): return self._inplace(o, "sub_op")

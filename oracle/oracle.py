@@ -29,6 +29,7 @@ __all__ = [
     "logical", "logical_not", "predicate", "isclose", "allclose", "array_equal", "count_nonzero",
     "nan_to_num", "bitwise", "invert", "op_and", "op_or", "op_xor", "op_invert", "op_shift",
     "nanprod", "nancumsum", "nancumprod", "nanvar", "nanstd", "nanargmax", "nanargmin",
+    "sort", "argsort", "searchsorted",
 ]
 
 
@@ -355,3 +356,27 @@ def nanargmax(a, axis=None):
 def nanargmin(a, axis=None):
     """``nan_ops.nanargmin`` (nan_ops.py:587-612)."""
     return _nanarg(np.nanargmin, np.argmin, a, axis)
+
+
+# ------------------------------------------------------ sort / searchsorted
+
+
+def sort(a, axis=-1):
+    """``sorting.sort`` CPU branch (sorting.py:22-35): ``np.sort``.  Values
+    do not depend on the sort kind (NaN last)."""
+    return np.sort(a, axis=axis)
+
+
+def argsort(a, axis=-1):
+    """``sorting.argsort`` CPU branch (sorting.py:41-54): ``np.argsort``.
+    The reference passes ``kind=None`` (numpy's unstable default, ties in an
+    unspecified order); this restatement uses ``kind="stable"``, which agrees
+    with it wherever there are no ties and defines the tie order the device
+    sort guarantees."""
+    return np.argsort(a, axis=axis, kind="stable")
+
+
+def searchsorted(a, v, side="left", sorter=None):
+    """``sorting.searchsorted`` fallback (sorting.py:270-272):
+    ``np.searchsorted`` (numpy order, NaN last; common dtype; int64)."""
+    return np.searchsorted(a, v, side=side, sorter=sorter)

@@ -146,6 +146,57 @@ def main():
     print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
     logic_golden(mp)
     nan_golden(mp)
+    sort_golden(mp)
+
+
+def sort_golden(mp):
+    """sort / argsort below the reference's 262,144-element GPU threshold
+    (``sorting.py:30,48``), i.e. its CPU branch: np.sort / np.argsort with
+    the default kind; argsort inputs have no ties (numpy's default kind
+    leaves their order unspecified).  searchsorted has a CPU branch only
+    with a sorter (``sorting.py:270-272``, np.searchsorted); without one it
+    always runs its Metal binary search (``:228-268``), so those cases record
+    np.searchsorted, the function its fallback calls."""
+    g = {}
+    rng = np.random.default_rng(7)
+    f = rng.standard_normal(5000).astype(np.float32)
+    f[:9] = [np.nan, -np.inf, np.inf, 0.0, -0.0, np.nan, 1e-45, -1e-45, 3e38]
+    i = rng.integers(-1000, 1000, 5000).astype(np.int32)
+    d = rng.standard_normal(3000)
+    u = rng.permutation(4000).astype(np.float32) * np.float32(0.5) - np.float32(700)
+    m = rng.standard_normal((37, 53)).astype(np.float32)
+    h = rng.standard_normal(2000).astype(np.float16)
+    g.update(f=f, i=i, d=d, u=u, m=m, h=h)
+    F, I, D, U, M, H = (mp.array(v) for v in (f, i, d, u, m, h))
+    g["sort_f"] = mp.sort(F).get()
+    g["sort_i"] = mp.sort(I).get()
+    g["sort_d"] = mp.sort(D).get()
+    g["sort_h"] = mp.sort(H).get()
+    g["sort_m_ax0"] = mp.sort(M, axis=0).get()
+    g["sort_m_ax1"] = mp.sort(M, axis=1).get()
+    g["sort_m_none"] = mp.sort(M, axis=None).get()
+    g["argsort_u"] = mp.argsort(U).get()
+    g["argsort_m_ax0"] = mp.argsort(M, axis=0).get()
+    g["argsort_m_ax1"] = mp.argsort(M, axis=1).get()
+    sf = np.sort(f)
+    q = np.concatenate([rng.standard_normal(500).astype(np.float32), f[:9], sf[100:110]])
+    g["q"] = q
+    Q = mp.array(q)
+    g["ss_left"] = np.searchsorted(sf, q)
+    g["ss_right"] = np.searchsorted(sf, q, side="right")
+    si = np.sort(i)
+    qi = rng.integers(-1100, 1100, 300).astype(np.int32)
+    g["qi"] = qi
+    g["ss_i_left"] = np.searchsorted(si, qi)
+    g["ss_i_right"] = np.searchsorted(si, qi, side="right")
+    perm = rng.permutation(5000)
+    srt = np.argsort(f[perm[:4000]], kind="stable")
+    g["perm_f"] = f[perm[:4000]]
+    g["sorter"] = srt
+    g["ss_sorter"] = mp.searchsorted(mp.array(f[perm[:4000]]), Q, sorter=mp.array(srt)).get()
+    out = os.path.join(HERE, "golden_sort_v1.npz")
+    np.savez_compressed(out, **g)
+    print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
 
 
 def nan_golden(mp):

@@ -51,3 +51,10 @@ def test_argument_checks_fail_cleanly():
     assert cb.lib.mmp_scan(0, 5, None, 7, None, -1, 1, 1, None) == -2
     assert cb.lib.mmp_gemm(10, 0, 1, -1, 1, 1, None, 1, 0, None, 1, 0, None, 1, 0) == -2
     assert cb.lib.mmp_reduce_axis(0, 10, None, 1, 0, 1, 10, ctypes.c_void_p(16), 0.0) == -2
+    assert cb.lib.mmp_sort(10, None, None, None, 1, -1) == -2
+    assert cb.lib.mmp_sort(10, ctypes.c_void_p(16), None, None, 1, 8) == -2  # no output
+    assert cb.lib.mmp_sort(10, ctypes.c_void_p(16), ctypes.c_void_p(16), None, 1 << 20, 1 << 20) == -2
+    assert b"2^32" in cb.lib.mmp_last_error()
+    assert cb.lib.mmp_searchsorted(10, None, -1, None, 1, 0, None, None) == -2
+    assert cb.lib.mmp_searchsorted(10, ctypes.c_void_p(16), 4, ctypes.c_void_p(16), 1, 2, None,
+                                   ctypes.c_void_p(16)) == -2

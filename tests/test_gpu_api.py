@@ -84,3 +84,14 @@ def test_native_library_loaded(cp):
     import macmetalpy_b200._cuda_backend as cb
     assert cb.lib.mmp_abi_version() == 1
     assert cb.CudaBackend().sm_count > 0
+
+
+def test_zero_d_arrays_keep_their_shape():
+    import macmetalpy_b200 as cp
+    for v in (3.5, np.float32(2.0), np.array(7, np.int32)):
+        a = cp.array(v)
+        assert a.shape == () and a.get().shape == ()
+        assert float(a.get()) == float(v)
+    b = cp.array(np.float32(1.0))
+    b.set(np.float32(4.0))
+    assert b.shape == () and float(b.get()) == 4.0

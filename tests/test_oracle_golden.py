@@ -172,3 +172,25 @@ def test_nan_reductions_and_scans():
     eq(O.nanargmax(mi, axis=0), N["nanargmax_i_ax0"])
     with pytest.raises(ValueError):
         O.nanargmax(m, axis=1)
+
+
+S = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_sort_v1.npz"))
+
+
+def test_sort_searchsorted():
+    for k in ("f", "i", "d", "h"):
+        eq(O.sort(S[k]), S[f"sort_{k}"])
+    m = S["m"]
+    eq(O.sort(m, axis=0), S["sort_m_ax0"])
+    eq(O.sort(m, axis=1), S["sort_m_ax1"])
+    eq(O.sort(m, axis=None), S["sort_m_none"])
+    eq(O.argsort(S["u"]), S["argsort_u"])
+    eq(O.argsort(m, axis=0), S["argsort_m_ax0"])
+    eq(O.argsort(m, axis=1), S["argsort_m_ax1"])
+    sf = np.sort(S["f"])
+    eq(O.searchsorted(sf, S["q"]), S["ss_left"])
+    eq(O.searchsorted(sf, S["q"], side="right"), S["ss_right"])
+    si = np.sort(S["i"])
+    eq(O.searchsorted(si, S["qi"]), S["ss_i_left"])
+    eq(O.searchsorted(si, S["qi"], side="right"), S["ss_i_right"])
+    eq(O.searchsorted(S["perm_f"], S["q"], sorter=S["sorter"]), S["ss_sorter"])
