@@ -15,19 +15,21 @@
 // sign bit set).  Rows are sorted together: an element's row id travels
 // with it and is sorted last, so the final order is by row, then by key.
 // One radix pass per byte (8-bit digits), least significant first:
-//   rs_hist     per-tile digit histogram, digit-major counts[d][tile]
+//   rs_hist     per-tile digit histogram (16-byte loads, per-warp counters),
+//               digit-major counts[d][tile]
 //   mmp_scan    inclusive scan of the counts -> (digit, tile) offsets
+//   rs_trivial  flags a pass whose digit is the same for every key; the host
+//               reads the flag (4 bytes) and skips that pass's scatter
 //   rs_scatter  stable placement: a tile is cut into one contiguous segment
 //               per warp, each warp walks its keys in memory order, ranking
-//               each key among equal digits with __match_any_sync and
-//               per-warp digit counters in shared memory.
-// rs_prep maps the keys and builds the histograms of every pass in one read;
-// the host reads them (one small copy) and skips passes whose digit is the
-// same for every key.  Temporary buffers come from the stream-ordered pool.
+//               each key among equal digits (one ballot per digit bit) and
+//               per-warp digit counters; the tile is first placed in digit
+//               order in shared memory, then written out by consecutive
+//               threads to consecutive addresses of each digit's range.
+// rs_prep maps the keys (and writes row / column ids) in one pass.
+// Temporary buffers come from the stream-ordered pool.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
-
-#include <vector>
 
 #include "mmp_dispatch.h"
 #include "mmp_device.cuh"
@@ -122,50 +124,20 @@ __device__ __forceinline__ unsigned lanemask_lt() {
   return m;
 }
 
-// Map keys, write row / column ids, and histogram every pass's digit.
-// ghist: [kbytes + rbytes][256].
+// Map keys and write row / column ids.
 template <class T, bool HI, bool HR>
 __global__ void __launch_bounds__(RS_THREADS) rs_prep(const T *__restrict__ x, typename RKey<T>::K *__restrict__ kout,
                                                       unsigned *__restrict__ iout, unsigned *__restrict__ rout,
-                                                      unsigned long long n, FastDiv cols, int rbytes, int tie_zero,
-                                                      unsigned *__restrict__ ghist) {
-  typedef typename RKey<T>::K K;
-  constexpr int KB = (int)sizeof(K);
-  extern __shared__ unsigned sh[];  // (KB + rbytes) * 256
-  const int lane = threadIdx.x & 31;
-  const int nh = (KB + rbytes) * 256;
-  for (int j = threadIdx.x; j < nh; j += blockDim.x) sh[j] = 0;
-  __syncthreads();
+                                                      unsigned long long n, FastDiv cols, int tie_zero) {
   const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
-  for (unsigned long long base = (unsigned long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31u); base < n;
-       base += stride) {
-    const unsigned long long i = base + lane;
-    const bool valid = i < n;
-    const unsigned act = __ballot_sync(0xffffffffu, valid);
-    if (!valid) continue;
-    const K k = RKey<T>::key(x[i], tie_zero != 0);
-    kout[i] = k;
-    unsigned r = 0;
+  for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    kout[i] = RKey<T>::key(x[i], tie_zero != 0);
     if (HI || HR) {
-      r = cols.div((unsigned)i);
+      const unsigned r = cols.div((unsigned)i);
       if (HI) iout[i] = (unsigned)i - r * cols.d;
       if (HR) rout[i] = r;
     }
-#pragma unroll
-    for (int b = 0; b < KB; ++b) {
-      const unsigned d = (unsigned)(k >> (8 * b)) & 255u;
-      const unsigned peers = __match_any_sync(act, d);
-      if ((peers & lanemask_lt()) == 0) atomicAdd(&sh[b * 256 + d], (unsigned)__popc(peers));
-    }
-    for (int b = 0; b < rbytes; ++b) {
-      const unsigned d = (r >> (8 * b)) & 255u;
-      const unsigned peers = __match_any_sync(act, d);
-      if ((peers & lanemask_lt()) == 0) atomicAdd(&sh[(KB + b) * 256 + d], (unsigned)__popc(peers));
-    }
   }
-  __syncthreads();
-  for (int j = threadIdx.x; j < nh; j += blockDim.x)
-    if (sh[j]) atomicAdd(&ghist[j], sh[j]);
 }
 
 template <class K, bool FR>
@@ -174,44 +146,97 @@ __device__ __forceinline__ unsigned digit_of(K k, unsigned r, int shift) {
 }
 
 // Digit histogram of one tile; counts are digit-major: counts[d * tiles + t].
+// Full tiles are read with 16-byte loads (tiles start 16-byte aligned); the
+// last, partial tile element by element.
 template <class K, bool FR>
 __global__ void __launch_bounds__(RS_THREADS) rs_hist(const K *__restrict__ kin, const unsigned *__restrict__ rin,
                                                       unsigned long long n, int shift, unsigned *__restrict__ counts,
                                                       unsigned tiles) {
-  __shared__ unsigned h[256];
-  h[threadIdx.x] = 0;
+  __shared__ unsigned h[RS_WARPS][256];
+  const int tid = threadIdx.x, w = tid >> 5;
+  for (int j = tid; j < RS_WARPS * 256; j += RS_THREADS) (&h[0][0])[j] = 0;
   __syncthreads();
   const unsigned long long t0 = (unsigned long long)blockIdx.x * RS_TILE;
-#pragma unroll 4
-  for (int e = 0; e < RS_ITEMS; ++e) {
-    const unsigned long long i = t0 + (unsigned long long)e * RS_THREADS + threadIdx.x;
-    if (i < n) atomicAdd(&h[digit_of<K, FR>(FR ? K(0) : kin[i], FR ? rin[i] : 0u, shift)], 1u);
+  if (t0 + RS_TILE <= n) {
+    if (FR) {
+      const uint4 *v = reinterpret_cast<const uint4 *>(rin + t0);
+#pragma unroll
+      for (int q = 0; q < RS_TILE / 4 / RS_THREADS; ++q) {
+        const uint4 c = v[q * RS_THREADS + tid];
+        atomicAdd(&h[w][(c.x >> shift) & 255u], 1u);
+        atomicAdd(&h[w][(c.y >> shift) & 255u], 1u);
+        atomicAdd(&h[w][(c.z >> shift) & 255u], 1u);
+        atomicAdd(&h[w][(c.w >> shift) & 255u], 1u);
+      }
+    } else {
+      constexpr int PER = 16 / (int)sizeof(K);
+      const uint4 *v = reinterpret_cast<const uint4 *>(kin + t0);
+#pragma unroll
+      for (int q = 0; q < RS_TILE / PER / RS_THREADS; ++q) {
+        uint4 c = v[q * RS_THREADS + tid];
+        const K *e = reinterpret_cast<const K *>(&c);
+#pragma unroll
+        for (int u = 0; u < PER; ++u) atomicAdd(&h[w][(unsigned)(e[u] >> shift) & 255u], 1u);
+      }
+    }
+  } else {
+    for (int e = 0; e < RS_ITEMS; ++e) {
+      const unsigned long long i = t0 + (unsigned long long)e * RS_THREADS + tid;
+      if (i < n) atomicAdd(&h[w][digit_of<K, FR>(FR ? K(0) : kin[i], FR ? rin[i] : 0u, shift)], 1u);
+    }
   }
   __syncthreads();
-  counts[(unsigned long long)threadIdx.x * tiles + blockIdx.x] = h[threadIdx.x];
+  unsigned c = 0;
+#pragma unroll
+  for (int v = 0; v < RS_WARPS; ++v) c += h[v][tid];
+  counts[(unsigned long long)tid * tiles + blockIdx.x] = c;
+}
+
+// Flags (sets *trivial) a pass whose digit is the same for every key: the
+// total of some digit equals n.  incl is the inclusive scan of counts.
+__global__ void rs_trivial(const unsigned long long *__restrict__ incl, unsigned tiles, unsigned long long n,
+                           unsigned *trivial) {
+  const unsigned d = threadIdx.x;
+  const unsigned long long end = incl[(unsigned long long)(d + 1) * tiles - 1];
+  const unsigned long long beg = d ? incl[(unsigned long long)d * tiles - 1] : 0ull;
+  if (end - beg == n) *trivial = 1u;
 }
 
 // Stable scatter of one tile (see the file comment).  incl is the inclusive
-// scan of counts.
+// scan of counts.  Dynamic shared memory: the tile's keys, then its column
+// ids (HI), then its row ids (HR), in digit order.
+template <class K, bool HI, bool HR>
+constexpr int ScatterSmem() {
+  return RS_TILE * ((int)sizeof(K) + (HI ? 4 : 0) + (HR ? 4 : 0));
+}
+
+// Resident blocks per SM asked of the register allocator: each key slot of
+// the 16 per thread costs sizeof(K) / 4 registers plus one per payload.
+template <class K, bool HI, bool HR>
+constexpr int ScatterMinBlocks() {
+  return ((int)sizeof(K) + (HI ? 4 : 0) + (HR ? 4 : 0)) <= 4 ? 4 : 3;
+}
+
 template <class K, bool HI, bool HR, bool FR>
-__global__ void __launch_bounds__(RS_THREADS) rs_scatter(
+__global__ void __launch_bounds__(RS_THREADS, (ScatterMinBlocks<K, HI, HR>())) rs_scatter(
     const K *__restrict__ kin, K *__restrict__ kout, const unsigned *__restrict__ iin, unsigned *__restrict__ iout,
     const unsigned *__restrict__ rin, unsigned *__restrict__ rout, unsigned long long n, int shift,
     const unsigned *__restrict__ counts, const unsigned long long *__restrict__ incl, unsigned tiles, int *err) {
   __shared__ unsigned s_cnt[RS_WARPS][256];
-  __shared__ unsigned long long s_off[256];
+  __shared__ unsigned long long s_off[256];  // global offset of (digit, this tile)
+  __shared__ unsigned s_bex[256];            // offset of each digit inside the tile
+  __shared__ unsigned s_wsum[RS_WARPS];
+  extern __shared__ __align__(16) unsigned char s_stage[];
+  K *sk = reinterpret_cast<K *>(s_stage);
+  unsigned *si = reinterpret_cast<unsigned *>(s_stage + RS_TILE * sizeof(K));
+  unsigned *sr = si + (HI ? RS_TILE : 0);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  for (int j = tid; j < RS_WARPS * 256; j += RS_THREADS) (&s_cnt[0][0])[j] = 0;
-  {
-    const unsigned long long c = (unsigned long long)tid * tiles + blockIdx.x;
-    s_off[tid] = incl[c] - counts[c];
-  }
-  __syncthreads();
-  const unsigned long long seg = (unsigned long long)blockIdx.x * RS_TILE + (unsigned long long)w * RS_SEG;
+  const unsigned long long t0 = (unsigned long long)blockIdx.x * RS_TILE;
+  const unsigned long long seg = t0 + (unsigned long long)w * RS_SEG;
   K k[RS_ITEMS];
   unsigned iv[RS_ITEMS], rv[RS_ITEMS], rank[RS_ITEMS];
 #pragma unroll
-  for (int e = 0; e < RS_ITEMS; ++e) {
+  for (int e = 0; e < RS_ITEMS; ++e) {  // the tile's loads go out first
     const unsigned long long i = seg + e * 32 + lane;
     k[e] = 0;
     iv[e] = rv[e] = 0;
@@ -221,47 +246,84 @@ __global__ void __launch_bounds__(RS_THREADS) rs_scatter(
       if (HR) rv[e] = rin[i];
     }
   }
+  for (int j = tid; j < RS_WARPS * 256; j += RS_THREADS) (&s_cnt[0][0])[j] = 0;
+  {
+    const unsigned long long c = (unsigned long long)tid * tiles + blockIdx.x;
+    s_off[tid] = incl[c] - counts[c];
+  }
+  __syncthreads();
   const unsigned lt = lanemask_lt();
 #pragma unroll
   for (int e = 0; e < RS_ITEMS; ++e) {
     const bool valid = seg + e * 32 + lane < n;
-    const unsigned vm = __ballot_sync(0xffffffffu, valid);
-    rank[e] = 0;
-    if (valid) {
-      const unsigned d = digit_of<K, FR>(k[e], rv[e], shift);
-      const unsigned peers = __match_any_sync(vm, d);
-      const unsigned before = (unsigned)__popc(peers & lt);
-      const unsigned c = s_cnt[w][d];
-      __syncwarp(vm);
-      if (before == 0) s_cnt[w][d] = c + (unsigned)__popc(peers);
-      __syncwarp(vm);
-      rank[e] = c + before;
+    const unsigned d = valid ? digit_of<K, FR>(k[e], rv[e], shift) : 0u;
+    // lanes holding the same digit: one ballot per digit bit (warp-level
+    // multisplit; a fixed cost, unlike __match_any_sync, whose cost grows
+    // with the number of distinct digits in the warp)
+    unsigned peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const bool bit = (d >> b) & 1u;
+      const unsigned bal = __ballot_sync(0xffffffffu, bit);
+      peers &= bit ? bal : ~bal;
     }
+    const unsigned before = (unsigned)__popc(peers & lt);
+    const unsigned c = valid ? s_cnt[w][d] : 0u;
+    __syncwarp();
+    if (valid && before == 0) s_cnt[w][d] = c + (unsigned)__popc(peers);
+    __syncwarp();
+    rank[e] = c + before;
   }
   __syncthreads();
-  {  // exclusive prefix of the warp counters, per digit (thread = digit)
-    unsigned run = 0;
+  {  // thread = digit: warp-exclusive counters, then the digit's offset in the tile
+    unsigned tot = 0;
 #pragma unroll
     for (int v = 0; v < RS_WARPS; ++v) {
       const unsigned c = s_cnt[v][tid];
-      s_cnt[v][tid] = run;
-      run += c;
+      s_cnt[v][tid] = tot;
+      tot += c;
     }
+    unsigned inc = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    if (lane == 31) s_wsum[w] = inc;
+    __syncthreads();
+    unsigned pre = 0;
+    for (int v = 0; v < w; ++v) pre += s_wsum[v];
+    s_bex[tid] = pre + inc - tot;
   }
   __syncthreads();
 #pragma unroll
   for (int e = 0; e < RS_ITEMS; ++e) {
     if (seg + e * 32 + lane < n) {
       const unsigned d = digit_of<K, FR>(k[e], rv[e], shift);
-      const unsigned long long dst = s_off[d] + s_cnt[w][d] + rank[e];
-      if (dst >= n) {  // inconsistent offsets: report, never write out of bounds
+      const unsigned lp = s_bex[d] + s_cnt[w][d] + rank[e];
+      if (lp >= (unsigned)RS_TILE) {  // inconsistent ranks: report, never write out of bounds
         atomicExch(err, 4);
         continue;
       }
-      kout[dst] = k[e];
-      if (HI) iout[dst] = iv[e];
-      if (HR) rout[dst] = rv[e];
+      sk[lp] = k[e];
+      if (HI) si[lp] = iv[e];
+      if (HR) sr[lp] = rv[e];
     }
+  }
+  __syncthreads();
+  const unsigned count = (unsigned)((n - t0) < (unsigned long long)RS_TILE ? (n - t0) : (unsigned long long)RS_TILE);
+  for (unsigned j = tid; j < count; j += RS_THREADS) {
+    const K key = sk[j];
+    const unsigned r = HR ? sr[j] : 0u;
+    const unsigned d = digit_of<K, FR>(key, r, shift);
+    const unsigned long long dst = s_off[d] + (j - s_bex[d]);
+    if (dst >= n) {  // inconsistent offsets: report, never write out of bounds
+      atomicExch(err, 4);
+      continue;
+    }
+    kout[dst] = key;
+    if (HI) iout[dst] = si[j];
+    if (HR) rout[dst] = r;
   }
 }
 
@@ -335,6 +397,22 @@ int grid_for(unsigned long long n, int threads) {
   return (int)(b < cap ? (b ? b : 1) : cap);
 }
 
+template <class K, bool HI, bool HR, bool FR>
+int launch_scatter(const K *kin, K *kout, const unsigned *iin, unsigned *iout, const unsigned *rin, unsigned *rout,
+                   unsigned long long n, int shift, const unsigned *cnt, const unsigned long long *inc,
+                   unsigned tiles) {
+  constexpr int SM = ScatterSmem<K, HI, HR>();
+  static bool attr = false;
+  if (!attr) {
+    MMP_CUDA_TRY(cudaFuncSetAttribute(rs_scatter<K, HI, HR, FR>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM));
+    attr = true;
+  }
+  rs_scatter<K, HI, HR, FR><<<tiles, RS_THREADS, SM, stream()>>>(kin, kout, iin, iout, rin, rout, n, shift, cnt,
+                                                                inc, tiles, device_error_word());
+  MMP_LAUNCH_CHECK("rs_scatter");
+  return MMP_OK;
+}
+
 template <class T, bool HI, bool HR>
 int run_passes(const T *x, T *y, long long *idx, unsigned long long rows, unsigned long long cols) {
   typedef typename RKey<T>::K K;
@@ -345,7 +423,7 @@ int run_passes(const T *x, T *y, long long *idx, unsigned long long rows, unsign
   if (HR)
     for (unsigned long long r = rows - 1; r; r >>= 8) ++rbytes;
   const unsigned tiles = (unsigned)((n + RS_TILE - 1) / RS_TILE);
-  PoolBuf kb[2], ib[2], rb[2], cnt, inc, gh;
+  PoolBuf kb[2], ib[2], rb[2], cnt, inc, flag;
   for (int b = 0; b < 2; ++b) {
     int rc = kb[b].alloc(n * sizeof(K));
     if (!rc && HI) rc = ib[b].alloc(n * 4);
@@ -355,23 +433,13 @@ int run_passes(const T *x, T *y, long long *idx, unsigned long long rows, unsign
   const size_t nc = (size_t)tiles * 256;
   int rc = cnt.alloc(nc * 4);
   if (!rc) rc = inc.alloc(nc * 8);
-  if (!rc) rc = gh.alloc((size_t)(KB + rbytes) * 256 * 4);
+  if (!rc) rc = flag.alloc(16);
   if (rc) return rc;
-  MMP_CUDA_TRY(cudaMemsetAsync(gh.p, 0, (size_t)(KB + rbytes) * 256 * 4, st));
-  const FastDiv fd = make_fastdiv((unsigned)cols);
-  const int smem = (KB + rbytes) * 256 * 4;
-  rs_prep<T, HI, HR><<<grid_for(n, RS_THREADS), RS_THREADS, smem, st>>>(
-      x, (K *)kb[0].p, (unsigned *)ib[0].p, (unsigned *)rb[0].p, n, fd, rbytes, HI ? 1 : 0, (unsigned *)gh.p);
+  rs_prep<T, HI, HR><<<grid_for(n, RS_THREADS), RS_THREADS, 0, st>>>(
+      x, (K *)kb[0].p, (unsigned *)ib[0].p, (unsigned *)rb[0].p, n, make_fastdiv((unsigned)cols), HI ? 1 : 0);
   MMP_LAUNCH_CHECK("rs_prep");
-  std::vector<unsigned> hist((size_t)(KB + rbytes) * 256);
-  MMP_CUDA_TRY(cudaMemcpyAsync(hist.data(), gh.p, hist.size() * 4, cudaMemcpyDeviceToHost, st));
-  MMP_CUDA_TRY(cudaStreamSynchronize(st));
   int cur = 0;
   for (int p = 0; p < KB + rbytes; ++p) {
-    bool trivial = false;
-    for (int d = 0; d < 256; ++d)
-      if (hist[(size_t)p * 256 + d] == n) trivial = true;
-    if (trivial) continue;  // every key has the same digit: the pass keeps the order
     const bool fr = p >= KB;
     const int shift = 8 * (fr ? p - KB : p);
     const K *kin = (const K *)kb[cur].p;
@@ -381,20 +449,22 @@ int run_passes(const T *x, T *y, long long *idx, unsigned long long rows, unsign
     MMP_LAUNCH_CHECK("rs_hist");
     rc = mmp_scan(MMP_S_SUM, MMP_UINT32, cnt.p, MMP_UINT64, inc.p, 1, (int64_t)nc, 1, nullptr);
     if (rc) return rc;
+    // a pass whose digit is the same for every key keeps the order: skip it
+    MMP_CUDA_TRY(cudaMemsetAsync(flag.p, 0, 4, st));
+    rs_trivial<<<1, 256, 0, st>>>((const unsigned long long *)inc.p, tiles, n, (unsigned *)flag.p);
+    MMP_LAUNCH_CHECK("rs_trivial");
+    unsigned trivial = 0;
+    MMP_CUDA_TRY(cudaMemcpyAsync(&trivial, flag.p, 4, cudaMemcpyDeviceToHost, st));
+    MMP_CUDA_TRY(cudaStreamSynchronize(st));
+    if (trivial) continue;
     K *kout = (K *)kb[cur ^ 1].p;
     const unsigned *iin = (const unsigned *)ib[cur].p;
     unsigned *iout = (unsigned *)ib[cur ^ 1].p, *rout = (unsigned *)rb[cur ^ 1].p;
-    if (fr)
-      rs_scatter<K, HI, HR, true><<<tiles, RS_THREADS, 0, st>>>(kin, kout, iin, iout, rin, rout, n, shift,
-                                                                 (const unsigned *)cnt.p,
-                                                                 (const unsigned long long *)inc.p, tiles,
-                                                                 device_error_word());
-    else
-      rs_scatter<K, HI, HR, false><<<tiles, RS_THREADS, 0, st>>>(kin, kout, iin, iout, rin, rout, n, shift,
-                                                                  (const unsigned *)cnt.p,
-                                                                  (const unsigned long long *)inc.p, tiles,
-                                                                  device_error_word());
-    MMP_LAUNCH_CHECK("rs_scatter");
+    const unsigned *cp = (const unsigned *)cnt.p;
+    const unsigned long long *ip = (const unsigned long long *)inc.p;
+    rc = fr ? launch_scatter<K, HI, HR, true>(kin, kout, iin, iout, rin, rout, n, shift, cp, ip, tiles)
+            : launch_scatter<K, HI, HR, false>(kin, kout, iin, iout, rin, rout, n, shift, cp, ip, tiles);
+    if (rc) return rc;
     cur ^= 1;
   }
   rs_finish<T><<<grid_for(n, 256), 256, 0, st>>>((const K *)kb[cur].p, (const unsigned *)ib[cur].p, y, idx, n);
