@@ -108,7 +108,8 @@ int mmp_synchronize(void);
 /* Synchronise, then read and clear the device-side error word that kernels
  * set instead of hanging or writing out of bounds: 0 = no error, 2 = scan
  * look-back wait ran out, 3 = GEMM pipeline wait ran out, 4 = sort scatter
- * offset out of range. */
+ * offset out of range, 5 = gather / scatter / compaction offset out of
+ * range. */
 int mmp_check_device_error(int *code);
 
 /* ---- timing */
@@ -192,6 +193,21 @@ int mmp_sort(int dtype, const void *x, void *y, int64_t *indices, int64_t rows,
  * numpy's order: NaN sorts last.  a and v share `dtype`; out is int64. */
 int mmp_searchsorted(int dtype, const void *a, int64_t n, const void *v,
                      int64_t m, int side, const int64_t *sorter, int64_t *out);
+
+/* ---- advanced indexing (ndarray.__getitem__/__setitem__ advanced keys,
+ * ndarray.py:874-957; indexing.take/put/nonzero/compress/extract,
+ * indexing.py:24-410 -- numpy on the host in the reference).  Offsets are in
+ * elements from `src` / `dst`; entries outside [0, limit) are skipped and
+ * set device error 5.  Elements move as raw 1/2/4/8-byte words. */
+int mmp_gather(int dtype, const void *src, int64_t limit, const int64_t *offsets,
+               int64_t n, void *out);
+int mmp_scatter(int dtype, void *dst, int64_t limit, const int64_t *offsets,
+                int64_t n, const void *values);
+/* out[k] = position of the k-th true entry of the bool mask[0..n), given
+ * incl = the inclusive scan of the mask and count = incl[n-1] (numpy's
+ * flatnonzero). */
+int mmp_compact_indices(const void *mask, const int64_t *incl, int64_t n,
+                        int64_t count, int64_t *out);
 
 #ifdef __cplusplus
 }

@@ -16,6 +16,7 @@ from ._config import get_config, set_config
 from ._cuda_backend import CudaBackend
 from .bitwise_ops import *  # noqa: F401,F403
 from .creation import *  # noqa: F401,F403
+from .indexing import *  # noqa: F401,F403
 from .linalg_top import matmul
 from .logic_ops import *  # noqa: F401,F403
 from .math_ops import *  # noqa: F401,F403

@@ -84,6 +84,9 @@ SIGNATURES = {
                         _i64, _i64]),
     "mmp_sort": (_int, [_int, _vp, _vp, _vp, _i64, _i64]),
     "mmp_searchsorted": (_int, [_int, _vp, _i64, _vp, _i64, _int, _vp, _vp]),
+    "mmp_gather": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
+    "mmp_scatter": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
+    "mmp_compact_indices": (_int, [_vp, _vp, _i64, _i64, _vp]),
 }
 
 

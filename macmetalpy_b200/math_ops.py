@@ -104,8 +104,13 @@ def dot(a, b, out=None):
 def where(condition, x=None, y=None):
     """``where(c, x, y)`` as a fused select: c*x + (1-c)*y is NOT used; the
     select is built from comparison masks so NaN/inf pass through."""
-    if x is None and y is None:
-        raise NotImplementedError("where(condition) (nonzero) is not on the device path")
+    if x is None and y is None:  # where(condition) is nonzero(condition)
+        from . import _advindex
+        from . import creation
+        c = condition if isinstance(condition, ndarray) else creation.asarray(np.asarray(condition))
+        return _advindex.nonzero(c)
+    if x is None or y is None:
+        raise ValueError("either both or neither of x and y should be given")
     from . import creation
     c = condition if isinstance(condition, ndarray) else creation.asarray(np.asarray(condition))
     cb = c if c.dtype == np.bool_ else (c != 0)

@@ -459,26 +459,20 @@ class ndarray:
 
     def __getitem__(self, key):
         self._materialize_if_lazy()
-        if isinstance(key, ndarray):
-            key = key.get()
-        if isinstance(key, tuple):
-            key = tuple(k.get() if isinstance(k, ndarray) else k for k in key)
         r = self._basic_index(key)
         if r is not None:
             return self._view(*r)
-        # advanced indexing (gather) is outside the device hot path: numpy on
-        # the host copy, result uploaded
-        return ndarray._from_numpy(np.asarray(self.get()[key]))
+        # advanced (integer / boolean array) indexing: device gather
+        from . import _advindex
+        return _advindex.getitem(self, key)
 
     def __setitem__(self, key, value):
         self._materialize_if_lazy()
-        if isinstance(key, ndarray):
-            key = key.get()
         r = self._basic_index(key)
         if r is None:
-            host = self.get()
-            host[key] = value.get() if isinstance(value, ndarray) else value
-            self.set(host)
+            # advanced indexing: device scatter (or a fused select for a mask)
+            from . import _advindex
+            _advindex.setitem(self, key, value)
             return
         shp, st, off = r
         target = self._view(shp, st, off)
@@ -697,6 +691,22 @@ class ndarray:
     def __ixor__(self, o): return self._inplace_result(self ^ o)
     def __ilshift__(self, o): return self._inplace_result(self << o)
     def __irshift__(self, o): return self._inplace_result(self >> o)
+
+    def nonzero(self):
+        from . import _advindex
+        return _advindex.nonzero(self)
+
+    def take(self, indices, axis=None, out=None, mode="raise"):
+        from . import indexing
+        return indexing.take(self, indices, axis=axis, out=out, mode=mode)
+
+    def put(self, ind, v, mode="raise"):
+        from . import indexing
+        return indexing.put(self, ind, v, mode=mode)
+
+    def compress(self, condition, axis=None, out=None):
+        from . import indexing
+        return indexing.compress(condition, self, axis=axis, out=out)
 
     # sorting (ndarray.py:2393-2412)
     def sort(self, axis=-1):

@@ -30,6 +30,8 @@ __all__ = [
     "nan_to_num", "bitwise", "invert", "op_and", "op_or", "op_xor", "op_invert", "op_shift",
     "nanprod", "nancumsum", "nancumprod", "nanvar", "nanstd", "nanargmax", "nanargmin",
     "sort", "argsort", "searchsorted",
+    "getitem", "setitem", "take", "take_along_axis", "nonzero", "flatnonzero", "argwhere", "compress",
+    "extract", "put", "putmask",
 ]
 
 
@@ -380,3 +382,69 @@ def searchsorted(a, v, side="left", sorter=None):
     """``sorting.searchsorted`` fallback (sorting.py:270-272):
     ``np.searchsorted`` (numpy order, NaN last; common dtype; int64)."""
     return np.searchsorted(a, v, side=side, sorter=sorter)
+
+
+# ------------------------------------------------------ advanced indexing
+
+
+def getitem(a, key):
+    """``ndarray.__getitem__`` with an advanced key (ndarray.py:874-941): the
+    CPU branch indexes the host copy with numpy."""
+    return np.asarray(a)[key]
+
+
+def setitem(a, key, value):
+    """``ndarray.__setitem__`` advanced branch (ndarray.py:948-957):
+    ``np_data[key] = value`` on a copy (returned)."""
+    b = np.array(a, copy=True)
+    b[key] = value
+    return b
+
+
+def take(a, indices, axis=None, mode="raise"):
+    """``indexing.take`` (indexing.py:24-91) -> ``np.take``."""
+    return np.take(a, indices, axis=axis, mode=mode)
+
+
+def take_along_axis(a, indices, axis):
+    """``indexing.take_along_axis`` (indexing.py:94-100)."""
+    return np.take_along_axis(a, indices, axis)
+
+
+def nonzero(a):
+    """``indexing.nonzero`` (indexing.py:370-374) -> ``np.nonzero``."""
+    return np.nonzero(a)
+
+
+def flatnonzero(a):
+    """``indexing.flatnonzero`` (indexing.py:377-381)."""
+    return np.flatnonzero(a)
+
+
+def argwhere(a):
+    """``indexing.argwhere`` (indexing.py:384-391)."""
+    return np.argwhere(a)
+
+
+def compress(condition, a, axis=None):
+    """``indexing.compress`` (indexing.py:221-231)."""
+    return np.compress(condition, a, axis=axis)
+
+
+def extract(condition, a):
+    """``indexing.extract`` (indexing.py:242-251)."""
+    return np.extract(condition, a)
+
+
+def put(a, ind, v, mode="raise"):
+    """``indexing.put`` (indexing.py:103-163): ``np.put`` on a copy."""
+    b = np.array(a, copy=True)
+    np.put(b, ind, v, mode=mode)
+    return b
+
+
+def putmask(a, mask, values):
+    """``indexing.putmask`` (indexing.py:179-189): ``np.putmask`` on a copy."""
+    b = np.array(a, copy=True)
+    np.putmask(b, mask, values)
+    return b

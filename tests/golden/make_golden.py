@@ -147,6 +147,70 @@ def main():
     logic_golden(mp)
     nan_golden(mp)
     sort_golden(mp)
+    index_golden(mp)
+
+
+def index_golden(mp):
+    """Advanced indexing and the indexing routines through the reference's
+    own __getitem__ / __setitem__ (numpy on the host, ``ndarray.py:874-957``)
+    and ``indexing.py`` functions."""
+    g = {}
+    rng = np.random.default_rng(8)
+    a = rng.standard_normal((6, 7, 8)).astype(np.float32)
+    m = rng.standard_normal((6, 7, 8)).astype(np.float32) > 0.3
+    i0 = np.array([5, 0, -1, 2, 2], np.int64)
+    i1 = np.array([[1, 6], [0, -7]], np.int64)
+    i2 = np.array([7, 0, 3], np.int64)
+    v = rng.integers(-50, 50, 40).astype(np.int32)
+    g.update(a=a, m=m, i0=i0, i1=i1, i2=i2, v=v)
+    A = mp.array(a)
+    g["get_mask"] = A[mp.array(m)].get()
+    g["get_i0"] = A[mp.array(i0)].get()
+    g["get_i0_i2"] = A[mp.array(i0[:3]), :, mp.array(i2)].get()            # non-adjacent: B first
+    g["get_s_i1"] = A[1:5, mp.array(i1)].get()                              # adjacent, 2-D index
+    g["get_int_arr"] = A[2, :, mp.array(i2)].get()                           # int + array, separated
+    g["get_i1_i1"] = A[mp.array(i1 % 6), mp.array(i1 % 7)].get()
+    g["get_mask_rows"] = A[mp.array(m[:, 0, 0])].get()
+    g["get_newaxis"] = A[None, mp.array(i0), ::2].get()
+    V = mp.array(v)
+    g["get_v_neg"] = V[mp.array(np.array([-1, -40, 3, 39]))].get()
+    # advanced __setitem__: the reference applies ``np_data[key] = value`` on
+    # the host copy and uploads it with ``set`` (ndarray.py:948-957), which
+    # needs Metal; the assignment itself is recorded here
+    b = a.copy()
+    b[m] = -1.0
+    g["set_mask_scalar"] = b
+    b = a.copy()
+    b[i0[:3], 2] = np.arange(24, dtype=np.float32).reshape(3, 8)
+    g["set_i0_row"] = b
+    b = a.copy()
+    b[:, np.array([6, 0]), 1] = 7.0
+    g["set_cols"] = b
+    g["take_v"] = mp.take(V, mp.array(np.array([0, 5, 39, -2]))).get()
+    g["take_ax1"] = mp.take(A, mp.array(np.array([6, 0, 3])), axis=1).get()
+    g["take_wrap"] = mp.take(V, mp.array(np.array([40, -41, 100])), mode="wrap").get()
+    g["take_clip"] = mp.take(V, mp.array(np.array([40, -41, 100])), mode="clip").get()
+    ta = rng.integers(0, 8, (6, 7, 3)).astype(np.int64)
+    g["ta"] = ta
+    g["take_along"] = mp.take_along_axis(A, mp.array(ta), axis=2).get()
+    nz = mp.nonzero(mp.array(m))
+    for k, x in enumerate(nz):
+        g[f"nonzero_{k}"] = x.get()
+    g["flatnonzero"] = mp.flatnonzero(mp.array(m)).get()
+    g["argwhere"] = mp.argwhere(mp.array(m[0])).get()
+    cond = rng.random(7) < 0.5
+    g["cond"] = cond
+    g["compress_ax1"] = mp.compress(mp.array(cond), A, axis=1).get()
+    g["extract"] = mp.extract(mp.array(m), A).get()
+    P = mp.array(v.copy())
+    mp.put(P, mp.array(np.array([0, 3, 39])), mp.array(np.array([100, 200], np.int32)))
+    g["put"] = P.get()
+    P = mp.array(v.copy())
+    mp.putmask(P, mp.array(v > 0), mp.array(np.array([7, 8, 9], np.int32)))
+    g["putmask"] = P.get()
+    out = os.path.join(HERE, "golden_index_v1.npz")
+    np.savez_compressed(out, **g)
+    print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
 
 
 def sort_golden(mp):

@@ -58,3 +58,6 @@ def test_argument_checks_fail_cleanly():
     assert cb.lib.mmp_searchsorted(10, None, -1, None, 1, 0, None, None) == -2
     assert cb.lib.mmp_searchsorted(10, ctypes.c_void_p(16), 4, ctypes.c_void_p(16), 1, 2, None,
                                    ctypes.c_void_p(16)) == -2
+    assert cb.lib.mmp_gather(10, None, 4, None, -1, None) == -2
+    assert cb.lib.mmp_scatter(10, None, -1, None, 1, None) == -2
+    assert cb.lib.mmp_compact_indices(None, None, -1, 0, None) == -2

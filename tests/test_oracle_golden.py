@@ -194,3 +194,35 @@ def test_sort_searchsorted():
     eq(O.searchsorted(si, S["qi"]), S["ss_i_left"])
     eq(O.searchsorted(si, S["qi"], side="right"), S["ss_i_right"])
     eq(O.searchsorted(S["perm_f"], S["q"], sorter=S["sorter"]), S["ss_sorter"])
+
+
+X = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_index_v1.npz"))
+
+
+def test_advanced_indexing_and_routines():
+    a, m, i0, i1, i2, v = (X[k] for k in ("a", "m", "i0", "i1", "i2", "v"))
+    eq(O.getitem(a, m), X["get_mask"])
+    eq(O.getitem(a, i0), X["get_i0"])
+    eq(O.getitem(a, (i0[:3], slice(None), i2)), X["get_i0_i2"])
+    eq(O.getitem(a, (slice(1, 5), i1)), X["get_s_i1"])
+    eq(O.getitem(a, (2, slice(None), i2)), X["get_int_arr"])
+    eq(O.getitem(a, (i1 % 6, i1 % 7)), X["get_i1_i1"])
+    eq(O.getitem(a, m[:, 0, 0]), X["get_mask_rows"])
+    eq(O.getitem(a, (None, i0, slice(None, None, 2))), X["get_newaxis"])
+    eq(O.getitem(v, np.array([-1, -40, 3, 39])), X["get_v_neg"])
+    eq(O.setitem(a, m, -1.0), X["set_mask_scalar"])
+    eq(O.setitem(a, (i0[:3], 2), np.arange(24, dtype=np.float32).reshape(3, 8)), X["set_i0_row"])
+    eq(O.setitem(a, (slice(None), np.array([6, 0]), 1), 7.0), X["set_cols"])
+    eq(O.take(v, np.array([0, 5, 39, -2])), X["take_v"])
+    eq(O.take(a, np.array([6, 0, 3]), axis=1), X["take_ax1"])
+    eq(O.take(v, np.array([40, -41, 100]), mode="wrap"), X["take_wrap"])
+    eq(O.take(v, np.array([40, -41, 100]), mode="clip"), X["take_clip"])
+    eq(O.take_along_axis(a, X["ta"], 2), X["take_along"])
+    for k, x in enumerate(O.nonzero(m)):
+        eq(x, X[f"nonzero_{k}"])
+    eq(O.flatnonzero(m), X["flatnonzero"])
+    eq(O.argwhere(m[0]), X["argwhere"])
+    eq(O.compress(X["cond"], a, axis=1), X["compress_ax1"])
+    eq(O.extract(m, a), X["extract"])
+    eq(O.put(v, np.array([0, 3, 39]), np.array([100, 200], np.int32)), X["put"])
+    eq(O.putmask(v, v > 0, np.array([7, 8, 9], np.int32)), X["putmask"])
