@@ -220,17 +220,17 @@ __device__ __forceinline__ I i_floor_divide(I a, I b) {
 __device__ __forceinline__ int i32_floor_divide(int a, int b) {
   const unsigned ua = (unsigned)(a < 0 ? -a : a), ub = (unsigned)(b < 0 ? -b : b);
   if (b != 0 && ua < (1u << 21) && ub < (1u << 24)) {
+    // corrections as selects (no divergent branches inside the fast path)
     int q = (int)truncf(__fdividef((float)a, (float)b));
     int r = a - q * b;
-    if (b > 0) {
-      if (r < 0) { q -= 1; r += b; }
-      if (r < 0) { q -= 1; r += b; }
-      if (r >= b) { q += 1; }
-    } else {
-      if (r > 0) { q -= 1; r += b; }
-      if (r > 0) { q -= 1; r += b; }
-      if (r <= b) { q += 1; }
-    }
+    const bool pos = b > 0;
+    bool c = pos ? (r < 0) : (r > 0);
+    q -= c ? 1 : 0;
+    r += c ? b : 0;
+    c = pos ? (r < 0) : (r > 0);
+    q -= c ? 1 : 0;
+    r += c ? b : 0;
+    q += (pos ? (r >= b) : (r <= b)) ? 1 : 0;
     return q;
   }
   return i_floor_divide<int>(a, b);
@@ -343,23 +343,26 @@ template <class R>
 __device__ __forceinline__ R log1p_of_exp(R t) {
   return (t < R(2.44140625e-4)) ? (t - R(0.5) * t * t) : m_log1p(t);
 }
+// numpy's npy_logaddexp: x == y -> x + ln 2 (equal infinities without nan);
+// otherwise max(x, y) + log1p(exp(-|x - y|)); nan in, nan out.  Written
+// with one divergent branch (inside log1p_of_exp) and selects for the
+// special cases, so a warp runs the exp once and the library log1p only
+// when one of its lanes needs it.
 template <class R>
 __device__ __forceinline__ R logaddexp(R x, R y) {
-  if (x == y) return x + Consts<R>::loge2();  // equal infinities without nan
-  R tmp = x - y;
-  if (tmp > R(0)) return x + log1p_of_exp(m_exp(-tmp));
-  if (tmp <= R(0)) return y + log1p_of_exp(m_exp(tmp));
-  return tmp;  // nan
+  const R tmp = x - y;
+  const R mx = (tmp > R(0)) ? x : y;
+  const R r = mx + log1p_of_exp(m_exp(-fabs(tmp)));
+  return (x == y) ? x + Consts<R>::loge2() : ((tmp != tmp) ? tmp : r);
 }
 template <class R>
 __device__ __forceinline__ R log2_1p(R x) { return Consts<R>::log2e() * m_log1p(x); }
 template <class R>
-__device__ __forceinline__ R logaddexp2(R x, R y) {
-  if (x == y) return x + R(1);
-  R tmp = x - y;
-  if (tmp > R(0)) return x + log2_1p(m_exp2(-tmp));
-  if (tmp <= R(0)) return y + log2_1p(m_exp2(tmp));
-  return tmp;
+__device__ __forceinline__ R logaddexp2(R x, R y) {  // numpy's npy_logaddexp2, same structure as logaddexp
+  const R tmp = x - y;
+  const R mx = (tmp > R(0)) ? x : y;
+  const R r = mx + log2_1p(m_exp2(-fabs(tmp)));
+  return (x == y) ? x + R(1) : ((tmp != tmp) ? tmp : r);
 }
 
 template <class R>
