@@ -434,7 +434,8 @@ def main():
 
 
 CASES = ("add_f32", "floor_divide_f32", "mod_f32", "logaddexp_f32", "add_i32", "floor_divide_i32", "mod_i32",
-         "bcast_add_f32", "c1_fused_sum", "sum_f32", "var_f32", "argmax_f32", "sum_axis0_f32", "sum_axis1_f32",
+         "bcast_add_f32", "c1_fused_sum", "sum_f32", "var_f32", "argmax_f32", "argmin_f32", "nansum_f32",
+         "sum_axis0_f32", "sum_axis1_f32",
          "var_axis0_f32",
          "cumsum_i32", "cumsum_f32", "cumsum_axis1_f32", "matmul_f32", "matmul_f16", "sort_f32", "argsort_f32",
          "searchsorted_f32")
@@ -465,9 +466,10 @@ def run_case(args):
     elif c == "c1_fused_sum":
         x = gen.normal((n,), 11)
         fn, nb = (lambda: cp.sum(cp.sqrt(cp.abs(x)) + cp.exp(-x ** 2))), 4 * n
-    elif c in ("sum_f32", "var_f32", "argmax_f32"):
+    elif c in ("sum_f32", "var_f32", "argmax_f32", "nansum_f32", "argmin_f32"):
         x = gen.normal((n,), 21)
-        f = {"sum_f32": cp.sum, "var_f32": cp.var, "argmax_f32": cp.argmax}[c]
+        f = {"sum_f32": cp.sum, "var_f32": cp.var, "argmax_f32": cp.argmax, "nansum_f32": cp.nansum,
+             "argmin_f32": cp.argmin}[c]
         fn, nb = (lambda: f(x)), 4 * n
     elif c in ("sum_axis0_f32", "sum_axis1_f32", "var_axis0_f32"):
         side = int(math.isqrt(n))

@@ -413,6 +413,56 @@ struct ArgOp {
       for (int j = 0; j < V; ++j) one(a, v[j], base + j);
     }
   }
+  // four vectors at element offsets b0, b0 + step, b0 + 2 step, b0 + 3 step
+  // (increasing): one NaN-propagating extreme of all of them, one compare
+  // with the running value, and the first-occurrence search only when it wins
+  template <int V>
+  __device__ static void vec4(Acc &a, const T (&v0)[V], const T (&v1)[V], const T (&v2)[V], const T (&v3)[V],
+                              long long b0, long long step) {
+    if constexpr (IsFloat<T>::value && sizeof(T) <= 4) {
+      float m0 = AsF<T>::f(v0[0]), m1 = AsF<T>::f(v1[0]), m2 = AsF<T>::f(v2[0]), m3 = AsF<T>::f(v3[0]);
+#pragma unroll
+      for (int j = 1; j < V; ++j) {
+        m0 = MAX ? max_nan(m0, AsF<T>::f(v0[j])) : min_nan(m0, AsF<T>::f(v0[j]));
+        m1 = MAX ? max_nan(m1, AsF<T>::f(v1[j])) : min_nan(m1, AsF<T>::f(v1[j]));
+        m2 = MAX ? max_nan(m2, AsF<T>::f(v2[j])) : min_nan(m2, AsF<T>::f(v2[j]));
+        m3 = MAX ? max_nan(m3, AsF<T>::f(v3[j])) : min_nan(m3, AsF<T>::f(v3[j]));
+      }
+      const float m = MAX ? max_nan(max_nan(m0, m1), max_nan(m2, m3)) : min_nan(min_nan(m0, m1), min_nan(m2, m3));
+      const bool mn = isnan_(m);
+      const bool take = (a.i < 0) || (!isnan_(a.v) && (mn || (MAX ? (m > a.v) : (m < a.v))));
+      if (take) {
+        long long idx = b0;
+#pragma unroll
+        for (int j = V - 1; j >= 0; --j) {  // last match in reverse order = first occurrence
+          const float x = AsF<T>::f(v3[j]);
+          if (mn ? isnan_(x) : (x == m)) idx = b0 + 3 * step + j;
+        }
+#pragma unroll
+        for (int j = V - 1; j >= 0; --j) {
+          const float x = AsF<T>::f(v2[j]);
+          if (mn ? isnan_(x) : (x == m)) idx = b0 + 2 * step + j;
+        }
+#pragma unroll
+        for (int j = V - 1; j >= 0; --j) {
+          const float x = AsF<T>::f(v1[j]);
+          if (mn ? isnan_(x) : (x == m)) idx = b0 + step + j;
+        }
+#pragma unroll
+        for (int j = V - 1; j >= 0; --j) {
+          const float x = AsF<T>::f(v0[j]);
+          if (mn ? isnan_(x) : (x == m)) idx = b0 + j;
+        }
+        a.v = m;
+        a.i = idx;
+      }
+    } else {
+      vec<V>(a, v0, b0);
+      vec<V>(a, v1, b0 + step);
+      vec<V>(a, v2, b0 + 2 * step);
+      vec<V>(a, v3, b0 + 3 * step);
+    }
+  }
   __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
     one(a, v0, i);
     one(a, v1, i + 8);
@@ -472,6 +522,30 @@ struct NanSumOp {
     } else {
 #pragma unroll
       for (int j = 0; j < V; ++j) one(a, v[j], 0);
+    }
+  }
+  // four vectors: one float partial and one count, then one double add
+  template <int V>
+  __device__ static void vec4(Acc &a, const T (&v0)[V], const T (&v1)[V], const T (&v2)[V], const T (&v3)[V],
+                              long long, long long) {
+    if constexpr (IsFloat<T>::value && sizeof(T) < 8) {
+      float s0 = 0.f, s1 = 0.f;
+      int c = 0;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float f0 = AsF<T>::f(v0[j]), f1 = AsF<T>::f(v1[j]), f2 = AsF<T>::f(v2[j]), f3 = AsF<T>::f(v3[j]);
+        const bool k0 = !isnan_(f0), k1 = !isnan_(f1), k2 = !isnan_(f2), k3 = !isnan_(f3);
+        s0 += (k0 ? f0 : 0.f) + (k1 ? f1 : 0.f);
+        s1 += (k2 ? f2 : 0.f) + (k3 ? f3 : 0.f);
+        c += (int)k0 + (int)k1 + (int)k2 + (int)k3;
+      }
+      a.s += (double)s0 + (double)s1;
+      a.c += c;
+    } else {
+      vec<V>(a, v0, 0);
+      vec<V>(a, v1, 0);
+      vec<V>(a, v2, 0);
+      vec<V>(a, v3, 0);
     }
   }
   __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
@@ -592,6 +666,17 @@ __device__ __forceinline__ typename Op::Acc block_reduce(typename Op::Acc a) {
 // vectors in flight per thread), writes its partial to scratch, and the last
 // block to take a ticket merges the partials in block order (deterministic)
 // and writes the result.  The ticket is returned to zero for the next call.
+// Ops may process the four vectors of one loop step together (vec4);
+// the others take them one by one.
+template <class Op, class = void>
+struct HasVec4 {
+  static constexpr bool value = false;
+};
+template <class Op>
+struct HasVec4<Op, decltype((void)&Op::template vec4<4>)> {
+  static constexpr bool value = true;
+};
+
 template <int OPC, class T, class L>
 __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void *out, int out_dt,
                                                  double ddof, void *scratch, unsigned *ticket,
@@ -619,10 +704,14 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
       ld.template apply<V>(r1, a1);
       ld.template apply<V>(r2, a2);
       ld.template apply<V>(r3, a3);
-      Op::template vec<V>(acc, a0, i * V);
-      Op::template vec<V>(acc, a1, (i + nth) * V);
-      Op::template vec<V>(acc, a2, (i + 2 * nth) * V);
-      Op::template vec<V>(acc, a3, (i + 3 * nth) * V);
+      if constexpr (HasVec4<Op>::value) {
+        Op::template vec4<V>(acc, a0, a1, a2, a3, i * V, nth * V);
+      } else {
+        Op::template vec<V>(acc, a0, i * V);
+        Op::template vec<V>(acc, a1, (i + nth) * V);
+        Op::template vec<V>(acc, a2, (i + 2 * nth) * V);
+        Op::template vec<V>(acc, a3, (i + 3 * nth) * V);
+      }
     }
     for (; i < nv; i += nth) {
       T a0[V];
