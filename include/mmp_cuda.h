@@ -118,6 +118,23 @@ int mmp_event_destroy(void *event);
 int mmp_event_record(void *event);
 int mmp_event_elapsed_ms(void *start, void *end, float *ms);
 
+/* ---- side streams and asynchronous copies (no counterpart in the
+ * reference: MetalBackend has one implicit queue, _metal_backend.py:341-372).
+ * They let a caller overlap host<->device copies with kernels and with
+ * each other (the copy engines of the two directions run concurrently).
+ * A NULL stream means the current device's library stream; order work
+ * across streams with events.  Memory used by work on a side stream must
+ * stay allocated until that work has finished.  Copies from / to pageable
+ * host memory are staged by the driver; pinned memory (mmp_host_alloc)
+ * runs at the full link rate. */
+int mmp_stream_create(void **stream);          /* non-blocking stream */
+int mmp_stream_destroy(void *stream);
+int mmp_stream_synchronize(void *stream);
+int mmp_stream_wait_event(void *stream, void *event);
+int mmp_event_record_on(void *event, void *stream);
+int mmp_h2d_async(void *dst, const void *src, size_t bytes, void *stream);
+int mmp_d2h_async(void *dst, const void *src, size_t bytes, void *stream);
+
 /* ---- runtime compilation (createLibraryFromString/setFunction/runFunction,
  *      _metal_backend.py:241-257): NVRTC for sm_100a, cached by source+options.
  * `options` is a '\n'-separated list.  `func` receives a launchable handle. */

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import numpy as _np
 
-from . import _cuda_backend
+from . import _cuda_backend, cuda
 from ._config import get_config, set_config
 from ._cuda_backend import CudaBackend
 from .bitwise_ops import *  # noqa: F401,F403

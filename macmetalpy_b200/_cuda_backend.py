@@ -84,6 +84,13 @@ SIGNATURES = {
                         _i64, _i64]),
     "mmp_sort": (_int, [_int, _vp, _vp, _vp, _i64, _i64]),
     "mmp_searchsorted": (_int, [_int, _vp, _i64, _vp, _i64, _int, _vp, _vp]),
+    "mmp_stream_create": (_int, [ctypes.POINTER(_vp)]),
+    "mmp_stream_destroy": (_int, [_vp]),
+    "mmp_stream_synchronize": (_int, [_vp]),
+    "mmp_stream_wait_event": (_int, [_vp, _vp]),
+    "mmp_event_record_on": (_int, [_vp, _vp]),
+    "mmp_h2d_async": (_int, [_vp, _vp, _sz, _vp]),
+    "mmp_d2h_async": (_int, [_vp, _vp, _sz, _vp]),
     "mmp_gather": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
     "mmp_scatter": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
     "mmp_compact_indices": (_int, [_vp, _vp, _i64, _i64, _vp]),

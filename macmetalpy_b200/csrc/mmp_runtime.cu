@@ -328,6 +328,66 @@ int mmp_d2d(void *dst, const void *src, size_t bytes) {
   return MMP_OK;
 }
 
+// ---- side streams, events across streams, asynchronous copies.  A NULL
+// stream argument means the current device's library stream.
+static cudaStream_t stream_or_lib(void *st) { return st ? (cudaStream_t)st : cur()->stream; }
+
+int mmp_stream_create(void **stream) {
+  if (!stream) return set_error(MMP_E_ARG, "stream is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  cudaStream_t s;
+  MMP_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = (void *)s;
+  return MMP_OK;
+}
+
+int mmp_stream_destroy(void *stream) {
+  if (stream) MMP_CUDA_TRY(cudaStreamDestroy((cudaStream_t)stream));
+  return MMP_OK;
+}
+
+int mmp_stream_synchronize(void *stream) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaStreamSynchronize(stream_or_lib(stream)));
+  return MMP_OK;
+}
+
+int mmp_stream_wait_event(void *stream, void *event) {
+  if (!event) return set_error(MMP_E_ARG, "event is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaStreamWaitEvent(stream_or_lib(stream), (cudaEvent_t)event, 0));
+  return MMP_OK;
+}
+
+int mmp_event_record_on(void *event, void *stream) {
+  if (!event) return set_error(MMP_E_ARG, "event is NULL");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaEventRecord((cudaEvent_t)event, stream_or_lib(stream)));
+  return MMP_OK;
+}
+
+int mmp_h2d_async(void *dst, const void *src, size_t bytes, void *stream) {
+  if (bytes == 0) return MMP_OK;
+  if (!dst || !src) return set_error(MMP_E_ARG, "null pointer in h2d_async");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream_or_lib(stream)));
+  return MMP_OK;
+}
+
+int mmp_d2h_async(void *dst, const void *src, size_t bytes, void *stream) {
+  if (bytes == 0) return MMP_OK;
+  if (!dst || !src) return set_error(MMP_E_ARG, "null pointer in d2h_async");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  MMP_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, stream_or_lib(stream)));
+  return MMP_OK;
+}
+
 int mmp_host_alloc(size_t bytes, void **ptr) {
   if (!ptr) return set_error(MMP_E_ARG, "ptr is NULL");
   MMP_CUDA_TRY(cudaMallocHost(ptr, bytes ? bytes : 1));

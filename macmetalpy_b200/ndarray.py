@@ -261,17 +261,44 @@ class ndarray:
 
     # ------------------------------------------------------------------ host transfer
     def get(self, stream=None, order="C", out=None) -> np.ndarray:
-        """Copy to host and return a numpy array (synchronises)."""
+        """Copy to host and return a numpy array.  Without ``stream`` it
+        synchronises; with a side stream (``macmetalpy_b200.cuda.Stream``)
+        the copy waits for the kernels enqueued so far and runs
+        asynchronously -- synchronise the stream before reading ``out``."""
         a = self._ensure_contiguous()
         host = np.empty(self._shape, dtype=self._dtype) if out is None else out
+        if out is not None and (out.shape != self._shape or out.dtype != self._dtype
+                                or not out.flags.c_contiguous):
+            raise ValueError("out must be a C-contiguous host array of this shape and dtype")
         if host.nbytes:
-            _cb.check(_cb.lib.mmp_d2h(host.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(a._ptr),
-                                      host.nbytes), "d2h")
+            if stream is None or getattr(stream, "ptr", None) is None:
+                _cb.check(_cb.lib.mmp_d2h(host.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(a._ptr),
+                                          host.nbytes), "d2h")
+            else:
+                from .cuda import Event
+                stream.wait_event(Event().record(None))
+                _cb.check(_cb.lib.mmp_d2h_async(host.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(a._ptr),
+                                                host.nbytes, ctypes.c_void_p(stream.ptr)), "d2h_async")
         return host
 
     def set(self, arr, stream=None) -> None:
-        """Copy host data into this array (broadcast to its shape)."""
+        """Copy host data into this array (broadcast to its shape).  With a
+        side stream the copy runs on it, asynchronously, and later kernels
+        wait for it; ``arr`` must then be an unchanged, C-contiguous array of
+        this shape and dtype (pinned for a copy that does not block)."""
         self._materialize_if_lazy()
+        if stream is not None and getattr(stream, "ptr", None) is not None and self._is_c_contiguous():
+            host = arr
+            if not (isinstance(host, np.ndarray) and host.shape == self._shape and host.dtype == self._dtype
+                    and host.flags.c_contiguous):
+                raise ValueError("set(stream=...) needs a C-contiguous host array of this shape and dtype")
+            if host.nbytes:
+                from .cuda import Event
+                _cb.check(_cb.lib.mmp_h2d_async(ctypes.c_void_p(self._ptr), host.ctypes.data_as(ctypes.c_void_p),
+                                                host.nbytes, ctypes.c_void_p(stream.ptr)), "h2d_async")
+                ev = Event().record(stream)
+                _cb.check(_cb.lib.mmp_stream_wait_event(None, ctypes.c_void_p(ev.ptr)), "stream wait")
+            return
         host = np.asarray(np.broadcast_to(np.asarray(arr, dtype=self._dtype), self._shape), order="C")
         if self._is_c_contiguous():
             if host.nbytes:

@@ -61,3 +61,7 @@ def test_argument_checks_fail_cleanly():
     assert cb.lib.mmp_gather(10, None, 4, None, -1, None) == -2
     assert cb.lib.mmp_scatter(10, None, -1, None, 1, None) == -2
     assert cb.lib.mmp_compact_indices(None, None, -1, 0, None) == -2
+    assert cb.lib.mmp_stream_create(None) == -2
+    assert cb.lib.mmp_stream_wait_event(None, None) == -2
+    assert cb.lib.mmp_event_record_on(None, None) == -2
+    assert cb.lib.mmp_h2d_async(None, None, 16, None) == -2

@@ -95,3 +95,33 @@ def test_zero_d_arrays_keep_their_shape():
     b = cp.array(np.float32(1.0))
     b.set(np.float32(4.0))
     assert b.shape == () and float(b.get()) == 4.0
+
+
+def test_streams_async_copies_and_pinned_memory():
+    import macmetalpy_b200 as cp
+    from macmetalpy_b200.cuda import Event, Stream, empty_pinned
+    n = 1 << 22
+    rng = np.random.default_rng(0)
+    s_in, s_out = Stream(), Stream()
+    src = empty_pinned((n,), np.float32)
+    src[...] = rng.standard_normal(n).astype(np.float32)
+    dst = empty_pinned((n,), np.float32)
+    X = cp.empty((n,), dtype=np.float32)
+    Y = cp.empty((n,), dtype=np.float32)
+    for rep in range(3):  # uploads on a side stream, kernel on the library stream, download on another
+        src[:8] = rep
+        X.set(src, stream=s_in)
+        cp.multiply(X, 2.0, out=Y)
+        Y.get(stream=s_out, out=dst)
+        s_out.synchronize()
+        np.testing.assert_array_equal(dst, src * np.float32(2))
+    e0, e1 = Event().record(), Event()
+    cp.add(X, X, out=Y)
+    e1.record()
+    e1.synchronize()
+    assert e0.elapsed_time(e1) >= 0.0
+    with pytest.raises(ValueError):
+        X.set(np.zeros(n + 1, np.float32), stream=s_in)
+    v = dst[10:20]  # a view keeps the pinned block alive
+    del dst
+    assert v.shape == (10,)
