@@ -109,7 +109,7 @@ int mmp_synchronize(void);
  * set instead of hanging or writing out of bounds: 0 = no error, 2 = scan
  * look-back wait ran out, 3 = GEMM pipeline wait ran out, 4 = sort scatter
  * offset out of range, 5 = gather / scatter / compaction offset out of
- * range. */
+ * range, 6 = the self-test wait ran out (mmp_selftest_bounded_wait). */
 int mmp_check_device_error(int *code);
 
 /* ---- timing */
@@ -225,6 +225,13 @@ int mmp_scatter(int dtype, void *dst, int64_t limit, const int64_t *offsets,
  * flatnonzero). */
 int mmp_compact_indices(const void *mask, const int64_t *incl, int64_t n,
                         int64_t count, int64_t *out);
+
+/* Self-test of the failure behaviour of waiting kernels (no counterpart in
+ * the reference): one kernel waits on a device flag that nothing sets, gives
+ * up after timeout_us of device time, sets device error 6 and returns; the
+ * next mmp_check_device_error reports 6 and the context stays usable.
+ * `polls` (may be NULL) receives the number of polls made. */
+int mmp_selftest_bounded_wait(int timeout_us, unsigned *polls);
 
 #ifdef __cplusplus
 }

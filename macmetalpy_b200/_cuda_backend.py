@@ -91,6 +91,7 @@ SIGNATURES = {
     "mmp_event_record_on": (_int, [_vp, _vp]),
     "mmp_h2d_async": (_int, [_vp, _vp, _sz, _vp]),
     "mmp_d2h_async": (_int, [_vp, _vp, _sz, _vp]),
+    "mmp_selftest_bounded_wait": (_int, [_int, ctypes.POINTER(ctypes.c_uint)]),
     "mmp_gather": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
     "mmp_scatter": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
     "mmp_compact_indices": (_int, [_vp, _vp, _i64, _i64, _vp]),

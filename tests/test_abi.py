@@ -65,3 +65,4 @@ def test_argument_checks_fail_cleanly():
     assert cb.lib.mmp_stream_wait_event(None, None) == -2
     assert cb.lib.mmp_event_record_on(None, None) == -2
     assert cb.lib.mmp_h2d_async(None, None, 16, None) == -2
+    assert cb.lib.mmp_selftest_bounded_wait(0, None) == -2
