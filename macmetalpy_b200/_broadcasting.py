@@ -15,6 +15,15 @@ def broadcast_shapes(*shapes: tuple) -> tuple:
     """Broadcast shape of ``shapes``; ``ValueError`` if incompatible."""
     if not shapes:
         return ()
+    first = None
+    for s in shapes:  # fast path: every non-scalar shape equal
+        if s:
+            if first is None:
+                first = s
+            elif s != first:
+                break
+    else:
+        return tuple(first) if first is not None else ()
     ndim = max(len(s) for s in shapes)
     out = []
     for axis in range(-ndim, 0):

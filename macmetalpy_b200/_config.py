@@ -36,7 +36,8 @@ class MacMetalConfig:
 
 def get_config() -> MacMetalConfig:
     """Return the global configuration singleton."""
-    return MacMetalConfig()
+    inst = MacMetalConfig._instance  # fast path: no lock once created
+    return inst if inst is not None else MacMetalConfig()
 
 
 def set_config(

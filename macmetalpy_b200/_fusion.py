@@ -384,35 +384,40 @@ class _Plan:
         self.inputs = []  # list of ndarray views (dedup)
         self.input_key = {}
         self.scalars = []  # ScalarNode list
+        self.topo = []  # per node, its part of the code key (built during the walk)
         self._visit(root)
         self.vec = vec
         self._layout()
 
     def _visit(self, node):
         nid = id(node)
-        if nid in self.ids:
-            return self.ids[nid]
+        idx = self.ids.get(nid)
+        if idx is not None:
+            return idx
         if isinstance(node, InputNode):
             a = node._array
-            key = (a._ptr, a._shape, a._strides, a._dtype.str)
-            if key not in self.input_key:
-                self.input_key[key] = len(self.inputs)
+            key = (a._ptr, a._shape, a._strides, a._dtype)
+            slot = self.input_key.get(key)
+            if slot is None:
+                slot = self.input_key[key] = len(self.inputs)
                 self.inputs.append(a)
+            t = ("in", slot, node._dtype)
         elif isinstance(node, ScalarNode):
+            t = ("sc", len(self.scalars), node._dtype)
             self.scalars.append(node)
-        elif isinstance(node, (UnaryOpNode, CastNode)):
-            self._visit(node._input)
+        elif isinstance(node, UnaryOpNode):
+            t = ("un", node._op_name, node._dtype, node._in_dtype, self._visit(node._input))
+        elif isinstance(node, CastNode):
+            t = ("cast", node._dtype, self._visit(node._input))
         elif isinstance(node, BinaryOpNode):
-            self._visit(node._lhs)
-            self._visit(node._rhs)
+            t = ("bin", node._op_name, node._dtype, node._in_dtype, self._visit(node._lhs), self._visit(node._rhs))
         elif isinstance(node, SelectNode):
-            self._visit(node._cond)
-            self._visit(node._x)
-            self._visit(node._y)
+            t = ("sel", node._dtype, self._visit(node._cond), self._visit(node._x), self._visit(node._y))
         else:
             raise TypeError(f"Unknown node type: {type(node)}")
         idx = len(self.order)
         self.order.append(node)
+        self.topo.append(t)
         self.ids[nid] = idx
         return idx
 
@@ -457,27 +462,8 @@ class _Plan:
 
     # -- identity of the generated code (not of the data)
     def key(self):
-        topo = []
-        for node in self.order:
-            if isinstance(node, InputNode):
-                a = node._array
-                k = (a._ptr, a._shape, a._strides, a._dtype.str)
-                topo.append(("in", self.input_key[k], node._dtype.str))
-            elif isinstance(node, ScalarNode):
-                topo.append(("sc", self.scalars.index(node), node._dtype.str))
-            elif isinstance(node, UnaryOpNode):
-                topo.append(("un", node._op_name, node._dtype.str, node._in_dtype.str,
-                             self.ids[id(node._input)]))
-            elif isinstance(node, CastNode):
-                topo.append(("cast", node._dtype.str, self.ids[id(node._input)]))
-            elif isinstance(node, SelectNode):
-                topo.append(("sel", node._dtype.str, self.ids[id(node._cond)], self.ids[id(node._x)],
-                             self.ids[id(node._y)]))
-            else:
-                topo.append(("bin", node._op_name, node._dtype.str, node._in_dtype.str,
-                             self.ids[id(node._lhs)], self.ids[id(node._rhs)]))
-        kinds = tuple((k, a._dtype.str) for k, a in zip(self.kinds, self.inputs))
-        return (tuple(topo), kinds, self.nd if self.strided else 0, self.idx64, self.vec,
+        kinds = tuple((k, a._dtype) for k, a in zip(self.kinds, self.inputs))
+        return (tuple(self.topo), kinds, self.nd if self.strided else 0, self.idx64, self.vec,
                 bool(get_config().fast_math))
 
 
@@ -530,7 +516,7 @@ def _emit_loader(plan: _Plan) -> tuple[str, list[str]]:
         names[id(node)] = nm
         if isinstance(node, InputNode):
             a = node._array
-            k = plan.input_key[(a._ptr, a._shape, a._strides, a._dtype.str)]
+            k = plan.input_key[(a._ptr, a._shape, a._strides, a._dtype)]
             lines.append(f"    const {t} {nm} = a{k};")
         elif isinstance(node, ScalarNode):
             lines.append(f"    const {t} {nm} = sc{plan.scalars.index(node)};")
@@ -854,7 +840,7 @@ def _loader_args(plan: _Plan) -> list:
 
 
 def _launch(fn, grid, args, block=_BLOCK):
-    arr = (ctypes.c_void_p * len(args))(*[ctypes.cast(ctypes.pointer(x), ctypes.c_void_p) for x in args])
+    arr = (ctypes.c_void_p * len(args))(*[ctypes.addressof(x) for x in args])
     g = (ctypes.c_uint * 3)(int(grid[0]), int(grid[1]) if len(grid) > 1 else 1,
                              int(grid[2]) if len(grid) > 2 else 1)
     b = (ctypes.c_uint * 3)(int(block), 1, 1)

@@ -57,7 +57,10 @@ def _c_contiguous_strides(shape) -> Tuple[int, ...]:
 # dtype resolution of elementwise ops (numpy ufunc rules + resolve_dtype)
 # ---------------------------------------------------------------------------
 
+from ._config import get_config  # noqa: E402
+
 _RES_CACHE: dict = {}
+_STRIDES_CACHE: dict = {}
 
 
 def _operand_spec(x):
@@ -80,8 +83,6 @@ def _operand_spec(x):
 
 def _resolve(op_name: str, specs: tuple):
     """(loop_dtype, out_dtype) for an elementwise op after resolve_dtype."""
-    from ._config import get_config
-
     cfg = get_config()
     key = (op_name, specs, cfg.float64_behavior, cfg.default_float_dtype)
     r = _RES_CACHE.get(key)
@@ -130,9 +131,14 @@ class ndarray:
     def _lazy(cls, node) -> "ndarray":
         a = cls.__new__(cls)
         a._buffer = None
-        a._shape = tuple(node._shape)
+        a._shape = shp = tuple(node._shape)
         a._dtype = node._dtype
-        a._strides = _c_contiguous_strides(a._shape)
+        st = _STRIDES_CACHE.get(shp)
+        if st is None:
+            if len(_STRIDES_CACHE) > 4096:
+                _STRIDES_CACHE.clear()
+            st = _STRIDES_CACHE[shp] = _c_contiguous_strides(shp)
+        a._strides = st
         a._offset = 0
         a._base = None
         a._fusion_node = node
@@ -556,8 +562,8 @@ class ndarray:
     def _to_node(x, target_dtype, shape_hint=None):
         """Node for operand ``x`` cast to ``target_dtype``."""
         if isinstance(x, ndarray):
-            node = x._node()
-        elif isinstance(x, (numbers.Number, np.generic)) and np.ndim(x) == 0:
+            node = x._fusion_node if x._fusion_node is not None else _fu.InputNode(x)
+        elif isinstance(x, (numbers.Number, np.generic)):
             return _fu.ScalarNode(x, target_dtype)
         else:
             node = ndarray._from_numpy(np.asarray(x))._node()
@@ -567,12 +573,29 @@ class ndarray:
 
     @staticmethod
     def _elementwise(op_name: str, *operands) -> "ndarray":
-        ops = [o if isinstance(o, (ndarray, numbers.Number, np.generic)) else ndarray._from_numpy(np.asarray(o))
-               for o in operands]
-        specs = tuple(_operand_spec(o) for o in ops)
-        loop, out = _resolve(op_name, specs)
-        shapes = [o._shape if isinstance(o, ndarray) else () for o in ops]
-        shape = broadcast_shapes(*shapes)
+        ops = []
+        specs = []
+        shape = None
+        same = True
+        for o in operands:
+            if isinstance(o, ndarray):
+                specs.append(o._dtype)
+            elif isinstance(o, (numbers.Number, np.generic)):
+                specs.append(_operand_spec(o))
+            else:
+                o = ndarray._from_numpy(np.asarray(o))
+                specs.append(o._dtype)
+            if isinstance(o, ndarray):
+                if shape is None:
+                    shape = o._shape
+                elif o._shape != shape:
+                    same = False
+            ops.append(o)
+        loop, out = _resolve(op_name, tuple(specs))
+        if shape is None:
+            shape = ()
+        elif not same:
+            shape = broadcast_shapes(*[o._shape if isinstance(o, ndarray) else () for o in ops])
         nodes = [ndarray._to_node(o, loop) for o in ops]
         # flush operands whose graphs would exceed the reference's depth cap
         for i, (o, nd) in enumerate(zip(ops, nodes)):

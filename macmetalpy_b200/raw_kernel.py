@@ -65,7 +65,7 @@ class RawKernel:
         g = [(grid[i] + blk[i] - 1) // blk[i] if i < len(grid) else 1 for i in range(3)]
         cargs = [self._arg(a) for a in args]
         ptrs = (ctypes.c_void_p * max(len(cargs), 1))(
-            *[ctypes.cast(ctypes.pointer(x), ctypes.c_void_p) for x in cargs])
+            *[ctypes.addressof(x) for x in cargs])
         gg = (ctypes.c_uint * 3)(*g)
         bb = (ctypes.c_uint * 3)(*blk)
         _cb.check(_cb.lib.mmp_launch(ctypes.c_void_p(self.kernel), gg, bb, int(shared_mem), ptrs), "RawKernel")
