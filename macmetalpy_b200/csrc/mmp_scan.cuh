@@ -12,9 +12,10 @@
 // Rows of a (rows, k) view are cut into tiles of STILE = 4096 elements
 // (256 threads x 16).  Each block
 // takes the next tile id from a global counter (so every lower tile is
-// already running), scans its tile in registers and shared memory, publishes
-// the tile aggregate, looks back over its predecessors within the same row
-// (decoupled look-back) until it meets a published inclusive prefix, then
+// already running), reduces its tile (one barrier) and publishes the tile
+// aggregate at once, then looks back over its predecessors within the same row
+// (decoupled look-back, warp 0, while the other warps compute their
+// tile-local prefixes) until it meets a published inclusive prefix, then
 // publishes its own inclusive prefix and writes its outputs: one read and
 // one write of the data, one launch.  Every wait is bounded; a wait that
 // runs out sets the device error word and the block carries on, so a fault
@@ -175,29 +176,29 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
       v[e] = (i < count) ? to_local<A, T>(x[start + i]) : Op::template id<A>();
     }
   }
+  // ---- the tile aggregate first, so that it is published as early as
+  // possible: thread totals, their warp-inclusive prefixes, one barrier
+  A tot = v[0];
 #pragma unroll
-  for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
-  // ---- exclusive scan of the thread totals across the block
-  A tot = v[SITEMS - 1];
+  for (int e = 1; e < SITEMS; ++e) tot = Op::op(tot, v[e]);
   A inc = tot;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
     A o = __shfl_up_sync(0xffffffffu, inc, d);
     if (lane >= d) inc = Op::op(o, inc);
   }
-  if (lane == 31) s_warp[w] = inc;
+  if (lane == 31) s_warp[w] = inc;  // warp totals
   __syncthreads();
-  if (w == 0) {
-    A wv = (lane < SBLOCK / 32) ? s_warp[lane] : Op::template id<A>();
+  // every warp folds the warp totals itself: its exclusive prefix and the
+  // tile aggregate (no second barrier)
+  A warp_excl = Op::template id<A>();
+  A tile_agg = Op::template id<A>();
 #pragma unroll
-    for (int d = 1; d < SBLOCK / 32; d <<= 1) {
-      A o = __shfl_up_sync(0xffffffffu, wv, d);
-      if (lane >= d) wv = Op::op(o, wv);
-    }
-    if (lane < SBLOCK / 32) s_warp[lane] = wv;  // inclusive warp prefixes
+  for (int q = 0; q < SBLOCK / 32; ++q) {
+    const A t = s_warp[q];
+    if (q < w) warp_excl = Op::op(warp_excl, t);
+    tile_agg = Op::op(tile_agg, t);
   }
-  __syncthreads();
-  A warp_excl = (w > 0) ? s_warp[w - 1] : Op::template id<A>();
   // inc is the inclusive prefix of thread totals within the warp; the
   // exclusive prefix is the neighbour's inclusive one.
   A thread_excl;
@@ -206,7 +207,6 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     A wexcl_in_warp = (lane == 0) ? Op::template id<A>() : o;
     thread_excl = Op::op(warp_excl, wexcl_in_warp);
   }
-  const A tile_agg = s_warp[SBLOCK / 32 - 1];
 
   // ---- decoupled look-back over earlier tiles of the same row
   if (w == 0) {
@@ -247,16 +247,18 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     }
     if (lane == 0) s_excl = excl;
   }
+  // ---- tile-local inclusive prefixes; warps 1.. do this while warp 0 is
+  // still looking back
+  v[0] = Op::op(thread_excl, v[0]);
+#pragma unroll
+  for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
   __syncthreads();
   const C excl = s_excl;
 
   // ---- outputs: carry (C) + tile-local prefix (A)
   O res[SITEMS];
 #pragma unroll
-  for (int e = 0; e < SITEMS; ++e) {
-    A loc = Op::op(thread_excl, v[e]);
-    res[e] = cvt<O>(Op::op(excl, (C)loc));
-  }
+  for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
   if (full_vec) {
     // stage the outputs through shared memory, write 16-byte vectors
     O *smO = reinterpret_cast<O *>(s_stage);
