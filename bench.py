@@ -438,7 +438,7 @@ CASES = ("add_f32", "floor_divide_f32", "mod_f32", "logaddexp_f32", "add_i32", "
          "sum_axis0_f32", "sum_axis1_f32",
          "var_axis0_f32",
          "cumsum_i32", "cumsum_f32", "cumsum_axis1_f32", "matmul_f32", "matmul_f16", "sort_f32", "argsort_f32",
-         "searchsorted_f32")
+         "searchsorted_f32", "count_nonzero_gt_f32")
 
 
 def run_case(args):
@@ -497,6 +497,9 @@ def run_case(args):
         x = gen.normal((n,), 21)
         f = cp.sort if c == "sort_f32" else cp.argsort
         fn, nb = (lambda: f(x)), n
+    elif c == "count_nonzero_gt_f32":
+        x = gen.normal((n,), 21)
+        fn, nb = (lambda: cp.count_nonzero(x > 0)), 4 * n
     elif c == "searchsorted_f32":
         a = cp.sort(gen.normal((1 << 20,), 22))
         x = gen.normal((n,), 21)

@@ -135,6 +135,13 @@ struct SumLike {
 #pragma unroll
       for (int j = 0; j < V; ++j) s += AsF<T>::f(v[j]);
       a += (Acc)s;
+    } else if (!IsFloat<T>::value && sizeof(T) <= 2 && V <= 8) {
+      // bool / 8- and 16-bit integers: a vector's sum fits 32 bits, one
+      // 64-bit add per vector instead of one per element
+      int s = 0;
+#pragma unroll
+      for (int j = 0; j < V; ++j) s += (int)ar(v[j]);
+      a += (Acc)s;
     } else {
 #pragma unroll
       for (int j = 0; j < V; ++j) a += (Acc)ar(v[j]);
