@@ -65,6 +65,8 @@ int set_stage_smem() {
   if (!done) {
     MMP_CUDA_TRY(cudaFuncSetAttribute(scan_tiles_kernel<T, O, PROD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       StageSize<T, O>()));
+    MMP_CUDA_TRY(cudaFuncSetAttribute(scan_tiles_carry_kernel<T, O, PROD>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, StageSize<T, O>()));
     done = true;
   }
   return MMP_OK;
@@ -72,11 +74,51 @@ int set_stage_smem() {
 
 }  // namespace
 
+// Rows of at least kLongRowTiles tiles, in scans of at least
+// kLongRowElements elements, take the reduce-then-scan path
+// (tile_aggregates_kernel, a scan of the aggregates, scan_tiles_carry_kernel)
+// instead of the look-back kernel, whose chain of waits grows with the row.
+// Measured on B200: int32 -> int64 over 2^30 elements 4.6 TB/s against
+// 3.5 TB/s, float32 4.3 against 3.5; rows of 16 tiles (4096 x 65536) and
+// scans below ~2^24 elements (three launches, a pool allocation) stay
+// faster on the look-back kernel.
+constexpr long long kLongRowTiles = 64;
+constexpr long long kLongRowElements = 1ll << 24;
+
 template <int PRODI, class T>
 struct ScanRun {
+  typedef typename ScanOut<T>::type O;
+  typedef typename ScanTypes<T>::carry_t CT;
+
+  static int long_rows(const T *x, O *y, long long rows, long long k, long long tpr, long long total,
+                       const CT *cin, int vec_ok) {
+    constexpr bool PROD = PRODI != 0;
+    cudaStream_t st = stream();
+    CT *agg = nullptr;
+    MMP_CUDA_TRY(cudaMallocAsync((void **)&agg, (size_t)total * 2 * sizeof(CT), st));
+    CT *incl = agg + total;
+    long long blocks = (total * 32 + SBLOCK - 1) / SBLOCK;
+    const long long maxb = (long long)sm_count() * 8;
+    tile_aggregates_kernel<T, PROD><<<(unsigned)(blocks < maxb ? blocks : maxb), SBLOCK, 0, st>>>(
+        x, k, tpr, total, agg, vec_ok);
+    cudaError_t e = cudaGetLastError();
+    int rc = e == cudaSuccess ? MMP_OK : cuda_error(e, "tile_aggregates_kernel");
+    // the aggregates are scanned per row by this same library (CT is its
+    // own accumulation type), with the caller's carry
+    if (!rc) rc = ScanRun<PRODI, CT>::run(agg, ScanOut<CT>::code, incl, rows, tpr, 1, cin);
+    if (!rc) rc = set_stage_smem<T, O, PROD>();
+    if (!rc) {
+      scan_tiles_carry_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, StageSize<T, O>(), st>>>(
+          x, y, rows, k, tpr, total, incl, cin, vec_ok);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) rc = cuda_error(e, "scan_tiles_carry_kernel");
+    }
+    cudaFreeAsync(agg, st);
+    return rc;
+  }
+
   static int run(const void *xv, int out_dt, void *yv, long long outer, long long k, long long inner,
                  const void *carry) {
-    typedef typename ScanOut<T>::type O;
     constexpr bool PROD = PRODI != 0;
     if (out_dt != ScanOut<T>::code)
       return set_error(MMP_E_ARG, "scan output dtype must be the numpy accumulation type");
@@ -84,7 +126,6 @@ struct ScanRun {
     if (!st) return set_error(MMP_E_CUDA, "no stream");
     const T *x = (const T *)xv;
     O *y = (O *)yv;
-    typedef typename ScanTypes<T>::carry_t CT;
     const CT *cin = (const CT *)carry;
     const int sms = sm_count();
     if (inner > 1) {
@@ -108,6 +149,8 @@ struct ScanRun {
     long long tpr = (k + STILE - 1) / STILE;
     long long total = rows * tpr;
     if (total > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
+    int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
+    if (tpr >= kLongRowTiles && rows * k >= kLongRowElements) return long_rows(x, y, rows, k, tpr, total, cin, vec_ok);
     void *desc;
     unsigned *counter, epoch;
     int rc = scan_state(total, &desc, &counter, &epoch);
@@ -115,7 +158,6 @@ struct ScanRun {
     typedef typename ScanTypes<T>::carry_t C;
     TileState<C> ts;
     ts.desc = (TileDesc<C> *)desc;
-    int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
     rc = set_stage_smem<T, O, PROD>();
     if (rc) return rc;
     scan_tiles_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, StageSize<T, O>(), st>>>(

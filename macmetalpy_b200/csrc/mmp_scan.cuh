@@ -21,9 +21,11 @@
 // runs out sets the device error word and the block carries on, so a fault
 // shows up as an error from mmp_check_device_error, never as a hang.
 //
-// Float inputs are scanned inside a tile in f32 and carried between tiles in
-// f64, so the error stays near the f32 rounding of each output instead of
-// growing with the prefix length.
+// Float inputs are summed in f32 only over a thread's own 16 consecutive
+// elements; every total across threads, tile aggregate and carry is f64, so
+// the error does not grow with the prefix length (with values of both signs
+// too, where f32 rounding of tile aggregates would add up across tiles): it
+// stays within a few f32 roundings of the 16-element local sums.
 #pragma once
 #include "mmp_device.cuh"
 
@@ -125,8 +127,16 @@ constexpr int StageSize() {
   return StageBytes<T>::value > StageBytes<O>::value ? StageBytes<T>::value : StageBytes<O>::value;
 }
 
+// Resident blocks per SM the tile kernels are compiled for: the look-back
+// kernel's speed follows the number of tiles in flight (each waits on its
+// look-back), so float inputs (f32 locals, 17 KB of staging) keep 6 blocks
+// per SM, other 4-byte and smaller inputs 4, 8-byte inputs 2.
+template <class T> struct LookbackMinBlocks { static constexpr int value = sizeof(T) >= 8 ? 2 : 4; };
+template <> struct LookbackMinBlocks<float> { static constexpr int value = 6; };
+template <> struct LookbackMinBlocks<__half> { static constexpr int value = 6; };
+
 template <class T, class O, bool PROD>
-__global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
+__global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tiles_kernel(
     const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tiles_per_row,
     long long total_tiles, TileState<typename ScanTypes<T>::carry_t> st, unsigned *tile_counter,
     unsigned epoch, int *err, const typename ScanTypes<T>::carry_t *carry_in, int vec_ok) {
@@ -134,7 +144,7 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
   typedef typename ScanTypes<T>::carry_t C;
   typedef ScanOp<PROD> Op;
   __shared__ long long s_tile;
-  __shared__ A s_warp[SBLOCK / 32];
+  __shared__ C s_warp[SBLOCK / 32];
   __shared__ C s_excl;
   extern __shared__ __align__(16) unsigned char s_stage[];  // StageSize<T, O>() bytes
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -177,34 +187,35 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     }
   }
   // ---- the tile aggregate first, so that it is published as early as
-  // possible: thread totals, their warp-inclusive prefixes, one barrier
-  A tot = v[0];
+  // possible: thread totals, their warp-inclusive prefixes, one barrier.
+  // Everything across threads is in the carry type C (float64 for float
+  // inputs): only a thread's own SITEMS elements are summed in A.
 #pragma unroll
-  for (int e = 1; e < SITEMS; ++e) tot = Op::op(tot, v[e]);
-  A inc = tot;
+  for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);  // thread-local prefixes
+  C inc = (C)v[SITEMS - 1];
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
-    A o = __shfl_up_sync(0xffffffffu, inc, d);
+    C o = __shfl_up_sync(0xffffffffu, inc, d);
     if (lane >= d) inc = Op::op(o, inc);
   }
   if (lane == 31) s_warp[w] = inc;  // warp totals
   __syncthreads();
   // every warp folds the warp totals itself: its exclusive prefix and the
   // tile aggregate (no second barrier)
-  A warp_excl = Op::template id<A>();
-  A tile_agg = Op::template id<A>();
+  C warp_excl = Op::template id<C>();
+  C tile_agg = Op::template id<C>();
 #pragma unroll
   for (int q = 0; q < SBLOCK / 32; ++q) {
-    const A t = s_warp[q];
+    const C t = s_warp[q];
     if (q < w) warp_excl = Op::op(warp_excl, t);
     tile_agg = Op::op(tile_agg, t);
   }
   // inc is the inclusive prefix of thread totals within the warp; the
   // exclusive prefix is the neighbour's inclusive one.
-  A thread_excl;
+  C thread_excl;
   {
-    A o = __shfl_up_sync(0xffffffffu, inc, 1);
-    A wexcl_in_warp = (lane == 0) ? Op::template id<A>() : o;
+    C o = __shfl_up_sync(0xffffffffu, inc, 1);
+    C wexcl_in_warp = (lane == 0) ? Op::template id<C>() : o;
     thread_excl = Op::op(warp_excl, wexcl_in_warp);
   }
 
@@ -214,9 +225,9 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
     const unsigned long long ep2 = (unsigned long long)ep << 2;
     if (j == 0) {
       if (carry_in && rows == 1) excl = (C)(*carry_in);
-      if (lane == 0) desc_store(st.desc + tile, Op::op(excl, (C)tile_agg), ep2 | 2ull);
+      if (lane == 0) desc_store(st.desc + tile, Op::op(excl, tile_agg), ep2 | 2ull);
     } else {
-      if (lane == 0) desc_store(st.desc + tile, (C)tile_agg, ep2 | 1ull);
+      if (lane == 0) desc_store(st.desc + tile, tile_agg, ep2 | 1ull);
       const long long row_first = row * tiles_per_row;
       long long look = tile - 1;  // highest tile id still to fold in
       bool done = false;
@@ -243,22 +254,17 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
         if (m) done = true;
         else look -= 32;
       }
-      if (lane == 0) desc_store(st.desc + tile, Op::op(excl, (C)tile_agg), ep2 | 2ull);
+      if (lane == 0) desc_store(st.desc + tile, Op::op(excl, tile_agg), ep2 | 2ull);
     }
     if (lane == 0) s_excl = excl;
   }
-  // ---- tile-local inclusive prefixes; warps 1.. do this while warp 0 is
-  // still looking back
-  v[0] = Op::op(thread_excl, v[0]);
-#pragma unroll
-  for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
   __syncthreads();
-  const C excl = s_excl;
+  const C base = Op::op(s_excl, thread_excl);
 
-  // ---- outputs: carry (C) + tile-local prefix (A)
+  // ---- outputs: carry and thread prefix (C) + thread-local prefix (A)
   O res[SITEMS];
 #pragma unroll
-  for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
+  for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(base, (C)v[e]));
   if (full_vec) {
     // stage the outputs through shared memory, write 16-byte vectors
     O *smO = reinterpret_cast<O *>(s_stage);
@@ -284,6 +290,158 @@ __global__ void __launch_bounds__(SBLOCK) scan_tiles_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Reduce-then-scan for long rows.  The look-back chain makes every tile wait
+// for the slowest aggregate published before it (a tile whose loads came
+// back late holds up all later tiles), which caps the look-back kernel near
+// half of HBM bandwidth once a row has hundreds of tiles.  Long rows
+// therefore take three launches without any wait between tiles:
+//   1. tile_aggregates_kernel: one warp per tile sums (or multiplies) its
+//      STILE elements into the tile aggregate (no barriers);
+//   2. the library's own scan of the aggregates, per row, with the carry;
+//   3. scan_tiles_carry_kernel: every tile scans itself with its exclusive
+//      prefix (the inclusive aggregate prefix of the tile before it), in
+//      reverse tile order so that the tail of the input, the part the first
+//      launch read last, is still in L2.
+// Bytes moved: 2 reads and 1 write of the data (16 per int32 element
+// instead of 12), all at streaming speed.
+
+template <class T, bool PROD>
+__global__ void __launch_bounds__(SBLOCK) tile_aggregates_kernel(const T *__restrict__ x, long long k,
+                                                                 long long tiles_per_row, long long total_tiles,
+                                                                 typename ScanTypes<T>::carry_t *__restrict__ agg,
+                                                                 int vec_ok) {
+  typedef typename ScanTypes<T>::local_t A;
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> Op;
+  constexpr int VE = 16 / sizeof(T);          // elements per 16-byte load
+  constexpr int NVT = STILE / (32 * VE);      // loads per lane per tile
+  constexpr int BATCH = 8;                    // loads in flight per lane
+  static_assert(NVT % BATCH == 0, "whole batches per tile");
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = ((long long)gridDim.x * SBLOCK) >> 5;
+  for (long long t = ((long long)blockIdx.x * SBLOCK + threadIdx.x) >> 5; t < total_tiles; t += nwarps) {
+    const long long row = t / tiles_per_row;
+    const long long j = t - row * tiles_per_row;
+    const long long start = row * k + j * STILE;
+    long long count = k - j * STILE;
+    if (count > STILE) count = STILE;
+    C acc = Op::template id<C>();  // float64 for float inputs
+    if (vec_ok && count == STILE) {
+      const T *p = x + start + lane * VE;
+#pragma unroll 1
+      for (int q = 0; q < NVT; q += BATCH) {
+        Vec<T, VE> b[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) b[u] = ldvec<T, VE>(p + (long long)(q + u) * 32 * VE);
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u)
+#pragma unroll
+          for (int e = 0; e < VE; ++e) acc = Op::op(acc, (C)to_local<A, T>(b[u].v[e]));
+      }
+    } else {
+      for (long long i = lane; i < count; i += 32) acc = Op::op(acc, (C)to_local<A, T>(x[start + i]));
+    }
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) acc = Op::op(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    if (lane == 0) agg[t] = acc;
+  }
+}
+
+// Tile scan with a known exclusive prefix: incl holds, per row, the
+// inclusive scan of the tile aggregates (carry included), so tile j > 0 of
+// a row starts from incl[tile - 1].  One block per tile, highest tile first.
+template <class T, class O, bool PROD>
+__global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tiles_carry_kernel(
+    const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tiles_per_row,
+    long long total_tiles, const typename ScanTypes<T>::carry_t *__restrict__ incl,
+    const typename ScanTypes<T>::carry_t *carry_in, int vec_ok) {
+  typedef typename ScanTypes<T>::local_t A;
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> Op;
+  __shared__ C s_warp[SBLOCK / 32];
+  extern __shared__ __align__(16) unsigned char s_stage[];  // StageSize<T, O>() bytes
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const long long tile = total_tiles - 1 - (long long)blockIdx.x;
+  const long long row = tile / tiles_per_row;
+  const long long j = tile - row * tiles_per_row;
+  const long long start = row * k + j * STILE;
+  long long count = k - j * STILE;
+  if (count > STILE) count = STILE;
+  C excl = Op::template id<C>();
+  if (j > 0) excl = incl[tile - 1];
+  else if (carry_in && rows == 1) excl = (C)(*carry_in);
+
+  // ---- load: coalesced 16-byte vectors through padded shared memory to
+  // SITEMS consecutive elements per thread (as in scan_tiles_kernel)
+  A v[SITEMS];
+  const long long my0 = (long long)tid * SITEMS;
+  const bool full_vec = vec_ok && count == STILE;
+  if (full_vec) {
+    T *smT = reinterpret_cast<T *>(s_stage);
+    constexpr int VE = (16 / sizeof(T)) < SITEMS ? (16 / sizeof(T)) : SITEMS;
+#pragma unroll
+    for (int q = 0; q < SITEMS / VE; ++q) {
+      const int i0 = (q * SBLOCK + tid) * VE;
+      Vec<T, VE> t = ldvec_stream<T, VE>(x + start + i0);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) smT[spad<T>(i0 + e)] = t.v[e];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) v[e] = to_local<A, T>(smT[spad<T>(tid * SITEMS + e)]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) {
+      long long i = my0 + e;
+      v[e] = (i < count) ? to_local<A, T>(x[start + i]) : Op::template id<A>();
+    }
+  }
+  // ---- thread-local prefixes (A), then thread totals scanned across the
+  // tile in C (float64 for float inputs), one barrier
+#pragma unroll
+  for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
+  C inc = (C)v[SITEMS - 1];
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    C o = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc = Op::op(o, inc);
+  }
+  if (lane == 31) s_warp[w] = inc;
+  __syncthreads();  // also: every thread has read its staged inputs
+  C warp_excl = Op::template id<C>();
+#pragma unroll
+  for (int q = 0; q < SBLOCK / 32; ++q)
+    if (q < w) warp_excl = Op::op(warp_excl, s_warp[q]);
+  {
+    C o = __shfl_up_sync(0xffffffffu, inc, 1);
+    excl = Op::op(excl, Op::op(warp_excl, (lane == 0) ? Op::template id<C>() : o));
+  }
+
+  // ---- outputs: carry and thread prefix (C) + thread-local prefix (A)
+  if (full_vec) {
+    O *smO = reinterpret_cast<O *>(s_stage);
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) smO[spad<O>(tid * SITEMS + e)] = cvt<O>(Op::op(excl, (C)v[e]));
+    __syncthreads();
+    constexpr int VO = (16 / sizeof(O)) < SITEMS ? (16 / sizeof(O)) : SITEMS;
+#pragma unroll
+    for (int q = 0; q < SITEMS / VO; ++q) {
+      const int i0 = (q * SBLOCK + tid) * VO;
+      Vec<O, VO> t;
+#pragma unroll
+      for (int e = 0; e < VO; ++e) t.v[e] = smO[spad<O>(i0 + e)];
+      stvec_stream<O, VO>(y + start + i0, t);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) {
+      long long i = my0 + e;
+      if (i < count) y[start + i] = cvt<O>(Op::op(excl, (C)v[e]));
+    }
+  }
+}
+
 // One warp per row for short rows (k < STILE / 4).
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,
@@ -300,15 +458,14 @@ __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restr
     if (carry_in && rows == 1) carry = (C)(*carry_in);
     for (long long c0 = 0; c0 < k; c0 += 32) {
       long long i = c0 + lane;
-      A v = (i < k) ? to_local<A, T>(x[r * k + i]) : Op::template id<A>();
+      C v = (i < k) ? (C)to_local<A, T>(x[r * k + i]) : Op::template id<C>();
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
-        A o = __shfl_up_sync(0xffffffffu, v, d);
+        C o = __shfl_up_sync(0xffffffffu, v, d);
         if (lane >= d) v = Op::op(o, v);
       }
-      if (i < k) y[r * k + i] = cvt<O>(Op::op(carry, (C)v));
-      A last = __shfl_sync(0xffffffffu, v, 31);
-      carry = Op::op(carry, (C)last);
+      if (i < k) y[r * k + i] = cvt<O>(Op::op(carry, v));
+      carry = Op::op(carry, __shfl_sync(0xffffffffu, v, 31));
     }
   }
 }

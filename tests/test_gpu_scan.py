@@ -1,6 +1,7 @@
 """cumsum / cumprod vs the oracle: int32 -> int64 bit-exact across tile
 boundaries (4096-element tiles), float32 within 1e-4 of the float64 scan,
-row (axis=-1) and column (axis=0) scans, carry-in."""
+row (axis=-1) and column (axis=0) scans, the look-back kernel and the
+reduce-then-scan path for long rows, carry-in."""
 
 import numpy as np
 import pytest
@@ -86,3 +87,61 @@ def test_repeated_calls_reuse_state(cp):
     for _ in range(5):
         np.testing.assert_array_equal(cp.cumsum(X).get(), want)
     cp.synchronize()
+
+
+# Rows of at least 64 tiles in scans of at least 2^24 elements take the
+# reduce-then-scan path (tile aggregates, a scan of the aggregates, tile
+# scans with known carries).  Full-range int32 keeps the int64 carries exact;
+# odd k takes the unaligned (scalar) tile path; a ragged last tile per row.
+@pytest.mark.parametrize("rows,k", [(1, 1 << 25), (2, (1 << 23) + 2 * 4096 + 48), (3, (1 << 23) + 1000),
+                                    (1, (1 << 24) + 5)])
+def test_long_rows_reduce_then_scan(cp, rows, k):
+    rng = np.random.default_rng(k + rows)
+    x = rng.integers(-(1 << 31), (1 << 31) - 1, (rows, k), dtype=np.int64).astype(np.int32)
+    X = cp.array(x)
+    got = cp.cumsum(X, axis=1) if rows > 1 else cp.cumsum(X.reshape(-1)).reshape(rows, k)
+    assert got.dtype == np.int64
+    np.testing.assert_array_equal(got.get(), O.cumsum(x, axis=1))
+    # values of both signs: the prefix crosses zero, so the bar's floor is
+    # eps * sum|x| over the row (float32 eps), as stated for scans
+    xf = rng.standard_normal((rows, k)).astype(np.float32)
+    gf = cp.cumsum(cp.array(xf), axis=1).get()
+    assert gf.dtype == np.float32
+    ref = O.cumsum_f64(xf, axis=1)
+    floor = np.finfo(np.float32).eps * np.abs(xf.astype(np.float64)).sum(axis=1, keepdims=True)
+    assert np.max(np.abs(gf - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
+
+
+def test_long_rows_carry_prod_and_dtypes(cp):
+    from macmetalpy_b200 import reductions
+
+    n = 1 << 25
+    rng = np.random.default_rng(77)
+    x = rng.integers(-1000, 1001, n).astype(np.int32)
+    carry = 123456789012
+    c = cp.array(np.array([carry], np.int64))
+    got = reductions._scan(cp.array(x), 0, None, carry_ptr=c._ptr).get()
+    np.testing.assert_array_equal(got, carry + np.cumsum(x, dtype=np.int64))
+    xf = rng.uniform(0, 1, n).astype(np.float32)
+    cf = cp.array(np.array([1.0e6], np.float64))
+    gf = reductions._scan(cp.array(xf), 0, None, carry_ptr=cf._ptr).get()
+    ref = 1.0e6 + np.cumsum(xf.astype(np.float64))
+    assert np.max(np.abs(gf - ref) / ref) <= 1e-6
+    # cumprod: signs only (exact), and values near 1
+    s = rng.choice(np.array([-1, 1], np.int32), 1 << 24)
+    np.testing.assert_array_equal(cp.cumprod(cp.array(s)).get(), np.cumprod(s.astype(np.int64)))
+    p = rng.uniform(0.99999, 1.00001, 1 << 24).astype(np.float32)
+    pref = np.cumprod(p.astype(np.float64))
+    assert np.max(np.abs(cp.cumprod(cp.array(p)).get() - pref) / pref) <= 1e-4
+    # other element types on the same path
+    for dt in (np.int16, np.uint16, np.uint32, np.bool_, np.int64, np.float64):
+        xd = rng.integers(0, 3, 1 << 24).astype(dt)
+        gd = cp.cumsum(cp.array(xd))
+        want = np.cumsum(xd)
+        assert gd.dtype == want.dtype, dt
+        np.testing.assert_array_equal(gd.get(), want)
+    h = rng.uniform(0, 2e-3, 1 << 24).astype(np.float16)
+    gh = cp.cumsum(cp.array(h)).get()
+    assert gh.dtype == np.float16
+    href = np.cumsum(h.astype(np.float64))
+    assert np.max(np.abs(gh.astype(np.float64) - href) / np.maximum(href, 1e-3)) <= 2e-3
