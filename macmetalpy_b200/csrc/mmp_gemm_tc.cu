@@ -145,6 +145,20 @@ __device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory descriptor of an MN-major operand that TMA wrote in boxes of
+// 64 MN-elements (128 bytes) x K-rows with the 128-byte swizzle: 8 K-rows
+// form a 1024-byte atom, the next 8 K-rows follow at +1024 (stride byte
+// offset) and the next 64 MN-elements at +mn_stride (leading byte offset).
+__device__ __forceinline__ uint64_t sw_desc_mn(uint32_t saddr, uint32_t mn_stride) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(mn_stride >> 4) << 16;  // leading byte offset
+  d |= (uint64_t)(1024u >> 4) << 32;      // stride byte offset
+  d |= (uint64_t)1 << 46;  // descriptor version
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+
 // Instruction descriptor: D = f32, A/B format, both K-major, N and M.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_fmt, int M, int N) {
   return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -225,7 +239,10 @@ __device__ __forceinline__ void store_chunk32(char *crow, long long col0, long l
   }
 }
 
-template <int MODE>
+// B_MN: B is read straight from the caller's row-major (K x N) matrix,
+// MN-major in shared memory (four 64-column boxes per stage), instead of
+// from the pre-pass's K-major copy.
+template <int MODE, bool B_MN>
 __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1, void *C,
@@ -300,8 +317,15 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
           const int kc = kt * G::BK;
           tma_load_3d(st, &tmA0, &full[s], kc, m_blk * BM, ca);
           if (G::NOPS == 2) tma_load_3d(st + G::A_BYTES, &tmA1, &full[s], kc, m_blk * BM, ca);
-          tma_load_3d(st + G::NOPS * G::A_BYTES, &tmB0, &full[s], kc, n_blk * BN, cb);
-          if (G::NOPS == 2) tma_load_3d(st + G::NOPS * G::A_BYTES + G::B_BYTES, &tmB1, &full[s], kc, n_blk * BN, cb);
+          if (B_MN) {
+#pragma unroll
+            for (int q = 0; q < BN / 64; ++q)
+              tma_load_3d(st + G::A_BYTES + q * (G::BK * 128), &tmB0, &full[s], n_blk * BN + 64 * q, kc, cb);
+          } else {
+            tma_load_3d(st + G::NOPS * G::A_BYTES, &tmB0, &full[s], kc, n_blk * BN, cb);
+            if (G::NOPS == 2)
+              tma_load_3d(st + G::NOPS * G::A_BYTES + G::B_BYTES, &tmB1, &full[s], kc, n_blk * BN, cb);
+          }
         }
       }
       // drain: every load this CTA issued has landed before it may exit
@@ -310,7 +334,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t ID = make_idesc(MODE == MODE_F16 ? 0u : 2u, BM, BN);
+      // bit 16: B is MN-major
+      constexpr uint32_t ID = make_idesc(MODE == MODE_F16 ? 0u : 2u, BM, BN) | (B_MN ? (1u << 16) : 0u);
       long long g = 0, cg = 0;  // k-tiles and accumulator chunks consumed by this CTA
       bool ok = true;
       for (long long t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -338,7 +363,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
           for (int kk = 0; kk < G::KSTEPS; ++kk) {
             const uint32_t off = kk * G::UMMA_K_BYTES;
             const uint64_t da0 = sw_desc<G::ROW_BYTES>(base + off);
-            const uint64_t db0 = sw_desc<G::ROW_BYTES>(b0 + off);
+            // MN-major B: one MMA's K (16 rows of 128 bytes) is 2048 bytes
+            const uint64_t db0 = B_MN ? sw_desc_mn(b0 + kk * 2048, G::BK * 128) : sw_desc<G::ROW_BYTES>(b0 + off);
             const uint32_t acc = (!first_of_chunk || kk > 0) ? 1u : 0u;
             if (MODE == MODE_3XTF32) {
               const uint64_t da1 = sw_desc<G::ROW_BYTES>(base + G::A_BYTES + off);
@@ -523,6 +549,55 @@ static int make_map(CUtensorMap *map, const void *base, bool f16, long long kp, 
   return MMP_OK;
 }
 
+// Tensor map over a caller's matrix: dims {d0 (contiguous), d1, d2}, byte
+// strides of d1 and d2, box {box0, box1}, 128-byte swizzle; loads past the
+// edges read zeros.
+static int make_map_user(CUtensorMap *map, const void *base, long long d0, long long d1, long long d2,
+                         long long s1_bytes, long long s2_bytes, int box0, int box1) {
+  static PFN_Encode enc = nullptr;
+  if (!enc) enc = (PFN_Encode)mmp::driver_fn("cuTensorMapEncodeTiled");
+  if (!enc) return mmp::set_error(MMP_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)s1_bytes, (cuuint64_t)s2_bytes};
+  cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return mmp::set_error(MMP_E_CUDA, "cuTensorMapEncodeTiled failed");
+  return MMP_OK;
+}
+
+template <int MODE, bool B_MN>
+static int launch(const CUtensorMap &mA0, const CUtensorMap &mA1, const CUtensorMap &mB0, const CUtensorMap &mB1,
+                  void *c, long long m, long long n, long long ldc, long long sc, long long m_blocks,
+                  long long n_blocks, long long k_tiles, long long batch, int a_bc, int b_bc, cudaStream_t st) {
+  typedef Cfg<MODE> G;
+  static bool attr = false;
+  if (!attr) {
+    MMP_CUDA_TRY(
+        cudaFuncSetAttribute(gemm_tc_kernel<MODE, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+    attr = true;
+  }
+  // float16: persistent, one CTA per SM (the stage ring fills shared
+  // memory), tiles handed out round-robin -- the next tile's MMAs overlap
+  // this tile's epilogue (measured 2-8 % faster than a CTA per tile).  The
+  // TF32 modes launch one CTA per tile (the tile loop runs once): their
+  // epilogue already overlaps the chunked MMAs, and the hardware's dynamic
+  // CTA order kept L2 reuse better (16384^3 3xTF32 measured 11 % slower
+  // with the static round-robin order).
+  const long long tiles = m_blocks * n_blocks * batch;
+  const long long sms = (long long)mmp::sm_count();
+  const long long ctas = (MODE == MODE_F16 && tiles > sms) ? sms : tiles;
+  if (ctas > 0x7fffffffll) return mmp::set_error(MMP_E_UNSUPPORTED, "GEMM too large for one launch");
+  gemm_tc_kernel<MODE, B_MN><<<(unsigned)ctas, G::THREADS, G::SMEM, st>>>(
+      mA0, mA1, mB0, mB1, c, m, n, ldc, sc, (int)m_blocks, (int)n_blocks, (int)k_tiles, (int)batch, a_bc, b_bc,
+      mmp::device_error_word());
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return mmp::cuda_error(e, "gemm_tc_kernel");
+  return MMP_OK;
+}
+
 template <int MODE, class T>
 static int run(long long batch, long long m, long long n, long long k, const void *a, long long lda, long long sa,
                const void *b, long long ldb, long long sb, void *c, long long ldc, long long sc) {
@@ -538,6 +613,23 @@ static int run(long long batch, long long m, long long n, long long k, const voi
   const long long m_blocks = Mp / BM, n_blocks = Np / BN, k_tiles = Kp / G::BK;
   if (m_blocks * n_blocks > 0x7fffffffll || m_blocks * n_blocks * batch > (1ll << 40) || k_tiles > 0x7fffffffll)
     return mmp::set_error(MMP_E_UNSUPPORTED, "GEMM too large for one launch");
+  if constexpr (MODE == MODE_F16) {
+    // No pre-pass: TMA reads A (row-major, K-major tiles) and B (row-major,
+    // MN-major tiles) from the caller's buffers, zero-filling past the
+    // edges, when every row and batch pitch is a multiple of 16 bytes.
+    const bool aligned = (uintptr_t)a % 16 == 0 && (uintptr_t)b % 16 == 0 && lda % 8 == 0 && ldb % 8 == 0 &&
+                         (a_bc || batch == 1 || sa % 8 == 0) && (b_bc || batch == 1 || sb % 8 == 0);
+    if (aligned) {
+      CUtensorMap mA, mB;
+      const long long sa_b = (a_bc || batch == 1) ? lda * m * 2 : sa * 2;
+      const long long sb_b = (b_bc || batch == 1) ? ldb * k * 2 : sb * 2;
+      int rc = make_map_user(&mA, a, k, m, ba, lda * 2, sa_b > 0 ? sa_b : 16, G::BK, BM);
+      if (!rc) rc = make_map_user(&mB, b, n, k, bb, ldb * 2, sb_b > 0 ? sb_b : 16, 64, G::BK);
+      if (rc) return rc;
+      return launch<MODE, true>(mA, mA, mB, mB, c, m, n, ldc, sc, m_blocks, n_blocks, k_tiles, batch, a_bc, b_bc,
+                                st);
+    }
+  }
   const size_t es = G::ELEM;
   const size_t a_el = (size_t)ba * Mp * Kp, b_el = (size_t)bb * Np * Kp;
   const size_t ws_bytes = G::NOPS * (a_el + b_el) * es + 1024;
@@ -566,29 +658,10 @@ static int run(long long batch, long long m, long long n, long long k, const voi
     cudaFreeAsync(ws, st);
     return rc;
   }
-  static bool attr = false;
-  if (!attr) {
-    MMP_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
-    attr = true;
-  }
-  // float16: persistent, one CTA per SM (the stage ring fills shared
-  // memory), tiles handed out round-robin -- the next tile's MMAs overlap
-  // this tile's epilogue (measured 2-8 % faster than a CTA per tile).  The
-  // TF32 modes launch one CTA per tile (the tile loop runs once): their
-  // epilogue already overlaps the chunked MMAs, and the hardware's dynamic
-  // CTA order kept L2 reuse better (16384^3 3xTF32 measured 11 % slower
-  // with the static round-robin order).
-  const long long tiles = m_blocks * n_blocks * batch;
-  const long long sms = (long long)mmp::sm_count();
-  const long long ctas = (MODE == MODE_F16 && tiles > sms) ? sms : tiles;
-  if (ctas > 0x7fffffffll) return mmp::set_error(MMP_E_UNSUPPORTED, "GEMM too large for one launch");
-  gemm_tc_kernel<MODE><<<(unsigned)ctas, G::THREADS, G::SMEM, st>>>(mA0, mA1, mB0, mB1, c, m, n, ldc, sc,
-                                                                  (int)m_blocks, (int)n_blocks, (int)k_tiles,
-                                                                  (int)batch, a_bc, b_bc, mmp::device_error_word());
-  cudaError_t e = cudaGetLastError();
+  rc = launch<MODE, false>(mA0, mA1, mB0, mB1, c, m, n, ldc, sc, m_blocks, n_blocks, k_tiles, batch, a_bc, b_bc,
+                           st);
   cudaFreeAsync(ws, st);
-  if (e != cudaSuccess) return mmp::cuda_error(e, "gemm_tc_kernel");
-  return MMP_OK;
+  return rc;
 }
 
 }  // namespace tc

@@ -40,6 +40,34 @@ def test_f16(cp, m, k, n):
     assert frob(got, a, b) <= 2e-3
 
 
+# float16 on the tensor cores: row pitches that are multiples of 8 elements
+# are read in place by TMA (B as an MN-major operand), with ragged M, N and
+# K edges zero-filled; other pitches go through the K-major pre-pass.
+@pytest.mark.parametrize("m,k,n", [(1000, 304, 712), (130, 264, 392), (2048, 2048, 2048), (256, 8, 1024),
+                                   (1000, 300, 700), (129, 257, 255)])
+def test_f16_tensor_core_paths(cp, m, k, n):
+    rng = np.random.default_rng(m * 7 + k * 3 + n)
+    a = (rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float16)
+    b = rng.standard_normal((k, n)).astype(np.float16)
+    got = cp.matmul(cp.array(a), cp.array(b)).get()
+    assert got.dtype == np.float16 and got.shape == (m, n)
+    assert frob(got, a, b) <= 2e-3
+
+
+def test_f16_batched_and_broadcast(cp):
+    rng = np.random.default_rng(9)
+    a = (rng.standard_normal((6, 256, 136)) / 12).astype(np.float16)
+    b = rng.standard_normal((6, 136, 520)).astype(np.float16)
+    got = cp.matmul(cp.array(a), cp.array(b)).get()
+    assert got.shape == (6, 256, 520) and frob(got, a, b) <= 2e-3
+    b2 = rng.standard_normal((136, 264)).astype(np.float16)
+    got = cp.matmul(cp.array(a), cp.array(b2)).get()
+    assert got.shape == (6, 256, 264) and frob(got, a, b2) <= 2e-3
+    a2 = (rng.standard_normal((256, 136)) / 12).astype(np.float16)
+    got = cp.matmul(cp.array(a2), cp.array(b)).get()
+    assert got.shape == (6, 256, 520) and frob(got, a2, b) <= 2e-3
+
+
 def test_batched_and_vectors(cp):
     rng = np.random.default_rng(2)
     a = (rng.standard_normal((8, 128, 64)) / 8).astype(np.float32)
