@@ -43,13 +43,14 @@ enum mmp_dtype {
 
 /* reduction ops: the reference's reduce_sum/max/min/prod (_kernels.py:422-565),
  * mean/var/std (ndarray.py:1779-1834), argmax/argmin (_kernels.py:1189-1257),
- * nan reductions (_kernels.py:612-730, nan_ops.py:112-432) */
+ * nan reductions (_kernels.py:612-730, nan_ops.py:112-432; nanvar/nanstd:
+ * nan_ops.py:444-530, float inputs only) */
 enum mmp_reduce_op {
   MMP_R_SUM = 0, MMP_R_PROD = 1, MMP_R_MAX = 2, MMP_R_MIN = 3,
   MMP_R_MEAN = 4, MMP_R_VAR = 5, MMP_R_STD = 6,
   MMP_R_ARGMAX = 7, MMP_R_ARGMIN = 8,
   MMP_R_NANSUM = 9, MMP_R_NANMEAN = 10, MMP_R_NANMAX = 11, MMP_R_NANMIN = 12,
-  MMP_R_ANY = 13, MMP_R_ALL = 14
+  MMP_R_ANY = 13, MMP_R_ALL = 14, MMP_R_NANVAR = 15, MMP_R_NANSTD = 16
 };
 
 /* scan ops: prefix_sum / prefix_prod (_kernels.py:1148-1170, 1263-1358) */

@@ -29,7 +29,8 @@ template <> struct DtypeCode<double> { static constexpr int value = MMP_FLOAT64;
 // plain op, as nan_ops.nansum does at nan_ops.py:132-134).
 template <int OPC, class T> struct RedSupported {
   static constexpr bool value =
-      !(OPC == MMP_R_NANSUM || OPC == MMP_R_NANMEAN || OPC == MMP_R_NANMAX || OPC == MMP_R_NANMIN) ||
+      !(OPC == MMP_R_NANSUM || OPC == MMP_R_NANMEAN || OPC == MMP_R_NANMAX || OPC == MMP_R_NANMIN ||
+        OPC == MMP_R_NANVAR || OPC == MMP_R_NANSTD) ||
       IsFloatT<T>::value;
 };
 
@@ -70,6 +71,8 @@ int dispatch_op(int op, int dt, Args... args) {
     case MMP_R_NANMIN: return dispatch_dtype<F, MMP_R_NANMIN>(dt, args...);
     case MMP_R_ANY: return dispatch_dtype<F, MMP_R_ANY>(dt, args...);
     case MMP_R_ALL: return dispatch_dtype<F, MMP_R_ALL>(dt, args...);
+    case MMP_R_NANVAR: return dispatch_dtype<F, MMP_R_NANVAR>(dt, args...);
+    case MMP_R_NANSTD: return dispatch_dtype<F, MMP_R_NANSTD>(dt, args...);
     default: return set_error(MMP_E_ARG, "unsupported reduction op");
   }
 }

@@ -35,6 +35,8 @@
 #define MMP_R_NANMIN 12
 #define MMP_R_ANY 13
 #define MMP_R_ALL 14
+#define MMP_R_NANVAR 15
+#define MMP_R_NANSTD 16
 
 namespace mmpd {
 
@@ -578,6 +580,140 @@ struct NanSumOp {
 };
 template <class T> struct RedOp<MMP_R_NANSUM, T> : NanSumOp<T, false> {};
 template <class T> struct RedOp<MMP_R_NANMEAN, T> : NanSumOp<T, true> {};
+
+// nanvar / nanstd in one pass.  An accumulator holds the count n of the
+// non-NaN values it has seen and their sums S1 = sum(x - k), S2 =
+// sum((x - k)^2) around its own shift k: the first non-NaN value it saw (the
+// array's first element may be NaN, so there is no common shift as in
+// VarOp).  Per element that is a subtract, an add and an fma, with the f32
+// partial of a loop step added to f64.  Two accumulators merge without a
+// division by moving b's sums to a's shift, d = kb - ka:
+//   S1 = S1a + S1b + nb d,  S2 = S2a + S2b + d (2 S1b + nb d)
+// (exact algebra; in f64 the d^2 terms cost precision only when the shifts,
+// two values of the data, lie ~1e5 standard deviations apart).
+// var = (S2 - S1^2/n) / (n - ddof), NaN when n - ddof <= 0 (numpy's nanvar).
+template <class T, bool STD>
+struct NanVarOp {
+  struct Acc {
+    double n, k, s1, s2;
+  };
+  __device__ static Acc init() {
+    Acc a;
+    a.n = 0.0;
+    a.k = 0.0;
+    a.s1 = 0.0;
+    a.s2 = 0.0;
+    return a;
+  }
+  __device__ static Acc start(Acc a, T) { return a; }
+  __device__ static void one(Acc &a, T v, long long) {
+    if (isnan_(v)) return;
+    const double x = as_d(v);
+    if (a.n == 0.0) a.k = x;
+    const double d = x - a.k;
+    a.s1 += d;
+    a.s2 += d * d;
+    a.n += 1.0;
+  }
+  // the non-NaN values of f[0..K): f32 partial sums around the shift
+  template <int K>
+  __device__ static void group(Acc &a, const float (&f)[K]) {
+    if (a.n == 0.0) {  // the first values this accumulator sees
+      float g = 0.f;
+      bool any = false;
+#pragma unroll
+      for (int j = K - 1; j >= 0; --j) {
+        const bool ok = !isnan_(f[j]);
+        g = ok ? f[j] : g;
+        any = any || ok;
+      }
+      if (!any) return;
+      a.k = (double)g;
+    }
+    const float kf = (float)a.k;  // exact: k is one of the f32 inputs
+    float s1 = 0.f, s2 = 0.f;
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const bool ok = !isnan_(f[j]);
+      const float d = ok ? f[j] - kf : 0.f;
+      s1 += d;
+      s2 += d * d;
+      c += ok ? 1 : 0;
+    }
+    a.s1 += (double)s1;
+    a.s2 += (double)s2;
+    a.n += (double)c;
+  }
+  template <int V>
+  __device__ static void vec(Acc &a, const T (&v)[V], long long) {
+    if constexpr (IsFloat<T>::value && sizeof(T) < 8) {
+      float f[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) f[j] = AsF<T>::f(v[j]);
+      group<V>(a, f);
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) one(a, v[j], 0);
+    }
+  }
+  template <int V>
+  __device__ static void vec4(Acc &a, const T (&v0)[V], const T (&v1)[V], const T (&v2)[V], const T (&v3)[V],
+                              long long, long long) {
+    if constexpr (IsFloat<T>::value && sizeof(T) < 8) {
+      float f[4 * V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        f[j] = AsF<T>::f(v0[j]);
+        f[V + j] = AsF<T>::f(v1[j]);
+        f[2 * V + j] = AsF<T>::f(v2[j]);
+        f[3 * V + j] = AsF<T>::f(v3[j]);
+      }
+      group<4 * V>(a, f);
+    } else {
+      vec<V>(a, v0, 0);
+      vec<V>(a, v1, 0);
+      vec<V>(a, v2, 0);
+      vec<V>(a, v3, 0);
+    }
+  }
+  __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
+    if constexpr (IsFloat<T>::value && sizeof(T) < 8) {
+      const float f[4] = {AsF<T>::f(v0), AsF<T>::f(v1), AsF<T>::f(v2), AsF<T>::f(v3)};
+      group<4>(a, f);
+    } else {
+      one(a, v0, i);
+      one(a, v1, i);
+      one(a, v2, i);
+      one(a, v3, i);
+    }
+  }
+  __device__ static Acc combine(Acc a, Acc b) {
+    if (b.n == 0.0) return a;
+    if (a.n == 0.0) return b;
+    const double d = b.k - a.k;
+    a.s2 += b.s2 + d * (2.0 * b.s1 + b.n * d);
+    a.s1 += b.s1 + b.n * d;
+    a.n += b.n;
+    return a;
+  }
+  __device__ static void finish(Acc a, long long, void *out, long long idx, int dt, double ddof,
+                                PartialOut *p) {
+    double m2 = a.n > 0.0 ? a.s2 - a.s1 * a.s1 / a.n : 0.0;
+    if (m2 < 0.0) m2 = 0.0;
+    const double dof = a.n - ddof;
+    const double var = dof > 0.0 ? m2 / dof : __longlong_as_double(0x7ff8000000000000ll);
+    store_acc_value(out, idx, dt, STD ? sqrt(var) : var);
+    if (p) {  // the shifted form of VarOp's partial
+      p->s1 = a.s1;
+      p->s2 = a.s2;
+      p->shift = a.k;
+      p->count = (long long)a.n;
+    }
+  }
+};
+template <class T> struct RedOp<MMP_R_NANVAR, T> : NanVarOp<T, false> {};
+template <class T> struct RedOp<MMP_R_NANSTD, T> : NanVarOp<T, true> {};
 
 template <class T, bool ANY>
 struct BoolOp {

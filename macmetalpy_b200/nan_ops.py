@@ -11,9 +11,10 @@ reference does (``nan_ops.py:132-134``).
 The others follow numpy's nan-functions (the reference's CPU branch):
 ``nanprod``/``nancumsum``/``nancumprod`` replace NaN by the identity in a
 fused select that feeds the reduction or scan (``nan_ops.py:171-270``);
-``nanvar``/``nanstd`` are numpy's two passes -- the NaN-skipping mean, then
-the sum of squared deviations of the non-NaN elements over ``count - ddof``,
-NaN where that is <= 0 (``nan_ops.py:444-559``); ``nanargmax``/``nanargmin``
+``nanvar``/``nanstd`` give numpy's values -- the sum of squared deviations
+of the non-NaN elements from their mean over ``count - ddof``, NaN where
+that is <= 0 (``nan_ops.py:444-559``) -- in one pass that merges (count,
+mean, M2) pairwise; ``nanargmax``/``nanargmin``
 raise numpy's ``ValueError`` on an all-NaN slice, otherwise take the
 arg-extreme with NaN replaced by -inf / +inf, returning a Python int without
 an axis and numpy's int64 with one (``nan_ops.py:562-612``).
@@ -105,35 +106,30 @@ def nancumprod(a, axis=None, dtype=None, out=None):
 
 def nanvar(a, axis=None, dtype=None, out=None, ddof=0, keepdims=False, where=None, *, correction=None,
            mean=None):
-    """Variance of the non-NaN elements (numpy's two-pass nanvar)."""
+    """Variance of the non-NaN elements: one pass (count, mean and M2 merged
+    pairwise; NaN where fewer than ddof + 1 values remain).  The reference
+    runs numpy's two-pass algorithm on the GPU (nan_ops.py:484-530)."""
     from . import reductions
-    from .logic_ops import isnan
-    from .ndarray import ndarray
 
     if correction is not None:
         ddof = correction
     a = _asarray(a)
     if a.dtype.kind != "f":
         return reductions.var(a, axis=axis, dtype=dtype, out=out, ddof=ddof, keepdims=keepdims)
-    if dtype is not None:
-        a = a.astype(dtype)
-    mask = isnan(a)
-    avg = _reduce(a, "nanmean", axis, True)
-    dev = ndarray._select(mask, 0, a - avg)
-    ss = reductions.sum(dev * dev, axis=axis, keepdims=keepdims)
-    cnt = reductions.sum(~mask, axis=axis, keepdims=keepdims)
-    dof = cnt - ddof
-    r = ndarray._select(dof > 0, ss / dof.astype(ss.dtype), np.nan)
-    return _out(r.astype(ss.dtype), out)
+    return _reduce(a, "nanvar", axis, keepdims, ddof=float(ddof), dtype=dtype, out=out)
 
 
 def nanstd(a, axis=None, dtype=None, out=None, ddof=0, keepdims=False, where=None, *, correction=None,
            mean=None):
-    """Standard deviation of the non-NaN elements."""
-    from .math_ops import sqrt
+    """Standard deviation of the non-NaN elements (nan_ops.py:444-481)."""
+    from . import reductions
 
-    return _out(sqrt(nanvar(a, axis=axis, dtype=dtype, ddof=ddof, keepdims=keepdims, correction=correction)),
-                out)
+    if correction is not None:
+        ddof = correction
+    a = _asarray(a)
+    if a.dtype.kind != "f":
+        return reductions.std(a, axis=axis, dtype=dtype, out=out, ddof=ddof, keepdims=keepdims)
+    return _reduce(a, "nanstd", axis, keepdims, ddof=float(ddof), dtype=dtype, out=out)
 
 
 def _nanarg(a, kind, fill, axis, out, keepdims):

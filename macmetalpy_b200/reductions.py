@@ -41,12 +41,13 @@ __all__ = [
 OPC = {
     "sum": 0, "prod": 1, "max": 2, "min": 3, "mean": 4, "var": 5, "std": 6, "argmax": 7,
     "argmin": 8, "nansum": 9, "nanmean": 10, "nanmax": 11, "nanmin": 12, "any": 13, "all": 14,
+    "nanvar": 15, "nanstd": 16,
 }
 
 _NP_FN = {
     "sum": np.sum, "prod": np.prod, "max": np.max, "min": np.min, "mean": np.mean, "var": np.var,
     "std": np.std, "nansum": np.nansum, "nanmean": np.nanmean, "nanmax": np.nanmax,
-    "nanmin": np.nanmin,
+    "nanmin": np.nanmin, "nanvar": np.nanvar, "nanstd": np.nanstd,
 }
 
 _NO_IDENTITY = {"max": "maximum", "min": "minimum", "argmax": "argmax", "argmin": "argmin",
@@ -104,7 +105,7 @@ def _reduce(a, kind: str, axis=None, keepdims=False, ddof=0.0, dtype=None, out=N
     a = _asarray(a)
     if dtype is not None:
         a = a.astype(resolve_dtype(dtype), copy=False)
-    if a._dtype.kind == "f" or kind not in ("nansum", "nanmean", "nanmax", "nanmin"):
+    if a._dtype.kind == "f" or kind not in ("nansum", "nanmean", "nanmax", "nanmin", "nanvar", "nanstd"):
         k = kind
     else:  # no NaN in integer/bool arrays (nan_ops.py:132-134)
         k = kind[3:]

@@ -107,3 +107,30 @@ def test_large_vs_oracle(cp, shape):
     ref = np.nancumsum(x.astype(np.float64), axis=-1)
     scale = np.nancumsum(np.abs(x.astype(np.float64)), axis=-1)
     assert np.max(np.abs(c - ref) / np.maximum(scale, 1e-6)) <= 1e-4
+
+
+def test_nanvar_one_pass_edges(cp):
+    """One-pass nanvar: the first element NaN with a large common offset
+    (no shift to lean on), all-NaN rows and dof <= 0 give NaN, float16 and
+    float64 inputs, and a fused expression as input."""
+    rng = np.random.default_rng(21)
+    x = (rng.standard_normal((64, 5000)) + 1.0e4).astype(np.float32)
+    x[rng.random(x.shape) < 0.05] = np.nan
+    x[:, 0] = np.nan
+    x[7] = np.nan                      # an all-NaN row
+    x[9, 1:] = np.nan                  # one value left: ddof=1 gives NaN
+    X = cp.array(x)
+    for ax in (None, 0, 1):
+        for ddof in (0, 1):
+            close(cp.nanvar(X, axis=ax, ddof=ddof), O.nanvar(x, axis=ax, ddof=ddof))
+    close(cp.nanstd(X, axis=1), O.nanstd(x, axis=1))
+    # float16: scale kept small so that numpy's own float16 sum of squares
+    # does not overflow to inf (this library accumulates in f32/f64)
+    for dt, sc in ((np.float16, 0.3), (np.float64, 3.0)):
+        xd = (rng.standard_normal(30000) * sc).astype(dt)
+        xd[::7] = np.nan
+        close(cp.nanvar(cp.array(xd)), O.nanvar(xd), rtol=3e-3 if dt == np.float16 else 1e-6)
+    y = rng.standard_normal(1 << 20).astype(np.float32)
+    y[::13] = np.nan
+    Y = cp.array(y)
+    close(cp.nanvar(Y * 2 + 1), O.nanvar(y * np.float32(2) + np.float32(1)))
