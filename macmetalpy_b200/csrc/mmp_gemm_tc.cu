@@ -469,60 +469,97 @@ __device__ __forceinline__ float tf32_round(float v) {
   return __uint_as_float(u);
 }
 
-// A[b] (M x K, row stride lda) -> out0/out1 [b][Mp][Kp], zero padded.
+// One element of an operand in the pre-pass's output form(s).
+template <class T, int MODE>
+__device__ __forceinline__ void prep_split(T v, T &o0, T &o1) {
+  if constexpr (MODE == MODE_3XTF32) {
+    const float big = tf32_round((float)v);
+    o0 = big;
+    o1 = (float)v - big;
+  } else if constexpr (MODE == MODE_TF32) {
+    o0 = tf32_round((float)v);
+  } else {
+    o0 = v;
+  }
+}
+
+// A[b] (M x K, row stride lda) -> out0/out1 [b][Mp][Kp], zero padded: rows
+// of Kp over blockIdx.y (grid-stride), 4 consecutive k per thread (one
+// vector load when the source row allows, `vec_src`), vector stores.
 template <class T, int MODE>
 __global__ void __launch_bounds__(256) prep_rows_kernel(const T *__restrict__ A, long long lda, long long sA,
                                                         long long M, long long K, long long Mp, long long Kp,
                                                         long long batch, T *__restrict__ out0,
-                                                        T *__restrict__ out1) {
-  const long long total = batch * Mp * Kp;
-  for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
-    const long long k = i % Kp;
-    const long long t = i / Kp;
-    const long long m = t % Mp;
-    const long long b = t / Mp;
-    T v = (m < M && k < K) ? A[b * sA + m * lda + k] : T(0);
-    if constexpr (MODE == MODE_3XTF32) {
-      float big = tf32_round((float)v);
-      out0[i] = big;
-      out1[i] = (float)v - big;
-    } else if constexpr (MODE == MODE_TF32) {
-      out0[i] = tf32_round((float)v);
-    } else {
-      out0[i] = v;
+                                                        T *__restrict__ out1, int vec_src) {
+  const long long rows = batch * Mp;
+  for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
+    const long long b = r / Mp, m = r - b * Mp;
+    const T *src = A + b * sA + m * lda;
+    T *d0 = out0 + r * Kp;
+    T *d1 = out1 + r * Kp;
+    for (long long k0 = ((long long)blockIdx.x * 256 + threadIdx.x) * 4; k0 < Kp;
+         k0 += (long long)gridDim.x * 256 * 4) {
+      T v[4];
+      if (m < M && vec_src && k0 + 3 < K) {
+        const mmpd::Vec<T, 4> t = mmpd::ldvec_stream<T, 4>(src + k0);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = t.v[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = (m < M && k0 + e < K) ? src[k0 + e] : T(0);
+      }
+      mmpd::Vec<T, 4> o0, o1;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) prep_split<T, MODE>(v[e], o0.v[e], o1.v[e]);
+      mmpd::stvec<T, 4>(d0 + k0, o0);
+      if (MODE == MODE_3XTF32) mmpd::stvec<T, 4>(d1 + k0, o1);
     }
   }
 }
 
-// B[b] (K x N, row stride ldb) -> out[b][Np][Kp] = B^T, through a 32x32
-// shared tile so that reads and writes are both coalesced.
+// B[b] (K x N, row stride ldb) -> out[b][Np][Kp] = B^T, through a 32 (k) x
+// 128 (n) shared tile: 4 consecutive n per thread on the way in (one vector
+// load when the source row allows), 4 consecutive k per thread on the way
+// out (vector stores); the one-word row padding keeps the column reads free
+// of bank conflicts.
 template <class T, int MODE>
 __global__ void __launch_bounds__(256) prep_cols_kernel(const T *__restrict__ B, long long ldb, long long sB,
                                                         long long K, long long N, long long Np, long long Kp,
-                                                        T *__restrict__ out0, T *__restrict__ out1) {
-  __shared__ T tile[32][33];  // grid.y = ceil(Kp / 32): Kp need not be a multiple of 32
-  const long long b = blockIdx.z;
-  const long long n0 = (long long)blockIdx.x * 32, k0 = (long long)blockIdx.y * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int r = ty; r < 32; r += 8) {
-    const long long k = k0 + r, n = n0 + tx;
-    tile[r][tx] = (k < K && n < N) ? B[b * sB + k * ldb + n] : T(0);
-  }
-  __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
-    const long long n = n0 + r, k = k0 + tx;
-    if (k >= Kp) continue;
-    const long long o = (b * Np + n) * Kp + k;
-    T v = tile[tx][r];
-    if constexpr (MODE == MODE_3XTF32) {
-      float big = tf32_round((float)v);
-      out0[o] = big;
-      out1[o] = (float)v - big;
-    } else if constexpr (MODE == MODE_TF32) {
-      out0[o] = tf32_round((float)v);
-    } else {
-      out0[o] = v;
+                                                        long long batch, T *__restrict__ out0,
+                                                        T *__restrict__ out1, int vec_src) {
+  __shared__ T tile[32][129];
+  const long long n0 = (long long)blockIdx.x * 128, k0 = (long long)blockIdx.y * 32;
+  const int t = threadIdx.x;
+  for (long long b = blockIdx.z; b < batch; b += gridDim.z) {
+    const T *src = B + b * sB;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kr = (t >> 5) + 8 * i, nl = (t & 31) * 4;
+      const long long k = k0 + kr, n = n0 + nl;
+      T v[4];
+      if (k < K && vec_src && n + 3 < N) {
+        const mmpd::Vec<T, 4> q = mmpd::ldvec_stream<T, 4>(src + k * ldb + n);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = q.v[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = (k < K && n + e < N) ? src[k * ldb + n + e] : T(0);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[kr][nl + e] = v[e];
     }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int nl = (t >> 3) + 32 * i, kl = (t & 7) * 4;
+      const long long o = (b * Np + n0 + nl) * Kp + k0 + kl;
+      mmpd::Vec<T, 4> o0, o1;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) prep_split<T, MODE>(tile[kl + e][nl], o0.v[e], o1.v[e]);
+      mmpd::stvec<T, 4>(out0 + o, o0);
+      if (MODE == MODE_3XTF32) mmpd::stvec<T, 4>(out1 + o, o1);
+    }
+    __syncthreads();
   }
 }
 
@@ -640,12 +677,14 @@ static int run(long long batch, long long m, long long n, long long k, const voi
   T *B0 = A0 + (G::NOPS == 2 ? 2 * a_el : a_el);
   T *B1 = B0 + b_el;
   {
-    const long long tot = (long long)a_el;
-    long long blocks = (tot + 255) / 256;
-    if (blocks > (long long)mmp::sm_count() * 16) blocks = (long long)mmp::sm_count() * 16;
-    prep_rows_kernel<T, MODE><<<(unsigned)blocks, 256, 0, st>>>((const T *)a, lda, sa, m, k, Mp, Kp, ba, A0, A1);
-    dim3 g2((unsigned)(Np / 32), (unsigned)((Kp + 31) / 32), (unsigned)bb);
-    prep_cols_kernel<T, MODE><<<g2, 256, 0, st>>>((const T *)b, ldb, sb, k, n, Np, Kp, B0, B1);
+    const size_t vb = 4 * sizeof(T);  // one vector of 4 elements
+    const int va = (uintptr_t)a % vb == 0 && lda % 4 == 0 && (ba == 1 || sa % 4 == 0);
+    const int vbb = (uintptr_t)b % vb == 0 && ldb % 4 == 0 && (bb == 1 || sb % 4 == 0);
+    const long long rows = ba * Mp, gx = (Kp + 1023) / 1024;
+    dim3 g1((unsigned)gx, (unsigned)(rows < 65535 ? rows : 65535), 1);
+    prep_rows_kernel<T, MODE><<<g1, 256, 0, st>>>((const T *)a, lda, sa, m, k, Mp, Kp, ba, A0, A1, va);
+    dim3 g2((unsigned)(Np / 128), (unsigned)(Kp / 32), (unsigned)(bb < 65535 ? bb : 65535));
+    prep_cols_kernel<T, MODE><<<g2, 256, 0, st>>>((const T *)b, ldb, sb, k, n, Np, Kp, bb, B0, B1, vbb);
   }
   CUtensorMap mA0, mA1, mB0, mB1;
   const bool f16 = MODE == MODE_F16;
