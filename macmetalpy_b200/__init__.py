@@ -21,6 +21,7 @@ from .linalg_top import matmul
 from .logic_ops import *  # noqa: F401,F403
 from .math_ops import *  # noqa: F401,F403
 from .nan_ops import *  # noqa: F401,F403
+from .order_stats import *  # noqa: F401,F403
 from .ndarray import ndarray
 from .raw_kernel import RawKernel
 from .reductions import *  # noqa: F401,F403

@@ -448,3 +448,49 @@ def putmask(a, mask, values):
     b = np.array(a, copy=True)
     np.putmask(b, mask, values)
     return b
+
+
+# ---------------------------------------------------------------- order statistics
+def median(a, axis=None, keepdims=False):
+    """``reductions.median`` (reductions.py:627-641): ``np.median`` on the
+    host copy."""
+    return np.median(a, axis=axis, keepdims=keepdims)
+
+
+def percentile(a, q, axis=None, keepdims=False):
+    """``reductions.percentile`` (reductions.py:644-658): ``np.percentile``
+    (method 'linear', the reference passes no method)."""
+    return np.percentile(a, q, axis=axis, keepdims=keepdims)
+
+
+def quantile(a, q, axis=None, keepdims=False):
+    """``reductions.quantile`` (reductions.py:806-820): ``np.quantile``."""
+    return np.quantile(a, q, axis=axis, keepdims=keepdims)
+
+
+def nanmedian(a, axis=None, keepdims=False):
+    """``nan_ops.nanmedian`` (nan_ops.py:435-441): ``np.nanmedian``."""
+    return np.nanmedian(a, axis=axis, keepdims=keepdims)
+
+
+def nanpercentile(a, q, axis=None, keepdims=False):
+    """``nan_ops.nanpercentile`` (nan_ops.py:763-780): ``np.nanpercentile``."""
+    return np.nanpercentile(a, q, axis=axis, keepdims=keepdims)
+
+
+def nanquantile(a, q, axis=None, keepdims=False):
+    """``nan_ops.nanquantile`` (nan_ops.py:783-800): ``np.nanquantile``."""
+    return np.nanquantile(a, q, axis=axis, keepdims=keepdims)
+
+
+def unique(a, return_index=False, return_inverse=False, return_counts=False, axis=None):
+    """``sorting.unique`` (sorting.py:200-215): ``np.unique`` (equal_nan=True:
+    NaNs merge into one value)."""
+    return np.unique(a, return_index=return_index, return_inverse=return_inverse, return_counts=return_counts,
+                     axis=axis)
+
+
+def lexsort(keys):
+    """``sorting.lexsort`` (sorting.py:274-278): ``np.lexsort`` (stable, the
+    last key primary)."""
+    return np.lexsort(keys)

@@ -148,6 +148,50 @@ def main():
     nan_golden(mp)
     sort_golden(mp)
     index_golden(mp)
+    order_golden(mp)
+
+
+def order_golden(mp):
+    """median / percentile / quantile (``reductions.py:627-820``), their
+    nan-versions (``nan_ops.py:435-800``, below the 4,194,304-element
+    threshold: the CPU branch), unique with first indices, inverse and
+    counts (``sorting.py:200-215``) and lexsort (``sorting.py:274-278``),
+    called through the reference."""
+    g = {}
+    rng = np.random.default_rng(11)
+    a = (rng.standard_normal((9, 37)) * 10).astype(np.float32)
+    an = a.copy()
+    an[rng.random(a.shape) < 0.2] = np.nan
+    an[3] = np.nan
+    ai = rng.integers(-50, 50, (9, 37)).astype(np.int32)
+    u = rng.integers(-20, 20, 600).astype(np.int32)
+    uf = rng.standard_normal(800).astype(np.float32).round(1)
+    uf[rng.random(800) < 0.05] = np.nan
+    k1 = rng.integers(0, 5, 300).astype(np.int32)
+    k2 = rng.standard_normal(300).astype(np.float32).round(0)
+    g.update(a=a, an=an, ai=ai, u=u, uf=uf, k1=k1, k2=k2)
+    A, AN, AI = mp.array(a), mp.array(an), mp.array(ai)
+    for ax in (None, 0, 1):
+        t = "n" if ax is None else str(ax)
+        g[f"median_{t}"] = np.asarray(mp.median(A, axis=ax).get())
+        g[f"median_i_{t}"] = np.asarray(mp.median(AI, axis=ax).get())
+        g[f"pct37_{t}"] = np.asarray(mp.percentile(A, 37.5, axis=ax).get())
+        g[f"pct_list_{t}"] = np.asarray(mp.percentile(A, [10, 50, 90], axis=ax).get())
+        g[f"pct_i_{t}"] = np.asarray(mp.percentile(AI, 30, axis=ax).get())
+        g[f"q03_{t}"] = np.asarray(mp.quantile(A, 0.3, axis=ax).get())
+        g[f"nanmedian_{t}"] = np.asarray(mp.nanmedian(AN, axis=ax).get())
+        g[f"nanpct_{t}"] = np.asarray(mp.nanpercentile(AN, 12.5, axis=ax).get())
+        g[f"nanq_{t}"] = np.asarray(mp.nanquantile(AN, 0.6, axis=ax).get())
+    for name, v in (("u", u), ("uf", uf)):
+        vals, idx, inv, cnt = mp.unique(mp.array(v), return_index=True, return_inverse=True, return_counts=True)
+        g[f"unique_{name}"] = vals.get()
+        g[f"unique_{name}_index"] = idx.get()
+        g[f"unique_{name}_inverse"] = inv.get()
+        g[f"unique_{name}_counts"] = cnt.get()
+    g["lexsort"] = mp.lexsort([mp.array(k1), mp.array(k2)]).get()
+    out = os.path.join(HERE, "golden_order_v1.npz")
+    np.savez_compressed(out, **g)
+    print(f"wrote {out}: {len(g)} arrays, {os.path.getsize(out)} bytes")
 
 
 def index_golden(mp):

@@ -226,3 +226,28 @@ def test_advanced_indexing_and_routines():
     eq(O.extract(m, a), X["extract"])
     eq(O.put(v, np.array([0, 3, 39]), np.array([100, 200], np.int32)), X["put"])
     eq(O.putmask(v, v > 0, np.array([7, 8, 9], np.int32)), X["putmask"])
+
+
+R = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_order_v1.npz"))
+
+
+def test_order_statistics_unique_lexsort():
+    a, an, ai = R["a"], R["an"], R["ai"]
+    for ax in (None, 0, 1):
+        t = "n" if ax is None else str(ax)
+        eq(O.median(a, axis=ax), R[f"median_{t}"])
+        eq(O.median(ai, axis=ax), R[f"median_i_{t}"])
+        eq(O.percentile(a, 37.5, axis=ax), R[f"pct37_{t}"])
+        eq(O.percentile(a, [10, 50, 90], axis=ax), R[f"pct_list_{t}"])
+        eq(O.percentile(ai, 30, axis=ax), R[f"pct_i_{t}"])
+        eq(O.quantile(a, 0.3, axis=ax), R[f"q03_{t}"])
+        eq(O.nanmedian(an, axis=ax), R[f"nanmedian_{t}"])
+        eq(O.nanpercentile(an, 12.5, axis=ax), R[f"nanpct_{t}"])
+        eq(O.nanquantile(an, 0.6, axis=ax), R[f"nanq_{t}"])
+    for name in ("u", "uf"):
+        vals, idx, inv, cnt = O.unique(R[name], return_index=True, return_inverse=True, return_counts=True)
+        eq(vals, R[f"unique_{name}"])
+        eq(idx, R[f"unique_{name}_index"])
+        eq(inv, R[f"unique_{name}_inverse"])
+        eq(cnt, R[f"unique_{name}_counts"])
+    eq(O.lexsort([R["k1"], R["k2"]]), R["lexsort"])
