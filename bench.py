@@ -42,6 +42,9 @@ import numpy as np
 REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
+# stdout carries the one JSON line: NCCL's log (its version line, printed
+# when NCCL_DEBUG is set in the environment) goes to stderr instead
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 N_C2 = 1 << 28
 BC_ROWS, BC_COLS = 8192, 32768
