@@ -102,7 +102,7 @@ def _load():
     if not os.path.exists(LIB_PATH):
         raise RuntimeError(
             f"libmmp_cuda.so not found at {LIB_PATH}; build it with "
-            "`python -m macmetalpy_b200.csrc.build` (there is no CPU fallback)"
+            "`python macmetalpy_b200/csrc/build.py` or `__graft_entry__.build()` (there is no CPU fallback)"
         )
     L = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

@@ -6,7 +6,8 @@ with the static CUDA runtime and NVRTC, into
 ``macmetalpy_b200/_lib/libmmp_cuda.so``.  Objects are rebuilt only when a
 source or header is newer than the object.
 
-Usage: ``python -m macmetalpy_b200.csrc.build [--force] [--verbose]``.
+Usage: ``python macmetalpy_b200/csrc/build.py [--force] [--verbose]`` (run as a
+script: importing it through the package would need the library it builds).
 """
 
 from __future__ import annotations
