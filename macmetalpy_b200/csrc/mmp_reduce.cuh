@@ -422,6 +422,41 @@ struct ArgOp {
       for (int j = 0; j < V; ++j) one(a, v[j], base + j);
     }
   }
+  // Deferred first-occurrence search (float / half): the loop keeps only
+  // the running extreme pm and the loop step g whose vectors first reached
+  // it, branch-free; the element index inside that step is searched once
+  // after the loop (the kernel reloads the step's vectors and hands them to
+  // vec4 / vec).  Searching inside the loop cost the whole warp a divergent
+  // search whenever any one lane found a new extreme -- nearly every step
+  // early on.
+  static constexpr bool kGroupDeferred = IsFloat<T>::value && sizeof(T) <= 4;
+  template <int V>
+  __device__ static void group_step(float &pm, long long &pg, const T (&v0)[V], const T (&v1)[V],
+                                    const T (&v2)[V], const T (&v3)[V], long long g) {
+    float m0 = AsF<T>::f(v0[0]), m1 = AsF<T>::f(v1[0]), m2 = AsF<T>::f(v2[0]), m3 = AsF<T>::f(v3[0]);
+#pragma unroll
+    for (int j = 1; j < V; ++j) {
+      m0 = MAX ? max_nan(m0, AsF<T>::f(v0[j])) : min_nan(m0, AsF<T>::f(v0[j]));
+      m1 = MAX ? max_nan(m1, AsF<T>::f(v1[j])) : min_nan(m1, AsF<T>::f(v1[j]));
+      m2 = MAX ? max_nan(m2, AsF<T>::f(v2[j])) : min_nan(m2, AsF<T>::f(v2[j]));
+      m3 = MAX ? max_nan(m3, AsF<T>::f(v3[j])) : min_nan(m3, AsF<T>::f(v3[j]));
+    }
+    const float m = MAX ? max_nan(max_nan(m0, m1), max_nan(m2, m3)) : min_nan(min_nan(m0, m1), min_nan(m2, m3));
+    // the same rule as vec4: a strictly better value or the first NaN
+    const bool take = (pg < 0) || (!isnan_(pm) && (isnan_(m) || (MAX ? (m > pm) : (m < pm))));
+    pm = take ? m : pm;
+    pg = take ? g : pg;
+  }
+  // the same for one vector per step (the row kernels)
+  template <int V>
+  __device__ static void vec_step(float &pm, long long &pg, const T (&v)[V], long long g) {
+    float m = AsF<T>::f(v[0]);
+#pragma unroll
+    for (int j = 1; j < V; ++j) m = MAX ? max_nan(m, AsF<T>::f(v[j])) : min_nan(m, AsF<T>::f(v[j]));
+    const bool take = (pg < 0) || (!isnan_(pm) && (isnan_(m) || (MAX ? (m > pm) : (m < pm))));
+    pm = take ? m : pm;
+    pg = take ? g : pg;
+  }
   // four vectors at element offsets b0, b0 + step, b0 + 2 step, b0 + 3 step
   // (increasing): one NaN-propagating extreme of all of them, one compare
   // with the running value, and the first-occurrence search only when it wins
@@ -820,6 +855,17 @@ struct HasVec4<Op, decltype((void)&Op::template vec4<4>)> {
   static constexpr bool value = true;
 };
 
+// Ops that defer the first-occurrence search of their vector loop steps
+// (ArgOp on float / half).
+template <class Op, class = void>
+struct HasGroupDeferred {
+  static constexpr bool value = false;
+};
+template <class Op>
+struct HasGroupDeferred<Op, decltype((void)Op::kGroupDeferred)> {
+  static constexpr bool value = Op::kGroupDeferred;
+};
+
 template <int OPC, class T, class L>
 __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void *out, int out_dt,
                                                  double ddof, void *scratch, unsigned *ticket,
@@ -836,6 +882,31 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
   if (ld.aligned) {
     long long nv = n / V;
     long long i = tid;
+    if constexpr (HasGroupDeferred<Op>::value) {
+      float pm = 0.0f;
+      long long pg = -1;  // first vector index of the best loop step so far
+      for (; i + 3 * nth < nv; i += 4 * nth) {
+        typename L::template Raw<V> r0, r1, r2, r3;
+        ld.template load<V>(i * V, r0);
+        ld.template load<V>((i + nth) * V, r1);
+        ld.template load<V>((i + 2 * nth) * V, r2);
+        ld.template load<V>((i + 3 * nth) * V, r3);
+        T a0[V], a1[V], a2[V], a3[V];
+        ld.template apply<V>(r0, a0);
+        ld.template apply<V>(r1, a1);
+        ld.template apply<V>(r2, a2);
+        ld.template apply<V>(r3, a3);
+        Op::template group_step<V>(pm, pg, a0, a1, a2, a3, i);
+      }
+      if (pg >= 0) {  // the exact first index inside the best step
+        T a0[V], a1[V], a2[V], a3[V];
+        ld.template vec<V>(pg * V, a0);
+        ld.template vec<V>((pg + nth) * V, a1);
+        ld.template vec<V>((pg + 2 * nth) * V, a2);
+        ld.template vec<V>((pg + 3 * nth) * V, a3);
+        Op::template vec4<V>(acc, a0, a1, a2, a3, pg * V, nth * V);
+      }
+    }
     for (; i + 3 * nth < nv; i += 4 * nth) {
       typename L::template Raw<V> r0, r1, r2, r3;
       ld.template load<V>(i * V, r0);
@@ -917,6 +988,24 @@ __device__ __forceinline__ void reduce_rows_block_body(const L &ld, long long ro
     if (vec_ok) {
       long long nv = k / V;
       long long i = threadIdx.x;
+      if constexpr (HasGroupDeferred<Op>::value) {
+        // extreme and its vector first, the index inside the vector after
+        // the loop (see ArgOp::group_step)
+        float pm = 0.0f;
+        long long pg = -1;
+        for (; i + RBLOCK < nv; i += 2 * RBLOCK) {
+          T a0[V], a1[V];
+          ld.template vec<V>(base + i * V, a0);
+          ld.template vec<V>(base + (i + RBLOCK) * V, a1);
+          Op::template vec_step<V>(pm, pg, a0, i);
+          Op::template vec_step<V>(pm, pg, a1, i + RBLOCK);
+        }
+        if (pg >= 0) {
+          T a0[V];
+          ld.template vec<V>(base + pg * V, a0);
+          Op::template vec<V>(acc, a0, pg * V);
+        }
+      }
       for (; i + RBLOCK < nv; i += 2 * RBLOCK) {
         T a0[V], a1[V];
         ld.template vec<V>(base + i * V, a0);

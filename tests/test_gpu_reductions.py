@@ -106,6 +106,31 @@ def test_argmax_ties_and_nan(cp):
     np.testing.assert_array_equal(cp.argmax(cp.array(m), axis=0).get(), O.argmax_axis(m, 0))
 
 
+# Arrays this large take the vector loop that defers the first-occurrence
+# search to after the loop: ties between loop steps of different threads,
+# all-equal data, several NaNs, many tied extremes, a fused producer.
+def test_argmax_large_ties_and_nan(cp):
+    n = (1 << 24) + 12
+    x = np.zeros(n, np.float32)
+    assert cp.argmax(cp.array(x)) == 0 and cp.argmin(cp.array(x)) == 0
+    x[[5_000_001, 3_000_017, 9_999_999]] = 7.0
+    assert cp.argmax(cp.array(x)) == 3_000_017
+    x[[8_000_003, 4_100_000]] = np.nan
+    X = cp.array(x)
+    assert cp.argmax(X) == 4_100_000 and cp.argmin(X) == 4_100_000
+    r = np.random.default_rng(5).integers(-50, 50, n).astype(np.float32)
+    R = cp.array(r)
+    assert cp.argmax(R) == int(np.argmax(r)) and cp.argmin(R) == int(np.argmin(r))
+    assert cp.argmax(-R) == int(np.argmax(-r))
+    h = r.astype(np.float16)
+    assert cp.argmax(cp.array(h)) == int(np.argmax(h)) and cp.argmin(cp.array(h)) == int(np.argmin(h))
+    # rows: ties across the row threads' vectors, and a NaN
+    m = np.random.default_rng(6).integers(-20, 20, (64, 65536)).astype(np.float32)
+    m[3, 40000] = np.nan
+    np.testing.assert_array_equal(cp.argmax(cp.array(m), axis=1).get(), O.argmax_axis(m, 1))
+    np.testing.assert_array_equal(cp.argmin(cp.array(m), axis=1).get(), np.argmin(m, axis=1).astype(np.int32))
+
+
 def test_nan_reductions(cp):
     rng = np.random.default_rng(3)
     a = rng.standard_normal((300, 500)).astype(np.float32)

@@ -145,3 +145,38 @@ def test_long_rows_carry_prod_and_dtypes(cp):
     assert gh.dtype == np.float16
     href = np.cumsum(h.astype(np.float64))
     assert np.max(np.abs(gh.astype(np.float64) - href) / np.maximum(href, 1e-3)) <= 2e-3
+
+
+# The persistent round kernel with many rows per round: rows that start
+# inside a round, rows of a single tile, ragged last tiles, rows that span
+# several rounds.
+@pytest.mark.parametrize("rows,k", [(300, 65536), (1000, 8192 + 16), (5000, 4096), (700, 3 * 4096 + 16),
+                                    (3, (1 << 21) + 32)])
+def test_round_kernel_rows(cp, rows, k):
+    rng = np.random.default_rng(rows * 7 + k)
+    x = rng.integers(-(1 << 31), (1 << 31) - 1, (rows, k), dtype=np.int64).astype(np.int32)
+    got = cp.cumsum(cp.array(x), axis=1)
+    np.testing.assert_array_equal(got.get(), O.cumsum(x, axis=1))
+    xf = rng.standard_normal((rows, k)).astype(np.float32)
+    gf = cp.cumsum(cp.array(xf), axis=1).get()
+    ref = O.cumsum_f64(xf, axis=1)
+    floor = np.finfo(np.float32).eps * np.abs(xf.astype(np.float64)).sum(axis=1, keepdims=True)
+    assert np.max(np.abs(gf - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
+
+
+# Signed data under the stated scan bar, |y - ref| / max(|ref|, eps * sum|x|)
+# <= 1e-4 (eps: float32), at sizes the look-back kernel runs.  Float sums are
+# f64 from the first element on; with f32 sums over each thread's 16
+# elements these shapes gave 2.4e-4 to 8.7e-3.
+@pytest.mark.parametrize("shape", [(1, 1 << 20), (64, 65536), (1, 1 << 22), (3, 40000)])
+def test_signed_float_scan_bar(cp, shape):
+    xf = np.random.default_rng(shape[1] + shape[0]).standard_normal(shape).astype(np.float32)
+    gf = cp.cumsum(cp.array(xf), axis=1).get()
+    ref = O.cumsum_f64(xf, axis=1)
+    floor = np.finfo(np.float32).eps * np.abs(xf.astype(np.float64)).sum(axis=1, keepdims=True)
+    assert np.max(np.abs(gf - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
+    h = xf.astype(np.float16)
+    gh = cp.cumsum(cp.array(h), axis=1).get().astype(np.float64)
+    href = np.cumsum(h.astype(np.float64), axis=1)
+    hfloor = np.finfo(np.float16).eps * np.abs(h.astype(np.float64)).sum(axis=1, keepdims=True)
+    assert np.max(np.abs(gh - href) / np.maximum(np.abs(href), hfloor)) <= 1e-3
