@@ -85,62 +85,10 @@ int set_stage_smem() {
 constexpr long long kLongRowTiles = 64;
 constexpr long long kLongRowElements = 1ll << 24;
 
-// Input tiles each block of scan_rounds_kernel keeps in shared memory (the
-// tile being summed, the tile being written, copies in flight).
-template <class T, class O> struct RoundsNbuf { static constexpr int value = 4; };
-
-// Scans of at least kRoundsMinRounds rounds of the persistent grid take
-// scan_rounds_kernel; shorter ones keep the look-back kernel.
-constexpr long long kRoundsMinRounds = 4;
-
 template <int PRODI, class T>
 struct ScanRun {
   typedef typename ScanOut<T>::type O;
   typedef typename ScanTypes<T>::carry_t CT;
-
-  // Persistent round scan (scan_rounds_kernel): one cooperative launch of
-  // as many blocks as fit on the GPU at once.  Sets *taken = false, and
-  // launches nothing, when the scan is too short for it or the kernel does
-  // not fit.
-  static int rounds_path(const T *x, O *y, long long rows, long long k, long long tpr, long long total,
-                         const CT *cin, bool *taken) {
-    constexpr bool PROD = PRODI != 0;
-    constexpr int NB = RoundsNbuf<T, O>::value;
-    constexpr int smem = RoundsSmem<T, O, NB>();
-    auto kern = scan_rounds_kernel<T, O, PROD, NB>;
-    *taken = false;
-    static int per_sm[64];  // resident blocks per SM, per device (0 = not measured yet)
-    const int dev = current_device();
-    if (dev < 0 || dev >= 64) return MMP_OK;
-    if (!per_sm[dev]) {
-      MMP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      int n = 0;
-      MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, SBLOCK, smem));
-      per_sm[dev] = n > 0 ? n : -1;
-    }
-    if (per_sm[dev] < 0) return MMP_OK;
-    const long long G = (long long)sm_count() * per_sm[dev];
-    const long long rounds = (total + G - 1) / G;
-    if (rounds < kRoundsMinRounds) return MMP_OK;
-    cudaStream_t st = stream();
-    CT *agg = nullptr;
-    const size_t agg_bytes = ((size_t)total * sizeof(CT) + 255) & ~(size_t)255;
-    MMP_CUDA_TRY(cudaMallocAsync((void **)&agg, agg_bytes + (size_t)rounds * sizeof(unsigned), st));
-    unsigned *arrive = (unsigned *)((char *)agg + agg_bytes);
-    cudaError_t e = cudaMemsetAsync(arrive, 0, (size_t)rounds * sizeof(unsigned), st);
-    int rc = e == cudaSuccess ? MMP_OK : cuda_error(e, "cudaMemsetAsync(scan arrivals)");
-    if (!rc) {
-      int rows_is_one = rows == 1;
-      int *err = device_error_word();
-      void *args[] = {(void *)&x, (void *)&y, (void *)&k, (void *)&tpr, (void *)&total, (void *)&rounds,
-                      (void *)&agg, (void *)&arrive, (void *)&cin, (void *)&rows_is_one, (void *)&err};
-      e = cudaLaunchCooperativeKernel((const void *)kern, dim3((unsigned)G), dim3(SBLOCK), args, (size_t)smem, st);
-      if (e != cudaSuccess) rc = cuda_error(e, "scan_rounds_kernel");
-    }
-    cudaFreeAsync(agg, st);
-    if (!rc) *taken = true;
-    return rc;
-  }
 
   static int long_rows(const T *x, O *y, long long rows, long long k, long long tpr, long long total,
                        const CT *cin, int vec_ok) {
@@ -202,11 +150,6 @@ struct ScanRun {
     long long total = rows * tpr;
     if (total > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
-    if (vec_ok) {
-      bool taken = false;
-      int rc = rounds_path(x, y, rows, k, tpr, total, cin, &taken);
-      if (rc || taken) return rc;
-    }
     if (tpr >= kLongRowTiles && rows * k >= kLongRowElements) return long_rows(x, y, rows, k, tpr, total, cin, vec_ok);
     void *desc;
     unsigned *counter, epoch;

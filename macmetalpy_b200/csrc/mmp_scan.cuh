@@ -442,270 +442,6 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tile
   }
 }
 
-// ---------------------------------------------------------------------------
-// Persistent round scan for long scans: one launch, the data read from HBM
-// once.  The grid (co-resident by cooperative launch, G blocks) walks the
-// tiles in rounds: in round r block b owns tile r*G + b.  Each block keeps
-// NBUF tiles in shared memory, filled by cp.async NBUF - 1 rounds ahead of
-// use, so HBM reads stay in flight while blocks wait on one another.  In
-// every round a block
-//   1. sums its tile (the aggregate), stores it and counts itself in the
-//      round's arrival counter;
-//   2. waits until every block has counted itself in the PREVIOUS round
-//      (normally long done: it had a whole round of work to get there),
-//      folds that round's aggregates before its own tile of that round and
-//      the carry from the rounds before (every block folds the round total
-//      in the same order, so all hold the same carry), and writes that
-//      tile's outputs, staged through shared memory for 16-byte coalesced
-//      stores;
-//   3. starts the copy of the tile NBUF - 1 rounds ahead into the buffer
-//      it has just finished with.
-// Rows are segments: a tile's prefix folds only earlier tiles of its row,
-// and the carry restarts at each row's first tile.  Every wait is bounded
-// (2 s of %globaltimer); a wait that runs out sets the device error word and
-// ends the kernel (cp.async copies drained first), never a hang.
-// Inputs must be 16-byte aligned with rows that are a multiple of 16
-// elements long (every tile then starts on a 16-byte boundary and holds
-// whole 16-byte chunks).
-
-__device__ __forceinline__ unsigned smem_addr(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void cp_async16(unsigned dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// 16-byte chunk c of a tile is kept at chunk c ^ ((c >> 3) & 7) of its
-// buffer: the coalesced copy (consecutive threads, consecutive chunks) and
-// the per-thread reads (SITEMS consecutive elements, 1 to 8 chunks per
-// thread) both touch eight different bank groups per quarter warp.
-__device__ __forceinline__ int chunk_swz(int c) { return c ^ ((c >> 3) & 7); }
-
-// Shared memory of scan_rounds_kernel: NBUF input tiles, then the output stage.
-template <class T, class O, int NBUF>
-constexpr int RoundsSmem() {
-  return NBUF * STILE * (int)sizeof(T) + STILE * (int)sizeof(O);
-}
-
-// Start the copy of round r's tile of block b into buffer r % NBUF of s_mem
-// (one commit group per round, empty past the end).
-template <class T, int NBUF>
-__device__ __forceinline__ void rounds_issue(unsigned char *s_mem, const T *__restrict__ x, long long r,
-                                             long long G, long long b, long long rounds, long long k,
-                                             long long tiles_per_row, long long total_tiles) {
-  constexpr int TB = STILE * (int)sizeof(T);
-  constexpr int VE = 16 / (int)sizeof(T);
-  constexpr int CPT = SITEMS / VE;
-  const long long t = r * G + b;
-  if (r < rounds && t < total_tiles) {
-    const long long row = t / tiles_per_row, j = t - row * tiles_per_row;
-    long long count = k - j * STILE;
-    if (count > STILE) count = STILE;
-    const int nch = (int)(count / VE);
-    const unsigned base = smem_addr(s_mem + (int)(r % NBUF) * TB);
-    const char *src = reinterpret_cast<const char *>(x + row * k + j * STILE);
-#pragma unroll
-    for (int q = 0; q < CPT; ++q) {
-      const int c = q * SBLOCK + (int)threadIdx.x;
-      if (c < nch) cp_async16(base + (unsigned)chunk_swz(c) * 16u, src + (long long)c * 16);
-    }
-  }
-  cp_async_commit();
-}
-
-// This thread's SITEMS consecutive elements of the tile in buf (elements at
-// or past count read as the identity).
-template <class T, class A, bool PROD>
-__device__ __forceinline__ void rounds_read(const unsigned char *buf, long long count, A (&v)[SITEMS]) {
-  constexpr int VE = 16 / (int)sizeof(T);
-  constexpr int CPT = SITEMS / VE;
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int q = 0; q < CPT; ++q) {
-    const int c = tid * CPT + q;
-    const Vec<T, VE> t = *reinterpret_cast<const Vec<T, VE> *>(buf + chunk_swz(c) * 16);
-#pragma unroll
-    for (int e = 0; e < VE; ++e)
-      v[q * VE + e] = (c * VE + e < count) ? to_local<A, T>(t.v[e]) : ScanOp<PROD>::template id<A>();
-  }
-}
-
-__device__ __forceinline__ long long rounds_count(long long t, long long k, long long tiles_per_row) {
-  const long long j = t - (t / tiles_per_row) * tiles_per_row;
-  const long long count = k - j * STILE;
-  return count > STILE ? (long long)STILE : count;
-}
-
-template <class T, class O, bool PROD, int NBUF>
-__global__ void __launch_bounds__(SBLOCK) scan_rounds_kernel(
-    const T *__restrict__ x, O *__restrict__ y, long long k, long long tiles_per_row, long long total_tiles,
-    long long rounds, typename ScanTypes<T>::carry_t *__restrict__ agg, unsigned *__restrict__ arrive,
-    const typename ScanTypes<T>::carry_t *carry_in, int rows_is_one, int *err) {
-  typedef typename ScanTypes<T>::local_t A;
-  typedef typename ScanTypes<T>::carry_t C;
-  typedef ScanOp<PROD> Op;
-  constexpr int TB = STILE * (int)sizeof(T);  // bytes of one input tile
-  constexpr int VO = 16 / (int)sizeof(O);      // output elements per chunk
-  constexpr int CPO = SITEMS / VO;              // output chunks per thread
-  static_assert(SITEMS * sizeof(T) >= 16 && CPO >= 1 && NBUF >= 2, "tile layout");
-  extern __shared__ __align__(128) unsigned char s_mem[];
-  unsigned char *s_out = s_mem + NBUF * TB;
-  __shared__ C s_red[SBLOCK / 32];
-  __shared__ C s_pref;
-  __shared__ int s_abort;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const long long G = gridDim.x, b = blockIdx.x;
-  if (tid == 0) s_abort = 0;
-
-  const C init = (carry_in && rows_is_one) ? (C)(*carry_in) : Op::template id<C>();
-  C carry = init;  // warp 0: the carry into the next round for its first tile's row
-
-#pragma unroll 1
-  for (int q = 0; q < NBUF - 1; ++q) rounds_issue<T, NBUF>(s_mem, x, q, G, b, rounds, k, tiles_per_row, total_tiles);
-
-#pragma unroll 1
-  for (long long r = 0; r <= rounds; ++r) {
-    // ---- 1. aggregate of this round's tile
-    if (r < rounds) {
-      cp_async_wait<NBUF - 2>();
-      __syncthreads();  // every thread's chunks of round r have landed
-      const long long t = r * G + b;
-      C part = Op::template id<C>();
-      if (t < total_tiles) {
-        A v[SITEMS];
-        rounds_read<T, A, PROD>(s_mem + (int)(r % NBUF) * TB, rounds_count(t, k, tiles_per_row), v);
-        A s = v[0];
-#pragma unroll
-        for (int e = 1; e < SITEMS; ++e) s = Op::op(s, v[e]);
-        part = (C)s;
-      }
-#pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) part = Op::op(part, __shfl_xor_sync(0xffffffffu, part, d));
-      if (lane == 0) s_red[w] = part;
-      __syncthreads();
-      if (tid == 0) {
-        C a = s_red[0];
-#pragma unroll
-        for (int q = 1; q < SBLOCK / 32; ++q) a = Op::op(a, s_red[q]);
-        if (t < total_tiles) agg[t] = a;
-        __threadfence();
-        atomicAdd(arrive + r, 1u);
-      }
-    }
-    // ---- 2. outputs of the previous round's tile
-    if (r >= 1) {
-      const long long rq = r - 1;
-      const long long rs = rq * G;
-      const long long re = rs + G < total_tiles ? rs + G : total_tiles;
-      const long long t = rs + b;
-      if (w == 0) {
-        int ok = 1;
-        if (lane == 0 && ld_acquire_u32(arrive + rq) < (unsigned)G) {
-          const unsigned long long t0 = global_ns();
-          unsigned ns = 32;
-          for (long long it = 0; ld_acquire_u32(arrive + rq) < (unsigned)G; ++it) {
-            if (it >= (1ll << 24) || global_ns() - t0 > 2000000000ull) {
-              atomicExch(err, 2);  // a scan wait ran out
-              ok = 0;
-              break;
-            }
-            __nanosleep(ns);
-            if (ns < 256) ns <<= 1;
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        __syncwarp();  // the other lanes' reads of the aggregates follow lane 0's acquire
-        // the carry into this round for the row of its first tile
-        const C ceff = (rs % tiles_per_row == 0) ? (rs == 0 ? init : Op::template id<C>()) : carry;
-        const long long row_lo = t < total_tiles ? (t / tiles_per_row) * tiles_per_row : re;
-        const long long lo = row_lo > rs ? row_lo : rs;
-        const long long row_lo2 = ((re - 1) / tiles_per_row) * tiles_per_row;
-        const long long lo2 = row_lo2 > rs ? row_lo2 : rs;
-        C s1 = Op::template id<C>(), s2 = Op::template id<C>();
-        if (ok) {
-          // lanes take the round's aggregates by position from rs, so every
-          // block folds the carry s2 in the same order
-          for (long long u = rs + lane; u < re; u += 32) {
-            const C a = __ldcg(agg + u);
-            if (u >= lo && u < t) s1 = Op::op(s1, a);
-            if (u >= lo2) s2 = Op::op(s2, a);
-          }
-        }
-#pragma unroll
-        for (int d = 16; d >= 1; d >>= 1) {
-          s1 = Op::op(s1, __shfl_xor_sync(0xffffffffu, s1, d));
-          s2 = Op::op(s2, __shfl_xor_sync(0xffffffffu, s2, d));
-        }
-        if (lo == rs) s1 = Op::op(ceff, s1);
-        if (lo2 == rs) s2 = Op::op(ceff, s2);
-        carry = s2;
-        if (lane == 0) {
-          s_pref = s1;
-          if (!ok) s_abort = 1;
-        }
-      }
-      __syncthreads();
-      if (s_abort) break;
-      if (t < total_tiles) {
-        const long long count = rounds_count(t, k, tiles_per_row);
-        const long long row = t / tiles_per_row;
-        O *dst = y + row * k + (t - row * tiles_per_row) * STILE;
-        A v[SITEMS];
-        rounds_read<T, A, PROD>(s_mem + (int)(rq % NBUF) * TB, count, v);
-#pragma unroll
-        for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
-        C inc = (C)v[SITEMS - 1];
-#pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-          const C o = __shfl_up_sync(0xffffffffu, inc, d);
-          if (lane >= d) inc = Op::op(o, inc);
-        }
-        if (lane == 31) s_red[w] = inc;
-        __syncthreads();
-        C warp_excl = Op::template id<C>();
-#pragma unroll
-        for (int q = 0; q < SBLOCK / 32; ++q)
-          if (q < w) warp_excl = Op::op(warp_excl, s_red[q]);
-        const C o = __shfl_up_sync(0xffffffffu, inc, 1);
-        const C base = Op::op(s_pref, Op::op(warp_excl, lane == 0 ? Op::template id<C>() : o));
-#pragma unroll
-        for (int q = 0; q < CPO; ++q) {
-          Vec<O, VO> ov;
-#pragma unroll
-          for (int e = 0; e < VO; ++e) ov.v[e] = cvt<O>(Op::op(base, (C)v[q * VO + e]));
-          *reinterpret_cast<Vec<O, VO> *>(s_out + chunk_swz(tid * CPO + q) * 16) = ov;
-        }
-        __syncthreads();
-        const int nch = (int)(count / VO);
-#pragma unroll
-        for (int q = 0; q < CPO; ++q) {
-          const int c = q * SBLOCK + tid;
-          if (c < nch)
-            stvec_stream<O, VO>(dst + (long long)c * VO,
-                                *reinterpret_cast<const Vec<O, VO> *>(s_out + chunk_swz(c) * 16));
-        }
-      }
-    }
-    __syncthreads();  // buffer (r - 1) % NBUF and the stage are free
-    rounds_issue<T, NBUF>(s_mem, x, r + NBUF - 1, G, b, rounds, k, tiles_per_row, total_tiles);
-  }
-  cp_async_wait_all();
-}
-
 // One warp per row for short rows (k < STILE / 4).
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,

@@ -147,12 +147,12 @@ def test_long_rows_carry_prod_and_dtypes(cp):
     assert np.max(np.abs(gh.astype(np.float64) - href) / np.maximum(href, 1e-3)) <= 2e-3
 
 
-# The persistent round kernel with many rows per round: rows that start
-# inside a round, rows of a single tile, ragged last tiles, rows that span
-# several rounds.
+# Many rows under the stated scan bar: rows of one tile, ragged last tiles,
+# rows of a few tiles and of hundreds; full-range int32 keeps the carries
+# exact in int64.
 @pytest.mark.parametrize("rows,k", [(300, 65536), (1000, 8192 + 16), (5000, 4096), (700, 3 * 4096 + 16),
                                     (3, (1 << 21) + 32)])
-def test_round_kernel_rows(cp, rows, k):
+def test_many_rows(cp, rows, k):
     rng = np.random.default_rng(rows * 7 + k)
     x = rng.integers(-(1 << 31), (1 << 31) - 1, (rows, k), dtype=np.int64).astype(np.int32)
     got = cp.cumsum(cp.array(x), axis=1)
