@@ -619,13 +619,15 @@ static int launch(const CUtensorMap &mA0, const CUtensorMap &mA1, const CUtensor
   // float16: persistent, one CTA per SM (the stage ring fills shared
   // memory), tiles handed out round-robin -- the next tile's MMAs overlap
   // this tile's epilogue (measured 2-8 % faster than a CTA per tile).  The
-  // TF32 modes launch one CTA per tile (the tile loop runs once): their
-  // epilogue already overlaps the chunked MMAs, and the hardware's dynamic
-  // CTA order kept L2 reuse better (16384^3 3xTF32 measured 11 % slower
-  // with the static round-robin order).
+  // TF32 modes are persistent too while K <= 8192 (a tile's fill and drain
+  // are then a visible share of it: batched 64 x 1024^3 3xTF32 139.5 ->
+  // 147.1 TFLOP/s, 4096^3 and 8192^3 +1 %); longer K launches one CTA per
+  // tile, whose dynamic hardware order kept L2 reuse better (16384^3
+  // 3xTF32 measured 11 % slower with the static round-robin order).
   const long long tiles = m_blocks * n_blocks * batch;
   const long long sms = (long long)mmp::sm_count();
-  const long long ctas = (MODE == MODE_F16 && tiles > sms) ? sms : tiles;
+  const bool persistent = MODE == MODE_F16 || k_tiles * G::BK <= 8192;
+  const long long ctas = (persistent && tiles > sms) ? sms : tiles;
   if (ctas > 0x7fffffffll) return mmp::set_error(MMP_E_UNSUPPORTED, "GEMM too large for one launch");
   gemm_tc_kernel<MODE, B_MN><<<(unsigned)ctas, G::THREADS, G::SMEM, st>>>(
       mA0, mA1, mB0, mB1, c, m, n, ldc, sc, (int)m_blocks, (int)n_blocks, (int)k_tiles, (int)batch, a_bc, b_bc,
