@@ -422,17 +422,18 @@ struct ArgOp {
       for (int j = 0; j < V; ++j) one(a, v[j], base + j);
     }
   }
-  // Deferred first-occurrence search (float / half): the loop keeps only
-  // the running extreme pm and the loop step g whose vectors first reached
-  // it, branch-free; the element index inside that step is searched once
-  // after the loop (the kernel reloads the step's vectors and hands them to
-  // vec4 / vec).  Searching inside the loop cost the whole warp a divergent
-  // search whenever any one lane found a new extreme -- nearly every step
-  // early on.
+  // Deferred first-occurrence search (float / half): the loop keeps the
+  // running extreme pm, the first of its step's four vectors that holds it
+  // (values in pv, first element index pg), branch-free; the index inside
+  // that vector is searched once after the loop.  Searching inside the loop
+  // cost the whole warp a divergent search whenever any one lane found a
+  // new extreme -- nearly every step early on; reloading the step after the
+  // loop instead of keeping pv cost a DRAM burst per 16-byte vector (27 %
+  // more DRAM reads at 2^26 float32).
   static constexpr bool kGroupDeferred = IsFloat<T>::value && sizeof(T) <= 4;
   template <int V>
-  __device__ static void group_step(float &pm, long long &pg, const T (&v0)[V], const T (&v1)[V],
-                                    const T (&v2)[V], const T (&v3)[V], long long g) {
+  __device__ static void group_step(float &pm, long long &pg, T (&pv)[V], const T (&v0)[V], const T (&v1)[V],
+                                    const T (&v2)[V], const T (&v3)[V], long long g0, long long step) {
     float m0 = AsF<T>::f(v0[0]), m1 = AsF<T>::f(v1[0]), m2 = AsF<T>::f(v2[0]), m3 = AsF<T>::f(v3[0]);
 #pragma unroll
     for (int j = 1; j < V; ++j) {
@@ -442,10 +443,20 @@ struct ArgOp {
       m3 = MAX ? max_nan(m3, AsF<T>::f(v3[j])) : min_nan(m3, AsF<T>::f(v3[j]));
     }
     const float m = MAX ? max_nan(max_nan(m0, m1), max_nan(m2, m3)) : min_nan(min_nan(m0, m1), min_nan(m2, m3));
+    const bool mn = isnan_(m);
     // the same rule as vec4: a strictly better value or the first NaN
-    const bool take = (pg < 0) || (!isnan_(pm) && (isnan_(m) || (MAX ? (m > pm) : (m < pm))));
+    const bool take = (pg < 0) || (!isnan_(pm) && (mn || (MAX ? (m > pm) : (m < pm))));
+    // the first of the four vectors whose extreme is m
+    const bool h0 = mn ? isnan_(m0) : (m0 == m), h1 = mn ? isnan_(m1) : (m1 == m),
+               h2 = mn ? isnan_(m2) : (m2 == m);
+    const int jv = h0 ? 0 : h1 ? 1 : h2 ? 2 : 3;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const T x = jv == 0 ? v0[e] : jv == 1 ? v1[e] : jv == 2 ? v2[e] : v3[e];
+      pv[e] = take ? x : pv[e];
+    }
     pm = take ? m : pm;
-    pg = take ? g : pg;
+    pg = take ? g0 + (long long)jv * step : pg;
   }
   // the same for one vector per step (the row kernels)
   template <int V>
@@ -884,7 +895,10 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
     long long i = tid;
     if constexpr (HasGroupDeferred<Op>::value) {
       float pm = 0.0f;
-      long long pg = -1;  // first vector index of the best loop step so far
+      long long pg = -1;  // first element index of the vector holding the best value so far
+      T pv[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) pv[e] = T(0);
       for (; i + 3 * nth < nv; i += 4 * nth) {
         typename L::template Raw<V> r0, r1, r2, r3;
         ld.template load<V>(i * V, r0);
@@ -896,16 +910,9 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
         ld.template apply<V>(r1, a1);
         ld.template apply<V>(r2, a2);
         ld.template apply<V>(r3, a3);
-        Op::template group_step<V>(pm, pg, a0, a1, a2, a3, i);
+        Op::template group_step<V>(pm, pg, pv, a0, a1, a2, a3, i * V, nth * V);
       }
-      if (pg >= 0) {  // the exact first index inside the best step
-        T a0[V], a1[V], a2[V], a3[V];
-        ld.template vec<V>(pg * V, a0);
-        ld.template vec<V>((pg + nth) * V, a1);
-        ld.template vec<V>((pg + 2 * nth) * V, a2);
-        ld.template vec<V>((pg + 3 * nth) * V, a3);
-        Op::template vec4<V>(acc, a0, a1, a2, a3, pg * V, nth * V);
-      }
+      if (pg >= 0) Op::template vec<V>(acc, pv, pg);  // the exact first index inside the vector
     }
     for (; i + 3 * nth < nv; i += 4 * nth) {
       typename L::template Raw<V> r0, r1, r2, r3;

@@ -79,10 +79,11 @@ int set_stage_smem() {
 // (tile_aggregates_kernel, a scan of the aggregates, scan_tiles_carry_kernel)
 // instead of the look-back kernel, whose chain of waits grows with the row.
 // Measured on B200: int32 -> int64 over 2^30 elements 4.6 TB/s against
-// 3.5 TB/s, float32 4.3 against 3.5; rows of 16 tiles (4096 x 65536) and
-// scans below ~2^24 elements (three launches, a pool allocation) stay
-// faster on the look-back kernel.
-constexpr long long kLongRowTiles = 64;
+// 3.5 TB/s; float32 (f64 sums) 3.84; rows of 16 tiles (4096 x 65536
+// float32) 3.71 against 3.35 on the look-back kernel.  Scans below ~2^24
+// elements (three launches, a pool allocation) stay on the look-back
+// kernel.
+constexpr long long kLongRowTiles = 16;
 constexpr long long kLongRowElements = 1ll << 24;
 
 template <int PRODI, class T>
