@@ -114,19 +114,62 @@ __device__ __forceinline__ unsigned wait_desc(const TileDesc<C> *desc, long long
   return (unsigned)(f & 3ull);
 }
 
-// Shared-memory index with one padding element per 128 bytes.
-template <class E>
-__device__ __forceinline__ int spad(int i) {
-  return i + i / (int)(128 / sizeof(E));
-}
-template <class E>
-struct StageBytes {
-  static constexpr int value = (STILE + STILE / (128 / sizeof(E))) * sizeof(E);
-};
+// Tile staging through shared memory in 16-byte chunks.  Chunk c of a tile
+// (elements c*16/sizeof(E) ...) is kept at chunk c ^ ((c >> 3) & 7): the
+// coalesced global side (consecutive threads, consecutive chunks) and the
+// per-thread side (a thread's SITEMS consecutive elements, 1 to 8 chunks)
+// both reach eight different bank groups per quarter warp, with one 16-byte
+// shared-memory access per chunk instead of one per element.
+__device__ __forceinline__ int chunk_swz(int c) { return c ^ ((c >> 3) & 7); }
 
 template <class T, class O>
 constexpr int StageSize() {
-  return StageBytes<T>::value > StageBytes<O>::value ? StageBytes<T>::value : StageBytes<O>::value;
+  return STILE * (int)(sizeof(T) > sizeof(O) ? sizeof(T) : sizeof(O));
+}
+
+// the whole tile (STILE elements from src, 16-byte aligned) into the stage
+template <class T>
+__device__ __forceinline__ void stage_load_tile(unsigned char *stage, const T *__restrict__ src) {
+  constexpr int VE = 16 / (int)sizeof(T);
+#pragma unroll
+  for (int q = 0; q < SITEMS / VE; ++q) {
+    const int c = q * SBLOCK + (int)threadIdx.x;
+    *reinterpret_cast<Vec<T, VE> *>(stage + chunk_swz(c) * 16) = ldvec_stream<T, VE>(src + (long long)c * VE);
+  }
+}
+// this thread's SITEMS consecutive elements out of the stage
+template <class T, class A>
+__device__ __forceinline__ void stage_read_thread(const unsigned char *stage, A (&v)[SITEMS]) {
+  constexpr int VE = 16 / (int)sizeof(T);
+#pragma unroll
+  for (int q = 0; q < SITEMS / VE; ++q) {
+    const Vec<T, VE> t =
+        *reinterpret_cast<const Vec<T, VE> *>(stage + chunk_swz((int)threadIdx.x * (SITEMS / VE) + q) * 16);
+#pragma unroll
+    for (int e = 0; e < VE; ++e) v[q * VE + e] = to_local<A, T>(t.v[e]);
+  }
+}
+// this thread's SITEMS consecutive outputs into the stage
+template <class O>
+__device__ __forceinline__ void stage_write_thread(unsigned char *stage, const O (&r)[SITEMS]) {
+  constexpr int VO = 16 / (int)sizeof(O);
+#pragma unroll
+  for (int q = 0; q < SITEMS / VO; ++q) {
+    Vec<O, VO> t;
+#pragma unroll
+    for (int e = 0; e < VO; ++e) t.v[e] = r[q * VO + e];
+    *reinterpret_cast<Vec<O, VO> *>(stage + chunk_swz((int)threadIdx.x * (SITEMS / VO) + q) * 16) = t;
+  }
+}
+// the whole staged tile out to dst (16-byte aligned), coalesced
+template <class O>
+__device__ __forceinline__ void stage_store_tile(const unsigned char *stage, O *__restrict__ dst) {
+  constexpr int VO = 16 / (int)sizeof(O);
+#pragma unroll
+  for (int q = 0; q < SITEMS / VO; ++q) {
+    const int c = q * SBLOCK + (int)threadIdx.x;
+    stvec_stream<O, VO>(dst + (long long)c * VO, *reinterpret_cast<const Vec<O, VO> *>(stage + chunk_swz(c) * 16));
+  }
 }
 
 // Resident blocks per SM the tile kernels are compiled for: the look-back
@@ -160,25 +203,16 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tile
   if (count > STILE) count = STILE;
   const unsigned ep = epoch & 0x3fffffffu;
 
-  // ---- load the tile: coalesced 16-byte vectors into shared memory (one
-  // padding element per 128 bytes keeps both access patterns free of bank
-  // conflicts), then SITEMS consecutive elements per thread
+  // ---- load the tile: coalesced 16-byte vectors into shared memory
+  // (swizzled 16-byte chunks, see chunk_swz), then SITEMS consecutive
+  // elements per thread
   A v[SITEMS];
   const long long my0 = (long long)tid * SITEMS;
   const bool full_vec = vec_ok && count == STILE;
   if (full_vec) {
-    T *smT = reinterpret_cast<T *>(s_stage);
-    constexpr int VE = (16 / sizeof(T)) < SITEMS ? (16 / sizeof(T)) : SITEMS;
-#pragma unroll
-    for (int q = 0; q < SITEMS / VE; ++q) {
-      const int i0 = (q * SBLOCK + tid) * VE;
-      Vec<T, VE> t = ldvec_stream<T, VE>(x + start + i0);
-#pragma unroll
-      for (int e = 0; e < VE; ++e) smT[spad<T>(i0 + e)] = t.v[e];
-    }
+    stage_load_tile<T>(s_stage, x + start);
     __syncthreads();
-#pragma unroll
-    for (int e = 0; e < SITEMS; ++e) v[e] = to_local<A, T>(smT[spad<T>(tid * SITEMS + e)]);
+    stage_read_thread<T, A>(s_stage, v);
   } else {
 #pragma unroll
     for (int e = 0; e < SITEMS; ++e) {
@@ -267,20 +301,10 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tile
   for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(base, (C)v[e]));
   if (full_vec) {
     // stage the outputs through shared memory, write 16-byte vectors
-    O *smO = reinterpret_cast<O *>(s_stage);
     __syncthreads();  // every thread has finished reading its inputs
-#pragma unroll
-    for (int e = 0; e < SITEMS; ++e) smO[spad<O>(tid * SITEMS + e)] = res[e];
+    stage_write_thread<O>(s_stage, res);
     __syncthreads();
-    constexpr int VO = (16 / sizeof(O)) < SITEMS ? (16 / sizeof(O)) : SITEMS;
-#pragma unroll
-    for (int q = 0; q < SITEMS / VO; ++q) {
-      const int i0 = (q * SBLOCK + tid) * VO;
-      Vec<O, VO> t;
-#pragma unroll
-      for (int e = 0; e < VO; ++e) t.v[e] = smO[spad<O>(i0 + e)];
-      stvec_stream<O, VO>(y + start + i0, t);
-    }
+    stage_store_tile<O>(s_stage, y + start);
   } else {
 #pragma unroll
     for (int e = 0; e < SITEMS; ++e) {
@@ -378,18 +402,9 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tile
   const long long my0 = (long long)tid * SITEMS;
   const bool full_vec = vec_ok && count == STILE;
   if (full_vec) {
-    T *smT = reinterpret_cast<T *>(s_stage);
-    constexpr int VE = (16 / sizeof(T)) < SITEMS ? (16 / sizeof(T)) : SITEMS;
-#pragma unroll
-    for (int q = 0; q < SITEMS / VE; ++q) {
-      const int i0 = (q * SBLOCK + tid) * VE;
-      Vec<T, VE> t = ldvec_stream<T, VE>(x + start + i0);
-#pragma unroll
-      for (int e = 0; e < VE; ++e) smT[spad<T>(i0 + e)] = t.v[e];
-    }
+    stage_load_tile<T>(s_stage, x + start);
     __syncthreads();
-#pragma unroll
-    for (int e = 0; e < SITEMS; ++e) v[e] = to_local<A, T>(smT[spad<T>(tid * SITEMS + e)]);
+    stage_read_thread<T, A>(s_stage, v);
   } else {
 #pragma unroll
     for (int e = 0; e < SITEMS; ++e) {
@@ -420,19 +435,12 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tile
 
   // ---- outputs: carry and thread prefix (C) + thread-local prefix (A)
   if (full_vec) {
-    O *smO = reinterpret_cast<O *>(s_stage);
+    O res[SITEMS];
 #pragma unroll
-    for (int e = 0; e < SITEMS; ++e) smO[spad<O>(tid * SITEMS + e)] = cvt<O>(Op::op(excl, (C)v[e]));
+    for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
+    stage_write_thread<O>(s_stage, res);
     __syncthreads();
-    constexpr int VO = (16 / sizeof(O)) < SITEMS ? (16 / sizeof(O)) : SITEMS;
-#pragma unroll
-    for (int q = 0; q < SITEMS / VO; ++q) {
-      const int i0 = (q * SBLOCK + tid) * VO;
-      Vec<O, VO> t;
-#pragma unroll
-      for (int e = 0; e < VO; ++e) t.v[e] = smO[spad<O>(i0 + e)];
-      stvec_stream<O, VO>(y + start + i0, t);
-    }
+    stage_store_tile<O>(s_stage, y + start);
   } else {
 #pragma unroll
     for (int e = 0; e < SITEMS; ++e) {
