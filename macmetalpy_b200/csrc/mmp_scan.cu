@@ -72,6 +72,26 @@ int set_stage_smem() {
   return MMP_OK;
 }
 
+// Resident blocks per SM of scan_carry_stream_kernel (its shared memory
+// raised past the 48 KB default once per device), for its persistent grid.
+template <class T, class O, bool PROD>
+int stream_blocks_per_sm(int *out) {
+  static int per_sm[64];
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
+  if (!per_sm[dev]) {
+    MMP_CUDA_TRY(cudaFuncSetAttribute(scan_carry_stream_kernel<T, O, PROD>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, StreamSmem<T, O>()));
+    int n = 0;
+    MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_carry_stream_kernel<T, O, PROD>, SBLOCK,
+                                                               StreamSmem<T, O>()));
+    if (n < 1) return set_error(MMP_E_CUDA, "scan_carry_stream_kernel does not fit on an SM");
+    per_sm[dev] = n;
+  }
+  *out = per_sm[dev];
+  return MMP_OK;
+}
+
 }  // namespace
 
 // Rows of at least kLongRowTiles tiles, in scans of at least
@@ -107,12 +127,26 @@ struct ScanRun {
     // the aggregates are scanned per row by this same library (CT is its
     // own accumulation type), with the caller's carry
     if (!rc) rc = ScanRun<PRODI, CT>::run(agg, ScanOut<CT>::code, incl, rows, tpr, 1, cin);
-    if (!rc) rc = set_stage_smem<T, O, PROD>();
-    if (!rc) {
-      scan_tiles_carry_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, StageSize<T, O>(), st>>>(
-          x, y, rows, k, tpr, total, incl, cin, vec_ok);
-      e = cudaGetLastError();
-      if (e != cudaSuccess) rc = cuda_error(e, "scan_tiles_carry_kernel");
+    if (!rc && vec_ok) {
+      // aligned: the persistent streaming carry scan, as many blocks as fit
+      int per_sm = 0;
+      rc = stream_blocks_per_sm<T, O, PROD>(&per_sm);
+      if (!rc) {
+        long long g = (long long)sm_count() * per_sm;
+        if (g > total) g = total;
+        scan_carry_stream_kernel<T, O, PROD><<<(unsigned)g, SBLOCK, StreamSmem<T, O>(), st>>>(
+            x, y, rows, k, tpr, total, incl, cin);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) rc = cuda_error(e, "scan_carry_stream_kernel");
+      }
+    } else {
+      if (!rc) rc = set_stage_smem<T, O, PROD>();
+      if (!rc) {
+        scan_tiles_carry_kernel<T, O, PROD><<<(unsigned)total, SBLOCK, StageSize<T, O>(), st>>>(
+            x, y, rows, k, tpr, total, incl, cin, vec_ok);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) rc = cuda_error(e, "scan_tiles_carry_kernel");
+      }
     }
     cudaFreeAsync(agg, st);
     return rc;

@@ -450,6 +450,134 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_tile
   }
 }
 
+// Streaming variant of scan_tiles_carry_kernel for aligned scans (rows a
+// multiple of 16 elements, 16-byte aligned input and output): a persistent
+// grid, block b taking tiles total-1-b, total-1-b-G, ... (highest first, as
+// scan_tiles_carry_kernel), with the next tile's input copied into shared
+// memory by cp.async while the current tile is scanned and stored.  Tiles
+// depend on nothing but their known prefix, so no block waits on another;
+// each block keeps a tile's load in flight at all times instead of loading,
+// scanning and storing in turn.
+__device__ __forceinline__ void cp_async16(unsigned dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Shared memory of scan_carry_stream_kernel: two input tiles, then the output stage.
+template <class T, class O>
+constexpr int StreamSmem() {
+  return 2 * STILE * (int)sizeof(T) + STILE * (int)sizeof(O);
+}
+
+// Start the copy of tile `tile` (skipped when negative) into buf, as
+// swizzled 16-byte chunks; one commit group either way.
+template <class T>
+__device__ __forceinline__ void stream_issue(unsigned char *buf, const T *__restrict__ x, long long tile, long long k,
+                                             long long tiles_per_row) {
+  constexpr int VE = 16 / (int)sizeof(T);
+  if (tile >= 0) {
+    const long long row = tile / tiles_per_row, j = tile - row * tiles_per_row;
+    long long count = k - j * STILE;
+    if (count > STILE) count = STILE;
+    const int nch = (int)(count / VE);
+    const unsigned base = (unsigned)__cvta_generic_to_shared(buf);
+    const char *src = reinterpret_cast<const char *>(x + row * k + j * STILE);
+#pragma unroll
+    for (int q = 0; q < SITEMS / VE; ++q) {
+      const int c = q * SBLOCK + (int)threadIdx.x;
+      if (c < nch) cp_async16(base + (unsigned)chunk_swz(c) * 16u, src + (long long)c * 16);
+    }
+  }
+  cp_async_commit();
+}
+
+template <class T, class O, bool PROD>
+__global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_carry_stream_kernel(
+    const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tiles_per_row,
+    long long total_tiles, const typename ScanTypes<T>::carry_t *__restrict__ incl,
+    const typename ScanTypes<T>::carry_t *carry_in) {
+  typedef typename ScanTypes<T>::local_t A;
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> Op;
+  constexpr int TB = STILE * (int)sizeof(T);
+  constexpr int VE = 16 / (int)sizeof(T);
+  constexpr int VO = 16 / (int)sizeof(O);
+  __shared__ C s_warp[SBLOCK / 32];
+  extern __shared__ __align__(128) unsigned char s_mem[];  // StreamSmem<T, O>() bytes
+  unsigned char *s_out = s_mem + 2 * TB;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const long long G = gridDim.x;
+  const long long first = total_tiles - 1 - (long long)blockIdx.x;
+
+  stream_issue<T>(s_mem, x, first, k, tiles_per_row);
+#pragma unroll 1
+  for (long long i = 0;; ++i) {
+    const long long tile = first - i * G;
+    if (tile < 0) break;
+    const long long next = tile - G;
+    // the other buffer was last read before the previous iteration's final barrier
+    stream_issue<T>(s_mem + (int)((i + 1) & 1) * TB, x, next, k, tiles_per_row);
+    const long long row = tile / tiles_per_row;
+    const long long j = tile - row * tiles_per_row;
+    const long long start = row * k + j * STILE;
+    long long count = k - j * STILE;
+    if (count > STILE) count = STILE;
+    C excl = Op::template id<C>();
+    if (j > 0) excl = incl[tile - 1];
+    else if (carry_in && rows == 1) excl = (C)(*carry_in);
+    cp_async_wait1();  // this tile's group has landed (the next one may still be in flight)
+    __syncthreads();
+
+    // ---- this thread's SITEMS consecutive elements (past count: identity)
+    A v[SITEMS];
+    const unsigned char *buf = s_mem + (int)(i & 1) * TB;
+#pragma unroll
+    for (int q = 0; q < SITEMS / VE; ++q) {
+      const int c = tid * (SITEMS / VE) + q;
+      const Vec<T, VE> t = *reinterpret_cast<const Vec<T, VE> *>(buf + chunk_swz(c) * 16);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) v[q * VE + e] = (c * VE + e < count) ? to_local<A, T>(t.v[e]) : Op::template id<A>();
+    }
+    // ---- thread-local prefixes (A), thread totals scanned in C
+#pragma unroll
+    for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
+    C inc = (C)v[SITEMS - 1];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      C o = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc = Op::op(o, inc);
+    }
+    if (lane == 31) s_warp[w] = inc;
+    __syncthreads();
+    C warp_excl = Op::template id<C>();
+#pragma unroll
+    for (int q = 0; q < SBLOCK / 32; ++q)
+      if (q < w) warp_excl = Op::op(warp_excl, s_warp[q]);
+    {
+      C o = __shfl_up_sync(0xffffffffu, inc, 1);
+      excl = Op::op(excl, Op::op(warp_excl, (lane == 0) ? Op::template id<C>() : o));
+    }
+    // ---- outputs through the stage, 16-byte coalesced stores
+    O res[SITEMS];
+#pragma unroll
+    for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
+    stage_write_thread<O>(s_out, res);
+    __syncthreads();
+    const int nch = (int)(count / VO);
+#pragma unroll
+    for (int q = 0; q < SITEMS / VO; ++q) {
+      const int c = q * SBLOCK + tid;
+      if (c < nch)
+        stvec_stream<O, VO>(y + start + (long long)c * VO,
+                            *reinterpret_cast<const Vec<O, VO> *>(s_out + chunk_swz(c) * 16));
+    }
+    __syncthreads();  // the stage, s_warp and this tile's buffer are free
+  }
+  cp_async_wait_all();
+}
+
 // One warp per row for short rows (k < STILE / 4).
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,
