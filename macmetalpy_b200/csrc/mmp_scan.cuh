@@ -533,12 +533,18 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_carr
     // ---- this thread's SITEMS consecutive elements (past count: identity)
     A v[SITEMS];
     const unsigned char *buf = s_mem + (int)(i & 1) * TB;
+    const bool full = count == STILE;  // every tile but a row's last: no masks
+    if (full) {
+      stage_read_thread<T, A>(buf, v);
+    } else {
+      const int cnt = (int)count;
 #pragma unroll
-    for (int q = 0; q < SITEMS / VE; ++q) {
-      const int c = tid * (SITEMS / VE) + q;
-      const Vec<T, VE> t = *reinterpret_cast<const Vec<T, VE> *>(buf + chunk_swz(c) * 16);
+      for (int q = 0; q < SITEMS / VE; ++q) {
+        const int c = tid * (SITEMS / VE) + q;
+        const Vec<T, VE> t = *reinterpret_cast<const Vec<T, VE> *>(buf + chunk_swz(c) * 16);
 #pragma unroll
-      for (int e = 0; e < VE; ++e) v[q * VE + e] = (c * VE + e < count) ? to_local<A, T>(t.v[e]) : Op::template id<A>();
+        for (int e = 0; e < VE; ++e) v[q * VE + e] = (c * VE + e < cnt) ? to_local<A, T>(t.v[e]) : Op::template id<A>();
+      }
     }
     // ---- thread-local prefixes (A), thread totals scanned in C
 #pragma unroll
@@ -565,13 +571,17 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_carr
     for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
     stage_write_thread<O>(s_out, res);
     __syncthreads();
-    const int nch = (int)(count / VO);
+    if (full) {
+      stage_store_tile<O>(s_out, y + start);
+    } else {
+      const int nch = (int)(count / VO);
 #pragma unroll
-    for (int q = 0; q < SITEMS / VO; ++q) {
-      const int c = q * SBLOCK + tid;
-      if (c < nch)
-        stvec_stream<O, VO>(y + start + (long long)c * VO,
-                            *reinterpret_cast<const Vec<O, VO> *>(s_out + chunk_swz(c) * 16));
+      for (int q = 0; q < SITEMS / VO; ++q) {
+        const int c = q * SBLOCK + tid;
+        if (c < nch)
+          stvec_stream<O, VO>(y + start + (long long)c * VO,
+                              *reinterpret_cast<const Vec<O, VO> *>(s_out + chunk_swz(c) * 16));
+      }
     }
     __syncthreads();  // the stage, s_warp and this tile's buffer are free
   }
