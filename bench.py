@@ -761,8 +761,13 @@ def run_suite(cp, gen):
     # next rows: logic (fused predicate + reduction), nan-ops, sort / searchsorted
     x = gen.normal((1 << 28,), 21)
     y = (x + np.float32(1e-7)).copy()
-    out["f1_allclose_2^28"] = gbs(8 * x.size, _time(cp, lambda: cp.allclose(x, y), iters=3))
-    out["f1_count_nonzero_gt_2^28"] = gbs(4 * x.size, _time(cp, lambda: cp.count_nonzero(x > 0), iters=3))
+    # the device forms keep the result on the GPU; allclose / count_nonzero
+    # themselves return Python scalars (a read back per call): the *_pyscalar lines
+    out["f1_allclose_2^28"] = gbs(8 * x.size, _time(cp, lambda: cp.isclose(x, y).all(), iters=5))
+    out["f1_count_nonzero_gt_2^28"] = gbs(4 * x.size, _time(cp, lambda: cp.count_nonzero(x > 0, keepdims=True),
+                                                            iters=5))
+    out["f1_allclose_2^28_pyscalar"] = gbs(8 * x.size, _time(cp, lambda: cp.allclose(x, y), iters=3))
+    out["f1_count_nonzero_gt_2^28_pyscalar"] = gbs(4 * x.size, _time(cp, lambda: cp.count_nonzero(x > 0), iters=3))
     out["f4_nanvar_2^28"] = gbs(4 * x.size, _time(cp, lambda: cp.nanvar(x), iters=3))
     del y
     for n, tag in ((1 << 24, "2^24"), (1 << 28, "2^28")):
