@@ -518,11 +518,26 @@ struct ArgOp {
       vec<V>(a, v3, b0 + 3 * step);
     }
   }
+  // rows i, i + 8, i + 16, i + 24 of one column: for float / half, the
+  // NaN-propagating extreme of the four first, then one compare with the
+  // running value and selects (the same result as one() four times in row
+  // order: a strictly better value or the first NaN, first occurrence kept)
   __device__ static void four(Acc &a, T v0, T v1, T v2, T v3, long long i) {
-    one(a, v0, i);
-    one(a, v1, i + 8);
-    one(a, v2, i + 16);
-    one(a, v3, i + 24);
+    if constexpr (IsFloat<T>::value && sizeof(T) <= 4) {
+      const float x0 = AsF<T>::f(v0), x1 = AsF<T>::f(v1), x2 = AsF<T>::f(v2), x3 = AsF<T>::f(v3);
+      const float m = MAX ? max_nan(max_nan(x0, x1), max_nan(x2, x3)) : min_nan(min_nan(x0, x1), min_nan(x2, x3));
+      const bool mn = isnan_(m);
+      const bool take = (a.i < 0) || (!isnan_(a.v) && (mn || (MAX ? (m > a.v) : (m < a.v))));
+      const int j = (mn ? isnan_(x0) : (x0 == m)) ? 0 : (mn ? isnan_(x1) : (x1 == m)) ? 8
+                  : (mn ? isnan_(x2) : (x2 == m)) ? 16 : 24;
+      a.v = take ? (V_)m : a.v;
+      a.i = take ? i + j : a.i;
+    } else {
+      one(a, v0, i);
+      one(a, v1, i + 8);
+      one(a, v2, i + 16);
+      one(a, v3, i + 24);
+    }
   }
   __device__ static Acc combine(Acc a, Acc b) { return pick(a, b); }
   __device__ static void finish(Acc a, long long n, void *out, long long idx, int dt, double,
