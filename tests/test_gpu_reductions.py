@@ -129,6 +129,15 @@ def test_argmax_large_ties_and_nan(cp):
     m[3, 40000] = np.nan
     np.testing.assert_array_equal(cp.argmax(cp.array(m), axis=1).get(), O.argmax_axis(m, 1))
     np.testing.assert_array_equal(cp.argmin(cp.array(m), axis=1).get(), np.argmin(m, axis=1).astype(np.int32))
+    # columns (axis 0): four rows folded at once; tied extremes, NaNs, float16
+    c = np.random.default_rng(7).integers(-10, 10, (4099, 300)).astype(np.float32)
+    c[[5, 2000, 4000], [3, 3, 3]] = np.nan
+    c[4098, 10] = np.nan
+    c[:, 20] = 1.0
+    for arr in (c, c.astype(np.float16)):
+        C = cp.array(arr)
+        np.testing.assert_array_equal(cp.argmax(C, axis=0).get(), O.argmax_axis(arr, 0))
+        np.testing.assert_array_equal(cp.argmin(C, axis=0).get(), np.argmin(arr, axis=0).astype(np.int32))
 
 
 def test_nan_reductions(cp):
