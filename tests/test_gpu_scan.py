@@ -180,3 +180,25 @@ def test_signed_float_scan_bar(cp, shape):
     href = np.cumsum(h.astype(np.float64), axis=1)
     hfloor = np.finfo(np.float16).eps * np.abs(h.astype(np.float64)).sum(axis=1, keepdims=True)
     assert np.max(np.abs(gh - href) / np.maximum(np.abs(href), hfloor)) <= 1e-3
+
+
+# One long aligned row read once (chunked aggregator / scanner kernel): a
+# short last chunk ending in a partial tile, full-range int32 (int64 carries
+# exact), signed float32 under the scan bar, a carry-in, and cumprod.
+def test_one_row_chunked_ragged(cp):
+    from macmetalpy_b200 import reductions
+
+    n = (1 << 24) + 37 * 4096 + 48
+    rng = np.random.default_rng(91)
+    x = rng.integers(-(1 << 31), (1 << 31) - 1, n, dtype=np.int64).astype(np.int32)
+    np.testing.assert_array_equal(cp.cumsum(cp.array(x)).get(), O.cumsum(x))
+    c = cp.array(np.array([-987654321], np.int64))
+    got = reductions._scan(cp.array(x), 0, None, carry_ptr=c._ptr).get()
+    np.testing.assert_array_equal(got, -987654321 + np.cumsum(x, dtype=np.int64))
+    xf = rng.standard_normal(n).astype(np.float32)
+    gf = cp.cumsum(cp.array(xf)).get()
+    ref = O.cumsum_f64(xf)
+    floor = np.finfo(np.float32).eps * np.abs(xf.astype(np.float64)).sum()
+    assert np.max(np.abs(gf - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
+    s = rng.choice(np.array([-1, 1], np.int32), n)
+    np.testing.assert_array_equal(cp.cumprod(cp.array(s)).get(), np.cumprod(s.astype(np.int64)))
