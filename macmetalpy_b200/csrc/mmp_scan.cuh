@@ -588,278 +588,6 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_carr
   cp_async_wait_all();
 }
 
-// ---------------------------------------------------------------------------
-// Chunked scan of one long row that reads the input from HBM once.  The row
-// is cut into chunks of CT tiles; a cooperative grid splits into GA
-// aggregator blocks and GB scanner blocks.
-//   * Aggregators, one chunk ahead: block a sums the tiles of its share of
-//     chunk c (one warp per tile, 16-byte loads), stores the tile aggregates
-//     and its share's total, and counts itself in done_a[c].  Reading the
-//     chunk brings it into L2.  Before chunk c an aggregator waits until the
-//     scanners are done with chunk c - 2, so at most about two chunks of
-//     input sit in L2.
-//   * Scanners: block b owns a contiguous run of tiles of chunk c.  It waits
-//     for done_a[c] (normally long reached), folds the carry, the totals of
-//     the aggregator shares before its run and the aggregates before its
-//     first tile inside its share, then scans its tiles in turn as
-//     scan_carry_stream_kernel does: the next tile, in this chunk or the
-//     next, is copied into shared memory by cp.async (from L2) while the
-//     current one is scanned and written.  Every scanner folds the chunk's
-//     total in the same order, so all keep the same carry.
-// done_b only limits how far the aggregators run ahead (L2 room), so it is
-// counted without a fence.  Every wait is bounded (2 s of %globaltimer); a
-// wait that runs out sets the device error word and ends the block's work.
-// One row, 16-byte aligned, a multiple of 16 elements long.
-
-__device__ __forceinline__ unsigned pipe_ld_acquire(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ unsigned long long pipe_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// wait (one thread) until *p >= want; false when the wait ran out
-__device__ __forceinline__ bool pipe_wait(const unsigned *p, unsigned want, int *err) {
-  if (pipe_ld_acquire(p) >= want) return true;
-  const unsigned long long t0 = pipe_ns();
-  unsigned ns = 64;
-  for (long long it = 0; pipe_ld_acquire(p) < want; ++it) {
-    if (it >= (1ll << 24) || pipe_ns() - t0 > 2000000000ull) {
-      atomicExch(err, 2);  // a scan wait ran out
-      return false;
-    }
-    __nanosleep(ns);
-    if (ns < 512) ns <<= 1;
-  }
-  return true;
-}
-
-constexpr int PIPE_MAX_SHARE = 64;  // tiles of one aggregator share, at most
-
-template <class T, class O, bool PROD>
-__global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_pipe_kernel(
-    const T *__restrict__ x, O *__restrict__ y, long long n, long long total_tiles, long long ct,
-    long long nchunks, int ga, typename ScanTypes<T>::carry_t *__restrict__ agg,
-    typename ScanTypes<T>::carry_t *__restrict__ share_tot, unsigned *__restrict__ done_a,
-    unsigned *__restrict__ done_b, const typename ScanTypes<T>::carry_t *carry_in, int *err) {
-  typedef typename ScanTypes<T>::local_t A;
-  typedef typename ScanTypes<T>::carry_t C;
-  typedef ScanOp<PROD> Op;
-  constexpr int TB = STILE * (int)sizeof(T);
-  constexpr int VE = 16 / (int)sizeof(T);
-  constexpr int VO = 16 / (int)sizeof(O);
-  __shared__ C s_warp[SBLOCK / 32];
-  __shared__ C s_part[PIPE_MAX_SHARE];
-  __shared__ C s_pref;
-  __shared__ int s_ok;
-  extern __shared__ __align__(128) unsigned char s_mem[];  // StreamSmem<T, O>() bytes
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int gb = (int)gridDim.x - ga;
-
-  if ((int)blockIdx.x < ga) {
-    // ------------------------------------------------------ aggregator
-    const int a = blockIdx.x;
-#pragma unroll 1
-    for (long long c = 0; c < nchunks; ++c) {
-      if (c >= 2) {
-        if (tid == 0) s_ok = pipe_wait(done_b + (c - 2), (unsigned)gb, err);
-        __syncthreads();
-        if (!s_ok) return;
-      }
-      const long long cs = c * ct;
-      const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-      const long long lo = cs + (long long)a * cn / ga, hi = cs + (long long)(a + 1) * cn / ga;
-      for (long long t = lo + w; t < hi; t += SBLOCK / 32) {
-        long long count = n - t * STILE;
-        if (count > STILE) count = STILE;
-        const T *p = x + t * STILE;
-        C acc = Op::template id<C>();
-        const int nv = (int)(count / VE);
-#pragma unroll 1
-        for (int q0 = 0; q0 < STILE / VE; q0 += 32 * 8) {
-          Vec<T, VE> bv[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int q = q0 + u * 32 + lane;
-            if (q < nv) bv[u] = ldvec<T, VE>(p + (long long)q * VE);
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int q = q0 + u * 32 + lane;
-            if (q < nv) {
-              A s = to_local<A, T>(bv[u].v[0]);
-#pragma unroll
-              for (int e = 1; e < VE; ++e) s = Op::op(s, to_local<A, T>(bv[u].v[e]));
-              acc = Op::op(acc, (C)s);
-            }
-          }
-        }
-#pragma unroll
-        for (int d = 16; d >= 1; d >>= 1) acc = Op::op(acc, __shfl_xor_sync(0xffffffffu, acc, d));
-        if (lane == 0) {
-          agg[t] = acc;
-          s_part[t - lo] = acc;
-          __threadfence();
-        }
-      }
-      __syncthreads();
-      if (tid == 0) {
-        C s = Op::template id<C>();
-        for (long long t = lo; t < hi; ++t) s = Op::op(s, s_part[t - lo]);
-        share_tot[c * ga + a] = s;
-        __threadfence();
-        atomicAdd(done_a + c, 1u);
-      }
-      __syncthreads();  // s_part is reused by the next chunk
-    }
-    return;
-  }
-
-  // -------------------------------------------------------- scanner
-  const int b = (int)blockIdx.x - ga;
-  unsigned char *s_out = s_mem + 2 * TB;
-  C carry = (carry_in != nullptr) ? (C)(*carry_in) : Op::template id<C>();  // warp 0
-  // this block's tiles of chunk c: [first(c), last(c))
-  auto run_lo = [&](long long c) {
-    const long long cs = c * ct;
-    const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-    return cs + (long long)b * cn / gb;
-  };
-  auto run_hi = [&](long long c) {
-    const long long cs = c * ct;
-    const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-    return cs + (long long)(b + 1) * cn / gb;
-  };
-  // the tile sequence of this block across chunks, and its successor
-  long long c = 0, t = run_lo(0);
-  while (c < nchunks && t >= run_hi(c)) {
-    ++c;
-    if (c < nchunks) t = run_lo(c);
-  }
-  auto next_of = [&](long long cc, long long tt, long long &nc, long long &nt) {
-    nc = cc;
-    nt = tt + 1;
-    while (nc < nchunks && nt >= run_hi(nc)) {
-      ++nc;
-      if (nc < nchunks) nt = run_lo(nc);
-    }
-  };
-  int buf = 0;
-  if (c < nchunks) stream_issue<T>(s_mem, x, t, n, total_tiles);
-  long long cur_chunk = -1;
-#pragma unroll 1
-  while (c < nchunks) {
-    long long nc, nt;
-    next_of(c, t, nc, nt);
-    stream_issue<T>(s_mem + (buf ^ 1) * TB, x, nc < nchunks ? nt : -1, n, total_tiles);
-    if (c != cur_chunk) {
-      // chunks this block had no tiles in still move the carry
-      if (w == 0) {
-        int ok = 1;
-        for (long long cc = cur_chunk + 1; cc <= c && ok; ++cc) {
-          if (lane == 0) ok = pipe_wait(done_a + cc, (unsigned)ga, err);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          __syncwarp();
-          if (!ok) break;
-          const long long cs = cc * ct;
-          const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-          C s_all = Op::template id<C>();
-          C pre = Op::template id<C>();
-          // the aggregator share holding this block's first tile of chunk cc
-          const long long j = t - cs;
-          long long a0 = ((j + 1) * ga - 1) / cn;
-          if (a0 > ga - 1) a0 = ga - 1;
-          for (int a = lane; a < ga; a += 32) {
-            const C v = __ldcg(share_tot + cc * ga + a);
-            s_all = Op::op(s_all, v);
-            if (cc == c && a < a0) pre = Op::op(pre, v);
-          }
-          if (cc == c) {
-            const long long lo0 = cs + a0 * cn / ga;
-            for (long long u = lo0 + lane; u < t; u += 32) pre = Op::op(pre, __ldcg(agg + u));
-          }
-#pragma unroll
-          for (int d = 16; d >= 1; d >>= 1) {
-            s_all = Op::op(s_all, __shfl_xor_sync(0xffffffffu, s_all, d));
-            pre = Op::op(pre, __shfl_xor_sync(0xffffffffu, pre, d));
-          }
-          if (cc == c && lane == 0) s_pref = Op::op(carry, pre);
-          carry = Op::op(carry, s_all);
-        }
-        if (lane == 0) s_ok = ok;
-      }
-      cur_chunk = c;
-    } else {
-      if (tid == 0) s_pref = Op::op(s_pref, __ldcg(agg + t - 1));
-    }
-    cp_async_wait1();
-    __syncthreads();  // this tile's input and s_pref are ready
-    if (!s_ok) break;
-    const C excl_tile = s_pref;
-    long long count = n - t * STILE;
-    if (count > STILE) count = STILE;
-    A v[SITEMS];
-    const unsigned char *bp = s_mem + buf * TB;
-    const bool full = count == STILE;
-    if (full) {
-      stage_read_thread<T, A>(bp, v);
-    } else {
-      const int cnt = (int)count;
-#pragma unroll
-      for (int q = 0; q < SITEMS / VE; ++q) {
-        const int ch = tid * (SITEMS / VE) + q;
-        const Vec<T, VE> tv = *reinterpret_cast<const Vec<T, VE> *>(bp + chunk_swz(ch) * 16);
-#pragma unroll
-        for (int e = 0; e < VE; ++e) v[q * VE + e] = (ch * VE + e < cnt) ? to_local<A, T>(tv.v[e]) : Op::template id<A>();
-      }
-    }
-#pragma unroll
-    for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
-    C inc = (C)v[SITEMS - 1];
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      C o = __shfl_up_sync(0xffffffffu, inc, d);
-      if (lane >= d) inc = Op::op(o, inc);
-    }
-    if (lane == 31) s_warp[w] = inc;
-    __syncthreads();
-    C excl = Op::template id<C>();
-#pragma unroll
-    for (int q = 0; q < SBLOCK / 32; ++q)
-      if (q < w) excl = Op::op(excl, s_warp[q]);
-    {
-      C o = __shfl_up_sync(0xffffffffu, inc, 1);
-      excl = Op::op(excl_tile, Op::op(excl, (lane == 0) ? Op::template id<C>() : o));
-    }
-    O res[SITEMS];
-#pragma unroll
-    for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
-    stage_write_thread<O>(s_out, res);
-    __syncthreads();
-    O *dst = y + t * STILE;
-    if (full) {
-      stage_store_tile<O>(s_out, dst);
-    } else {
-      const int nch = (int)(count / VO);
-#pragma unroll
-      for (int q = 0; q < SITEMS / VO; ++q) {
-        const int ch = q * SBLOCK + tid;
-        if (ch < nch)
-          stvec_stream<O, VO>(dst + (long long)ch * VO, *reinterpret_cast<const Vec<O, VO> *>(s_out + chunk_swz(ch) * 16));
-      }
-    }
-    __syncthreads();  // stage, s_warp and this buffer are free
-    if (tid == 0 && nc != c) atomicAdd(done_b + c, 1u);  // flow control only: no fence
-    c = nc;
-    t = nt;
-    buf ^= 1;
-  }
-  cp_async_wait_all();
-}
-
 // One warp per row for short rows (k < STILE / 4).
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,

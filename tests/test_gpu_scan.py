@@ -182,9 +182,8 @@ def test_signed_float_scan_bar(cp, shape):
     assert np.max(np.abs(gh - href) / np.maximum(np.abs(href), hfloor)) <= 1e-3
 
 
-# One long aligned row read once (chunked aggregator / scanner kernel): a
-# short last chunk ending in a partial tile, full-range int32 (int64 carries
-# exact), signed float32 under the scan bar, a carry-in, and cumprod.
+# One long aligned row ending in a partial tile: full-range int32 (int64
+# carries exact), signed float32 under the scan bar, a carry-in, and cumprod.
 def test_one_row_chunked_ragged(cp):
     from macmetalpy_b200 import reductions
 
