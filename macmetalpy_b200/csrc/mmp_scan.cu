@@ -106,70 +106,10 @@ int stream_blocks_per_sm(int *out) {
 constexpr long long kLongRowTiles = 16;
 constexpr long long kLongRowElements = 1ll << 24;
 
-// One long row takes scan_pipe_kernel (input read from HBM once) when it
-// has at least kPipeMinChunks chunks of kPipeChunkTiles tiles.
-constexpr long long kPipeChunkTiles = 1024;
-constexpr long long kPipeMinChunks = 4;
-
 template <int PRODI, class T>
 struct ScanRun {
   typedef typename ScanOut<T>::type O;
   typedef typename ScanTypes<T>::carry_t CT;
-
-  // scan_pipe_kernel: one cooperative launch, one aggregator block per SM and
-  // the rest scanners.  *taken = false (nothing launched) when the row is
-  // too short or the grid does not suit the chunk size.
-  static int pipe(const T *x, O *y, long long n, long long total, const CT *cin, bool *taken) {
-    constexpr bool PROD = PRODI != 0;
-    *taken = false;
-    if (sizeof(T) == 1) return MMP_OK;  // 1-byte inputs keep reduce-then-scan (not measured here)
-    const long long ct = kPipeChunkTiles;
-    const long long nchunks = (total + ct - 1) / ct;
-    if (nchunks < kPipeMinChunks) return MMP_OK;
-    static int per_sm[64];
-    const int dev = current_device();
-    if (dev < 0 || dev >= 64) return MMP_OK;
-    auto kern = scan_pipe_kernel<T, O, PROD>;
-    if (!per_sm[dev]) {
-      MMP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, StreamSmem<T, O>()));
-      int nb = 0;
-      MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, SBLOCK, StreamSmem<T, O>()));
-      per_sm[dev] = nb > 0 ? nb : -1;
-    }
-    if (per_sm[dev] < 2) return MMP_OK;
-    const int ga = sm_count();
-    const long long g = (long long)ga * per_sm[dev];
-    const long long gb = g - ga;
-    // every scanner needs a tile of every full chunk (it counts itself in
-    // each), and an aggregator share must fit its shared-memory table
-    if (gb > ct || ct > (long long)PIPE_MAX_SHARE * ga) return MMP_OK;
-    cudaStream_t st = stream();
-    const size_t agg_b = ((size_t)total * sizeof(CT) + 255) & ~(size_t)255;
-    const size_t tot_b = ((size_t)nchunks * ga * sizeof(CT) + 255) & ~(size_t)255;
-    const size_t cnt_b = (size_t)nchunks * 2 * sizeof(unsigned);
-    char *buf = nullptr;
-    MMP_CUDA_TRY(cudaMallocAsync((void **)&buf, agg_b + tot_b + cnt_b, st));
-    CT *agg = (CT *)buf;
-    CT *share_tot = (CT *)(buf + agg_b);
-    unsigned *done_a = (unsigned *)(buf + agg_b + tot_b);
-    unsigned *done_b = done_a + nchunks;
-    cudaError_t e = cudaMemsetAsync(done_a, 0, cnt_b, st);
-    int rc = e == cudaSuccess ? MMP_OK : cuda_error(e, "cudaMemsetAsync(scan chunk counts)");
-    if (!rc) {
-      int *err = device_error_word();
-      long long ctv = ct;
-      int gav = ga;
-      void *args[] = {(void *)&x, (void *)&y, (void *)&n, (void *)&total, (void *)&ctv, (void *)&nchunks,
-                      (void *)&gav, (void *)&agg, (void *)&share_tot, (void *)&done_a, (void *)&done_b,
-                      (void *)&cin, (void *)&err};
-      e = cudaLaunchCooperativeKernel((const void *)kern, dim3((unsigned)g), dim3(SBLOCK), args,
-                                      (size_t)StreamSmem<T, O>(), st);
-      if (e != cudaSuccess) rc = cuda_error(e, "scan_pipe_kernel");
-    }
-    cudaFreeAsync(buf, st);
-    if (!rc) *taken = true;
-    return rc;
-  }
 
   static int long_rows(const T *x, O *y, long long rows, long long k, long long tpr, long long total,
                        const CT *cin, int vec_ok) {
@@ -245,11 +185,6 @@ struct ScanRun {
     long long total = rows * tpr;
     if (total > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
-    if (vec_ok && rows == 1) {
-      bool taken = false;
-      int rc = pipe(x, y, k, total, cin, &taken);
-      if (rc || taken) return rc;
-    }
     if (tpr >= kLongRowTiles && rows * k >= kLongRowElements) return long_rows(x, y, rows, k, tpr, total, cin, vec_ok);
     void *desc;
     unsigned *counter, epoch;

@@ -588,293 +588,6 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_carr
   cp_async_wait_all();
 }
 
-// ---------------------------------------------------------------------------
-// Chunked scan of one long row that reads the input from HBM once.  The row
-// is cut into chunks of CT tiles; a cooperative grid splits into GA
-// aggregator blocks and GB scanner blocks.
-//   * Aggregators, one chunk ahead: block a streams the tiles of its share
-//     of chunk c through a ring of shared-memory tiles (cp.async, all but
-//     one in flight), sums each, stores the tile aggregates and its share's
-//     total, and counts itself in done_a[c].  Reading the
-//     chunk brings it into L2.  Before chunk c an aggregator waits until the
-//     scanners are done with chunk c - 2, so at most about two chunks of
-//     input sit in L2.
-//   * Scanners: block b owns a contiguous run of tiles of chunk c.  It waits
-//     for done_a[c] (normally long reached), folds the carry, the totals of
-//     the aggregator shares before its run and the aggregates before its
-//     first tile inside its share, then scans its tiles in turn as
-//     scan_carry_stream_kernel does: the next tile, in this chunk or the
-//     next, is copied into shared memory by cp.async (from L2) while the
-//     current one is scanned and written.  Every scanner folds the chunk's
-//     total in the same order, so all keep the same carry.
-// done_b only limits how far the aggregators run ahead (L2 room), so it is
-// counted without a fence.  Every wait is bounded (2 s of %globaltimer); a
-// wait that runs out sets the device error word and ends the block's work.
-// One row, 16-byte aligned, a multiple of 16 elements long.
-
-__device__ __forceinline__ unsigned pipe_ld_acquire(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ unsigned long long pipe_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// wait (one thread) until *p >= want; false when the wait ran out
-__device__ __forceinline__ bool pipe_wait(const unsigned *p, unsigned want, int *err) {
-  if (pipe_ld_acquire(p) >= want) return true;
-  const unsigned long long t0 = pipe_ns();
-  unsigned ns = 64;
-  for (long long it = 0; pipe_ld_acquire(p) < want; ++it) {
-    if (it >= (1ll << 24) || pipe_ns() - t0 > 2000000000ull) {
-      atomicExch(err, 2);  // a scan wait ran out
-      return false;
-    }
-    __nanosleep(ns);
-    if (ns < 512) ns <<= 1;
-  }
-  return true;
-}
-
-constexpr int PIPE_MAX_SHARE = 64;  // tiles of one aggregator share, at most
-
-template <class T, class O, bool PROD>
-__global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_pipe_kernel(
-    const T *__restrict__ x, O *__restrict__ y, long long n, long long total_tiles, long long ct,
-    long long nchunks, int ga, typename ScanTypes<T>::carry_t *__restrict__ agg,
-    typename ScanTypes<T>::carry_t *__restrict__ share_tot, unsigned *__restrict__ done_a,
-    unsigned *__restrict__ done_b, const typename ScanTypes<T>::carry_t *carry_in, int *err) {
-  typedef typename ScanTypes<T>::local_t A;
-  typedef typename ScanTypes<T>::carry_t C;
-  typedef ScanOp<PROD> Op;
-  constexpr int TB = STILE * (int)sizeof(T);
-  constexpr int VE = 16 / (int)sizeof(T);
-  constexpr int VO = 16 / (int)sizeof(O);
-  __shared__ C s_warp[SBLOCK / 32];
-  __shared__ C s_part[PIPE_MAX_SHARE];
-  __shared__ C s_pref;
-  __shared__ int s_ok;
-  extern __shared__ __align__(128) unsigned char s_mem[];  // StreamSmem<T, O>() bytes
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int gb = (int)gridDim.x - ga;
-
-  if ((int)blockIdx.x < ga) {
-    // ------------------------------------------------------ aggregator
-    // its share of each chunk streams through a ring of NA shared-memory
-    // tiles (cp.async, NA - 1 in flight), summed from there
-    constexpr int NA = StreamSmem<T, O>() / TB;
-    static_assert(NA >= 2, "aggregator ring");
-    const int a = blockIdx.x;
-#pragma unroll 1
-    for (long long c = 0; c < nchunks; ++c) {
-      if (c >= 2) {
-        if (tid == 0) s_ok = pipe_wait(done_b + (c - 2), (unsigned)gb, err);
-        __syncthreads();
-        if (!s_ok) return;
-      }
-      const long long cs = c * ct;
-      const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-      const long long lo = cs + (long long)a * cn / ga, hi = cs + (long long)(a + 1) * cn / ga;
-      const int cnt = (int)(hi - lo);
-#pragma unroll 1
-      for (int q = 0; q < NA - 1; ++q) stream_issue<T>(s_mem + (q % NA) * TB, x, q < cnt ? lo + q : -1, n, total_tiles);
-#pragma unroll 1
-      for (int jj = 0; jj < cnt; ++jj) {
-        const int nx = jj + NA - 1;
-        stream_issue<T>(s_mem + (nx % NA) * TB, x, nx < cnt ? lo + nx : -1, n, total_tiles);
-        asm volatile("cp.async.wait_group %0;" ::"n"(NA - 1) : "memory");
-        __syncthreads();  // tile jj has landed
-        const long long t = lo + jj;
-        long long count = n - t * STILE;
-        if (count > STILE) count = STILE;
-        A v[SITEMS];
-        const unsigned char *bp = s_mem + (jj % NA) * TB;
-        if (count == STILE) {
-          stage_read_thread<T, A>(bp, v);
-        } else {
-          const int cnt_e = (int)count;
-#pragma unroll
-          for (int q = 0; q < SITEMS / VE; ++q) {
-            const int ch = tid * (SITEMS / VE) + q;
-            const Vec<T, VE> tv = *reinterpret_cast<const Vec<T, VE> *>(bp + chunk_swz(ch) * 16);
-#pragma unroll
-            for (int e = 0; e < VE; ++e)
-              v[q * VE + e] = (ch * VE + e < cnt_e) ? to_local<A, T>(tv.v[e]) : Op::template id<A>();
-          }
-        }
-        A sl = v[0];
-#pragma unroll
-        for (int e = 1; e < SITEMS; ++e) sl = Op::op(sl, v[e]);
-        C part = (C)sl;
-#pragma unroll
-        for (int d = 16; d >= 1; d >>= 1) part = Op::op(part, __shfl_xor_sync(0xffffffffu, part, d));
-        if (lane == 0) s_warp[w] = part;
-        __syncthreads();  // also: every thread has read tile jj (its buffer is free)
-        if (tid == 0) {
-          C s = s_warp[0];
-#pragma unroll
-          for (int q = 1; q < SBLOCK / 32; ++q) s = Op::op(s, s_warp[q]);
-          agg[t] = s;
-          s_part[jj] = s;
-        }
-      }
-      __syncthreads();
-      if (tid == 0) {
-        C s = Op::template id<C>();
-        for (int jj = 0; jj < cnt; ++jj) s = Op::op(s, s_part[jj]);
-        share_tot[c * ga + a] = s;
-        __threadfence();  // the tile aggregates and the share total before the count
-        atomicAdd(done_a + c, 1u);
-      }
-    }
-    cp_async_wait_all();
-    return;
-  }
-
-  // -------------------------------------------------------- scanner
-  const int b = (int)blockIdx.x - ga;
-  unsigned char *s_out = s_mem + 2 * TB;
-  C carry = (carry_in != nullptr) ? (C)(*carry_in) : Op::template id<C>();  // warp 0
-  // this block's tiles of chunk c: [first(c), last(c))
-  auto run_lo = [&](long long c) {
-    const long long cs = c * ct;
-    const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-    return cs + (long long)b * cn / gb;
-  };
-  auto run_hi = [&](long long c) {
-    const long long cs = c * ct;
-    const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-    return cs + (long long)(b + 1) * cn / gb;
-  };
-  // the tile sequence of this block across chunks, and its successor
-  long long c = 0, t = run_lo(0);
-  while (c < nchunks && t >= run_hi(c)) {
-    ++c;
-    if (c < nchunks) t = run_lo(c);
-  }
-  auto next_of = [&](long long cc, long long tt, long long &nc, long long &nt) {
-    nc = cc;
-    nt = tt + 1;
-    while (nc < nchunks && nt >= run_hi(nc)) {
-      ++nc;
-      if (nc < nchunks) nt = run_lo(nc);
-    }
-  };
-  int buf = 0;
-  if (c < nchunks) stream_issue<T>(s_mem, x, t, n, total_tiles);
-  long long cur_chunk = -1;
-#pragma unroll 1
-  while (c < nchunks) {
-    long long nc, nt;
-    next_of(c, t, nc, nt);
-    stream_issue<T>(s_mem + (buf ^ 1) * TB, x, nc < nchunks ? nt : -1, n, total_tiles);
-    if (c != cur_chunk) {
-      // chunks this block had no tiles in still move the carry
-      if (w == 0) {
-        int ok = 1;
-        for (long long cc = cur_chunk + 1; cc <= c && ok; ++cc) {
-          if (lane == 0) ok = pipe_wait(done_a + cc, (unsigned)ga, err);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          __syncwarp();
-          if (!ok) break;
-          const long long cs = cc * ct;
-          const long long cn = (cs + ct < total_tiles ? cs + ct : total_tiles) - cs;
-          C s_all = Op::template id<C>();
-          C pre = Op::template id<C>();
-          // the aggregator share holding this block's first tile of chunk cc
-          const long long j = t - cs;
-          long long a0 = ((j + 1) * ga - 1) / cn;
-          if (a0 > ga - 1) a0 = ga - 1;
-          for (int a = lane; a < ga; a += 32) {
-            const C v = __ldcg(share_tot + cc * ga + a);
-            s_all = Op::op(s_all, v);
-            if (cc == c && a < a0) pre = Op::op(pre, v);
-          }
-          if (cc == c) {
-            const long long lo0 = cs + a0 * cn / ga;
-            for (long long u = lo0 + lane; u < t; u += 32) pre = Op::op(pre, __ldcg(agg + u));
-          }
-#pragma unroll
-          for (int d = 16; d >= 1; d >>= 1) {
-            s_all = Op::op(s_all, __shfl_xor_sync(0xffffffffu, s_all, d));
-            pre = Op::op(pre, __shfl_xor_sync(0xffffffffu, pre, d));
-          }
-          if (cc == c && lane == 0) s_pref = Op::op(carry, pre);
-          carry = Op::op(carry, s_all);
-        }
-        if (lane == 0) s_ok = ok;
-      }
-      cur_chunk = c;
-    } else {
-      if (tid == 0) s_pref = Op::op(s_pref, __ldcg(agg + t - 1));
-    }
-    cp_async_wait1();
-    __syncthreads();  // this tile's input and s_pref are ready
-    if (!s_ok) break;
-    const C excl_tile = s_pref;
-    long long count = n - t * STILE;
-    if (count > STILE) count = STILE;
-    A v[SITEMS];
-    const unsigned char *bp = s_mem + buf * TB;
-    const bool full = count == STILE;
-    if (full) {
-      stage_read_thread<T, A>(bp, v);
-    } else {
-      const int cnt = (int)count;
-#pragma unroll
-      for (int q = 0; q < SITEMS / VE; ++q) {
-        const int ch = tid * (SITEMS / VE) + q;
-        const Vec<T, VE> tv = *reinterpret_cast<const Vec<T, VE> *>(bp + chunk_swz(ch) * 16);
-#pragma unroll
-        for (int e = 0; e < VE; ++e) v[q * VE + e] = (ch * VE + e < cnt) ? to_local<A, T>(tv.v[e]) : Op::template id<A>();
-      }
-    }
-#pragma unroll
-    for (int e = 1; e < SITEMS; ++e) v[e] = Op::op(v[e - 1], v[e]);
-    C inc = (C)v[SITEMS - 1];
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      C o = __shfl_up_sync(0xffffffffu, inc, d);
-      if (lane >= d) inc = Op::op(o, inc);
-    }
-    if (lane == 31) s_warp[w] = inc;
-    __syncthreads();
-    C excl = Op::template id<C>();
-#pragma unroll
-    for (int q = 0; q < SBLOCK / 32; ++q)
-      if (q < w) excl = Op::op(excl, s_warp[q]);
-    {
-      C o = __shfl_up_sync(0xffffffffu, inc, 1);
-      excl = Op::op(excl_tile, Op::op(excl, (lane == 0) ? Op::template id<C>() : o));
-    }
-    O res[SITEMS];
-#pragma unroll
-    for (int e = 0; e < SITEMS; ++e) res[e] = cvt<O>(Op::op(excl, (C)v[e]));
-    stage_write_thread<O>(s_out, res);
-    __syncthreads();
-    O *dst = y + t * STILE;
-    if (full) {
-      stage_store_tile<O>(s_out, dst);
-    } else {
-      const int nch = (int)(count / VO);
-#pragma unroll
-      for (int q = 0; q < SITEMS / VO; ++q) {
-        const int ch = q * SBLOCK + tid;
-        if (ch < nch)
-          stvec_stream<O, VO>(dst + (long long)ch * VO, *reinterpret_cast<const Vec<O, VO> *>(s_out + chunk_swz(ch) * 16));
-      }
-    }
-    __syncthreads();  // stage, s_warp and this buffer are free
-    if (tid == 0 && nc != c) atomicAdd(done_b + c, 1u);  // flow control only: no fence
-    c = nc;
-    t = nt;
-    buf ^= 1;
-  }
-  cp_async_wait_all();
-}
-
 // One warp per row for short rows (k < STILE / 4).
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,
