@@ -610,11 +610,13 @@ static int launch(const CUtensorMap &mA0, const CUtensorMap &mA1, const CUtensor
                   void *c, long long m, long long n, long long ldc, long long sc, long long m_blocks,
                   long long n_blocks, long long k_tiles, long long batch, int a_bc, int b_bc, cudaStream_t st) {
   typedef Cfg<MODE> G;
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64];  // per device: function attributes are set per device
+  const int dev = mmp::current_device();
+  if (dev < 0 || dev >= 64) return mmp::set_error(MMP_E_ARG, "device out of range");
+  if (!attr[dev]) {
     MMP_CUDA_TRY(
         cudaFuncSetAttribute(gemm_tc_kernel<MODE, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
-    attr = true;
+    attr[dev] = true;
   }
   // float16: persistent, one CTA per SM (the stage ring fills shared
   // memory), tiles handed out round-robin -- the next tile's MMAs overlap

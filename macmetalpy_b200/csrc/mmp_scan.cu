@@ -58,16 +58,19 @@ template <> struct ScanOut<float> { typedef float type; static constexpr int cod
 template <> struct ScanOut<double> { typedef double type; static constexpr int code = MMP_FLOAT64; };
 
 // The tile kernel stages a tile through dynamic shared memory (more than
-// the 48 KB default for 8-byte outputs); raise the limit once per kernel.
+// the 48 KB default for 8-byte outputs); raise the limit once per kernel
+// and device (function attributes are set per device).
 template <class T, class O, bool PROD>
 int set_stage_smem() {
-  static bool done = false;
-  if (!done) {
+  static bool done[64];
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
+  if (!done[dev]) {
     MMP_CUDA_TRY(cudaFuncSetAttribute(scan_tiles_kernel<T, O, PROD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       StageSize<T, O>()));
     MMP_CUDA_TRY(cudaFuncSetAttribute(scan_tiles_carry_kernel<T, O, PROD>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, StageSize<T, O>()));
-    done = true;
+    done[dev] = true;
   }
   return MMP_OK;
 }

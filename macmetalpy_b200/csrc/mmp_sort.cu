@@ -402,10 +402,12 @@ int launch_scatter(const K *kin, K *kout, const unsigned *iin, unsigned *iout, c
                    unsigned long long n, int shift, const unsigned *cnt, const unsigned long long *inc,
                    unsigned tiles) {
   constexpr int SM = ScatterSmem<K, HI, HR>();
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64];  // per device: function attributes are set per device
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
+  if (!attr[dev]) {
     MMP_CUDA_TRY(cudaFuncSetAttribute(rs_scatter<K, HI, HR, FR>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM));
-    attr = true;
+    attr[dev] = true;
   }
   rs_scatter<K, HI, HR, FR><<<tiles, RS_THREADS, SM, stream()>>>(kin, kout, iin, iout, rin, rout, n, shift, cnt,
                                                                 inc, tiles, device_error_word());
