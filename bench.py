@@ -439,7 +439,7 @@ def main():
 CASES = ("add_f32", "floor_divide_f32", "mod_f32", "logaddexp_f32", "add_i32", "floor_divide_i32", "mod_i32",
          "bcast_add_f32", "c1_fused_sum", "sum_f32", "var_f32", "argmax_f32", "argmin_f32", "nansum_f32",
          "sum_axis0_f32", "sum_axis1_f32",
-         "var_axis0_f32",
+         "var_axis0_f32", "argmax_axis0_f32",
          "cumsum_i32", "cumsum_f32", "cumsum_axis1_f32", "matmul_f32", "matmul_f16", "sort_f32", "argsort_f32",
          "searchsorted_f32", "count_nonzero_gt_f32")
 
@@ -477,11 +477,11 @@ def run_case(args):
         # loop holds the kernels only, not a host read per call
         kw = {"keepdims": True} if c.startswith("arg") else {}
         fn, nb = (lambda: f(x, **kw)), 4 * n
-    elif c in ("sum_axis0_f32", "sum_axis1_f32", "var_axis0_f32"):
+    elif c in ("sum_axis0_f32", "sum_axis1_f32", "var_axis0_f32", "argmax_axis0_f32"):
         side = int(math.isqrt(n))
         x = gen.normal((side, side), 21)
         ax = 1 if c == "sum_axis1_f32" else 0
-        f = cp.var if c.startswith("var") else cp.sum
+        f = cp.var if c.startswith("var") else cp.argmax if c.startswith("argmax") else cp.sum
         fn, nb = (lambda: f(x, axis=ax)), 4 * side * side
     elif c == "cumsum_i32":
         x = gen.integers((n,), -100, 101, 31)
