@@ -238,11 +238,7 @@ def step_bytes(n=N_C2):
 
 
 # --------------------------------------------------------------------------- CPU legs (oracle port)
-def cpu_c2_pass(n, threads=1, seed=0):
-    """The reference's CPU path for the C2 op set on n elements (numpy port),
-    split over `threads` host threads (numpy releases the GIL in ufuncs)."""
-    from oracle import oracle as O
-
+def cpu_c2_inputs(n, seed=0):
     rng = np.random.default_rng(seed)
     af = rng.uniform(-1000, 1000, n).astype(np.float32)
     bf = (rng.uniform(1, 50, n) * rng.choice([-1, 1], n)).astype(np.float32)
@@ -251,6 +247,17 @@ def cpu_c2_pass(n, threads=1, seed=0):
     rows = max(1, int(BC_ROWS * n / N_C2))
     r = rng.standard_normal((rows, 1)).astype(np.float32)
     c = rng.standard_normal((1, BC_COLS)).astype(np.float32)
+    return (af, bf, ai, bi, r, c)
+
+
+def cpu_c2_pass(n, threads=1, seed=0, inputs=None):
+    """The reference's CPU path for the C2 op set on n elements (numpy port),
+    split over `threads` host threads (numpy releases the GIL in ufuncs).
+    Returns (algorithmic bytes, seconds); input generation is not timed."""
+    from oracle import oracle as O
+
+    af, bf, ai, bi, r, c = inputs if inputs is not None else cpu_c2_inputs(n, seed)
+    rows = r.shape[0]
     fns = [(O.add, af, bf), (O.floor_divide, af, bf), (O.mod, af, bf), (O.logaddexp, af, bf),
            (O.add, ai, bi), (O.floor_divide, ai, bi), (O.mod, ai, bi)]
     nbytes = 7 * 12 * n + 4 * rows * BC_COLS + 4 * (rows + BC_COLS)
@@ -278,8 +285,9 @@ def cpu_c2_pass(n, threads=1, seed=0):
 def cpu_baseline(sample_n=1 << 24, reps=2):
     best = None
     nbytes = 0
+    inputs = cpu_c2_inputs(sample_n, 0)
     for _ in range(reps):
-        nbytes, dt = cpu_c2_pass(sample_n, threads=1)
+        nbytes, dt = cpu_c2_pass(sample_n, threads=1, inputs=inputs)
         best = dt if best is None else min(best, dt)
     return {"value": round(nbytes / best / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
             "sample": f"C2 op set on {sample_n} elements per operand (broadcast add scaled to "
@@ -287,16 +295,22 @@ def cpu_baseline(sample_n=1 << 24, reps=2):
 
 
 def run_reference(args):
+    """The reference's CPU path (the numpy oracle port) on the GPU arm's own
+    configuration: the C2 op set on 2^28 elements per operand, inputs made
+    once (seed 0, not timed), every step a full pass over all host threads
+    (numpy releases the GIL inside ufuncs, so the pass is split into one
+    contiguous chunk per thread)."""
     rank, world, _ = _env()
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    sample = 1 << 25
+    n = N_C2
+    inputs = cpu_c2_inputs(n, 0)
     for _ in range(args.warmup):
-        cpu_c2_pass(sample // 4, threads=threads)
+        cpu_c2_pass(n, threads=threads, inputs=inputs)
     times, nbytes = [], 0
-    for s in range(args.steps):
-        nbytes, dt = cpu_c2_pass(sample, threads=threads, seed=s)
+    for _ in range(args.steps):
+        nbytes, dt = cpu_c2_pass(n, threads=threads, inputs=inputs)
         times.append(dt)
     tot = sum(times)
     val = nbytes * args.steps / tot / 1e9
@@ -305,10 +319,11 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+i32",
         "data": "synthetic (numpy default_rng, seeded)",
-        "config": {"workload": "C2 binary ufuncs + broadcast add (BASELINE configs[1])",
-                   "elements_per_operand": N_C2, "sample_per_step": sample},
+        "config": {"workload": "C2: binary ufuncs at 2^28 (add/floor_divide/mod/logaddexp f32, "
+                               "add/floor_divide/mod i32) + broadcast add (8192,1)+(1,32768) f32",
+                   "elements_per_operand": n},
         "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample} elements per operand per step, {threads} threads"},
+                         "sample": f"the full workload: {n} elements per operand per step, {threads} threads"},
         "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -333,19 +348,16 @@ def main():
     if args.case:
         return run_case(args)
     rank, world, local = _env()
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
     import macmetalpy_b200 as cp
     from macmetalpy_b200._cuda_backend import CudaBackend, Event
 
+    dist = None
+    if world > 1:
+        # the library's own communicator (NCCL through the C ABI), bound to
+        # the library stream; no torch process group
+        from macmetalpy_b200 import distributed as dist
+
+        dist.init(timeout_s=120)
     be = CudaBackend()
     gen = Gen(cp)
     d = c2_inputs(cp, gen)
@@ -383,11 +395,7 @@ def main():
         for j in range(len(ops)):
             per_op[j] += evs[s][j].elapsed_ms(evs[s][j + 1])
     if dist is not None:
-        import torch
-
-        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = dist.max_over_ranks(ms)
     sb = step_bytes()
     value = world * sb * args.steps / (ms / 1e3) / 1e9
     peaks, peak_kind = _peaks()
@@ -415,7 +423,7 @@ def main():
         "gpu_launches": args.steps * len(ops),
     }
     if not args.no_e2e:
-        line["e2e"] = e2e_c2(cp, d, steps=4, dist=dist, local=local)
+        line["e2e"] = e2e_c2(cp, d, steps=4, dist=dist)
     if rank == 0 and not args.no_cpu and world == 1:
         line["cpu_baseline"] = cpu_baseline()
     if not args.no_suite:
@@ -427,12 +435,13 @@ def main():
             if rank == 0:
                 line["suite"] = run_suite(cp, gen)
         else:
-            line["dist_suite"] = dist_suite(cp, gen, dist, local)
+            line["dist_suite"] = dist_suite(cp, gen)
+            line["dist_parity"] = line["dist_suite"].pop("parity")
     if rank == 0:
         print(json.dumps(line))
     if dist is not None:
         dist.barrier()
-        dist.destroy_process_group()
+        dist.finalize()
     return 0
 
 
@@ -534,37 +543,83 @@ def _traffic(opname):
     return None
 
 
-def dist_suite(cp, gen, dist, local):
-    """Block-distributed ops over all ranks (NCCL exchange steps included),
+def dist_parity(cp):
+    """The exchange steps at N ranks, checked against numpy on the whole
+    array: every rank builds the same global arrays from one seed (2^22
+    elements per rank), holds its row block, runs the distributed op and
+    compares the result with numpy's on the global array (int32 sums and
+    scans and argmax exact; float32 within 1e-4 of the float64 value;
+    matmul within 1e-5 relative Frobenius).  Returns "ok" or the first
+    mismatch (identical on every rank: every rank checks the same values)."""
+    from macmetalpy_b200 import distributed as D
+
+    W = D.world()
+    rng = np.random.default_rng(2024)
+    n = W << 22
+    x = (rng.standard_normal(n) + 0.25).astype(np.float32)
+    x[[5, n - 7]] = x.max() + 1  # a tie across the first and last shard
+    xi = rng.integers(-100, 101, n).astype(np.int32)
+    X, XI = D.DistArray.from_global(x), D.DistArray.from_global(xi)
+    x64 = x.astype(np.float64)
+    bad = []
+
+    def rel(got, ref):
+        return abs(float(got) - ref) / max(abs(ref), 1e-30)
+
+    if rel(X.sum(), x64.sum()) > 1e-4 * np.abs(x64).sum() / abs(x64.sum()):
+        bad.append("sum")
+    if rel(X.var(), x64.var()) > 1e-4:
+        bad.append("var")
+    if X.argmax() != int(np.argmax(x)):
+        bad.append("argmax")
+    if int(XI.sum()) != int(xi.sum(dtype=np.int64)):
+        bad.append("sum_i32")
+    if not np.array_equal(XI.cumsum().gather(), np.cumsum(xi, dtype=np.int64)):
+        bad.append("cumsum_i32")
+    m = x.reshape(-1, 1024)
+    M = D.DistArray.from_global(m)
+    s0 = M.sum(axis=0).get()
+    if np.max(np.abs(s0 - m.astype(np.float64).sum(axis=0))) > 1e-4 * np.abs(m).sum(axis=0).max():
+        bad.append("sum_axis0")
+    a = (rng.standard_normal((256 * W, 512)) / 20).astype(np.float32)
+    b = (rng.standard_normal((512, 384)) / 20).astype(np.float32)
+    A = D.DistArray.from_global(a)
+    B = cp.array(b) if D.rank() == 0 else cp.zeros(b.shape, dtype=np.float32)
+    C = A.matmul(B).gather()
+    r = a.astype(np.float64) @ b.astype(np.float64)
+    if np.linalg.norm(C - r) / np.linalg.norm(r) > 1e-5:
+        bad.append("matmul")
+    return "ok" if not bad else "mismatch: " + ",".join(bad)
+
+
+def dist_suite(cp, gen):
+    """Block-distributed ops over all ranks (the exchange steps included),
     weak-scaled: every rank holds the single-GPU C3 / C4 operand, so the
     global array is world x that.  Matmul is strong-scaled: A (16384,16384)
-    row-sharded, B broadcast from rank 0.  Device time (events on the
-    library stream, which is also torch's current stream), max over ranks;
-    values count every rank's bytes / FLOPs."""
-    import torch
-
+    row-sharded, B broadcast from rank 0; the broadcast alone and the local
+    GEMM alone are timed too.  Device time (events on the library stream,
+    where the collectives also run), max over ranks; values count every
+    rank's bytes / FLOPs.  ``parity``: see dist_parity."""
     from macmetalpy_b200 import distributed as D
+    from macmetalpy_b200 import linalg_top
     from macmetalpy_b200._cuda_backend import Event
 
-    D.init()
     W, R = D.world(), D.rank()
 
     def timed(fn, iters=3, warm=2):
         for _ in range(warm):
             fn()
-        cp.synchronize()
-        dist.barrier()
+        D.barrier()
         s, e = Event(), Event()
         s.record()
         for _ in range(iters):
             fn()
         e.record()
+        D.synchronize()
         ms = s.elapsed_ms(e) / iters
-        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return D.max_over_ranks(ms)
 
-    out = {}
+    out = {"parity": dist_parity(cp)}
     n = 1 << 28
     x = gen.normal((n,), 21 + 100 * R)
     X = D.DistArray.from_local(x, W * n)
@@ -586,12 +641,23 @@ def dist_suite(cp, gen, dist, local):
     b = gen.normal((m, m), 42) * np.float32(1 / 128)
     A = D.DistArray.from_local(a, m)
     ms = timed(lambda: A.matmul(b), iters=2, warm=1)
-    out["dist_matmul_f32_16384_bcastB"] = {"tflops": round(2 * m ** 3 / ms / 1e9, 2), "ms": round(ms, 3)}
+    ms_gemm = timed(lambda: linalg_top.matmul(a, b), iters=2, warm=1)
+    from macmetalpy_b200 import _cuda_backend as cb
+
+    def bcast():
+        cb.check(cb.lib.mmp_broadcast(ctypes.c_void_p(b._ptr), ctypes.c_void_p(b._ptr), 4 * m * m,
+                                      cb.dtype_code(np.uint8), 0), "broadcast")
+
+    ms_b = timed(bcast, iters=3, warm=1)
+    out["dist_matmul_f32_16384_bcastB"] = {"tflops": round(2 * m ** 3 / ms / 1e9, 2), "ms": round(ms, 3),
+                                           "broadcast_B_ms": round(ms_b, 3),
+                                           "broadcast_B_gbs": round(4 * m * m / ms_b / 1e6, 1),
+                                           "local_gemm_ms": round(ms_gemm, 3)}
     out["world"] = W
     return out
 
 
-def e2e_c2(cp, d, steps=2, dist=None, local=0):
+def e2e_c2(cp, d, steps=2, dist=None):
     """Same op set through the public API with host buffers: every step
     uploads its six inputs from pinned host memory and reads its eight
     results back into pinned host memory.  The copies go through
@@ -653,7 +719,7 @@ def e2e_c2(cp, d, steps=2, dist=None, local=0):
     world = 1
     if dist is not None:
         dist.barrier()
-        world = dist.get_world_size()
+        world = dist.world()
     t0 = Event().record(None)
     s_in.wait_event(t0)
     s_out.wait_event(t0)
@@ -665,11 +731,7 @@ def e2e_c2(cp, d, steps=2, dist=None, local=0):
     s_in.synchronize()
     s_out.synchronize()
     if dist is not None:
-        import torch
-
-        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = dist.max_over_ranks(ms)
     del sets, host_in, host_out
     return {"value": round(world * step_bytes() * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,

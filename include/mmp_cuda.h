@@ -32,6 +32,8 @@ extern "C" {
 #define MMP_E_NVRTC (-3)     /* NVRTC compile failed; log in the log buffer  */
 #define MMP_E_UNSUPPORTED (-4)
 #define MMP_E_DEVICE (-5)    /* a kernel reported an error (bounded wait)    */
+#define MMP_E_COMM (-6)      /* NCCL missing or failed, or a collective timed
+                                out (the communicator is then aborted)      */
 
 /* dtype codes (numpy kinds the reference supports, _dtypes.py:21-31, plus
  * int8/uint8 and float64 which B200 computes natively) */
@@ -226,6 +228,62 @@ int mmp_scatter(int dtype, void *dst, int64_t limit, const int64_t *offsets,
  * flatnonzero). */
 int mmp_compact_indices(const void *mask, const int64_t *incl, int64_t n,
                         int64_t count, int64_t *out);
+
+/* ---- block-distributed arrays: partials and their merge on the device.
+ * The reference is single-device (MetalBackend, _metal_backend.py:186-204);
+ * these split its full reductions (ndarray._reduce, ndarray.py:1895-1963;
+ * reductions.var, reductions.py:525-584; reductions.argmax,
+ * reductions.py:381-418) into a per-shard step and a merge step, with no
+ * host round trip in between. */
+
+/* Write the merged partial of a full reduction of x[0..n) to device memory
+ * `dev_partial` (8-byte aligned; layout mmp_partial), on the stream, without
+ * synchronising.  For argmax/argmin the index is offset by index_base (the
+ * shard's first global flat index); an empty shard gives index -1. */
+int mmp_reduce_partial(int op, int dtype, const void *x, int64_t n, int64_t index_base,
+                       mmp_partial *dev_partial);
+
+/* Fold nparts device partials (rank order) with the op's own arithmetic and
+ * write the result as mmp_reduce would (one out_dtype element at `out`, a
+ * device pointer); `dev_merged` (device, may be NULL) receives the merged
+ * partial.  nparts == 0 gives the op's identity, e.g. the zero carry of
+ * rank 0 in a distributed scan (op MMP_R_SUM, out_dtype int64/float64). */
+int mmp_merge_partials(int op, int dtype, const mmp_partial *dev_parts, int nparts, int out_dtype,
+                       void *out, double ddof, mmp_partial *dev_merged);
+
+/* ---- collectives over NCCL (one process per GPU; no counterpart in the
+ * reference, which is single-device -- these extend its ctypes ABI table,
+ * _metal_backend.py:221-263, with the exchange steps of block-distributed
+ * arrays).  NCCL is opened at run time (dlopen of libnccl.so.2, or the
+ * path in MMP_NCCL_LIB).  One communicator per device; every collective is
+ * enqueued on the current device's library stream, so kernels and
+ * collectives are ordered without host synchronisation.  Buffers are device
+ * pointers; count is in elements of dtype (bool is sent as 1-byte words).
+ * A call that does not complete within the communicator's timeout aborts
+ * it and returns MMP_E_COMM. */
+#define MMP_COMM_ID_BYTES 128
+enum mmp_comm_op { MMP_COMM_SUM = 0, MMP_COMM_PROD = 1, MMP_COMM_MAX = 2, MMP_COMM_MIN = 3 };
+int mmp_nccl_version(int *version);
+/* Rank 0 creates the id and hands the 128 bytes to every rank out of band. */
+int mmp_comm_unique_id(void *id);
+/* Join the communicator of nranks ranks as `rank`, on the current device
+ * (after mmp_init).  Blocks until every rank joined or timeout_s passed. */
+int mmp_comm_init(int nranks, int rank, const void *id, double timeout_s);
+int mmp_comm_rank(int *rank, int *nranks);
+int mmp_comm_destroy(void);   /* synchronises the stream first */
+int mmp_comm_abort(void);     /* no synchronisation: for error paths */
+int mmp_allreduce(const void *send, void *recv, size_t count, int dtype, int op);
+/* recv holds nranks * count elements, rank r's at offset r * count. */
+int mmp_allgather(const void *send, void *recv, size_t count, int dtype);
+/* send is read on `root` only; every rank receives into recv (in place
+ * when send == recv on the root). */
+int mmp_broadcast(const void *send, void *recv, size_t count, int dtype, int root);
+int mmp_group_start(void);
+int mmp_group_end(void);
+/* Wait for this device's stream, giving up after timeout_s seconds (<= 0:
+ * the communicator's timeout): then the communicator is aborted and
+ * MMP_E_COMM returned, so a lost rank ends in an error, not a hang. */
+int mmp_comm_synchronize(double timeout_s);
 
 /* Self-test of the failure behaviour of waiting kernels (no counterpart in
  * the reference): one kernel waits on a device flag that nothing sets, gives

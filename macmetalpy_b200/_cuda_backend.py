@@ -95,6 +95,20 @@ SIGNATURES = {
     "mmp_gather": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
     "mmp_scatter": (_int, [_int, _vp, _i64, _vp, _i64, _vp]),
     "mmp_compact_indices": (_int, [_vp, _vp, _i64, _i64, _vp]),
+    "mmp_reduce_partial": (_int, [_int, _int, _vp, _i64, _i64, _vp]),
+    "mmp_merge_partials": (_int, [_int, _int, _vp, _int, _int, _vp, ctypes.c_double, _vp]),
+    "mmp_nccl_version": (_int, [ctypes.POINTER(_int)]),
+    "mmp_comm_unique_id": (_int, [_vp]),
+    "mmp_comm_init": (_int, [_int, _int, _vp, ctypes.c_double]),
+    "mmp_comm_rank": (_int, [ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "mmp_comm_destroy": (_int, []),
+    "mmp_comm_abort": (_int, []),
+    "mmp_allreduce": (_int, [_vp, _vp, _sz, _int, _int]),
+    "mmp_allgather": (_int, [_vp, _vp, _sz, _int]),
+    "mmp_broadcast": (_int, [_vp, _vp, _sz, _int, _int]),
+    "mmp_group_start": (_int, []),
+    "mmp_group_end": (_int, []),
+    "mmp_comm_synchronize": (_int, [ctypes.c_double]),
 }
 
 

@@ -84,7 +84,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     if todo or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < _newest(objs):
         lib64 = os.path.join(home, "lib64")
         cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", "-o", LIB_PATH + ".tmp", *objs,
-               "-L" + lib64, "-lnvrtc", "-Xlinker", "-rpath=" + lib64, "-cudart", "static"]
+               "-L" + lib64, "-lnvrtc", "-ldl", "-Xlinker", "-rpath=" + lib64, "-cudart", "static"]
         p = subprocess.run(cmd, capture_output=True, text=True)
         if p.returncode:
             sys.stderr.write(p.stdout + p.stderr)

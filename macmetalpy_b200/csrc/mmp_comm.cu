@@ -1,0 +1,351 @@
+// mmp_comm: the collective exchange steps of block-distributed arrays, as
+// C-ABI entry points over NCCL (one process per GPU, one communicator per
+// device, every collective enqueued on the device's library stream).
+//
+// The reference is single-device (MetalBackend, src/macmetalpy/
+// _metal_backend.py:186-204); these exports extend its ctypes ABI table
+// (_metal_backend.py:221-263) with the exchange steps that the block
+// distribution needs: all-gather of per-shard partials, all-reduce of
+// per-column partials and the broadcast of a replicated matmul operand.
+//
+// NCCL is opened with dlopen on the first mmp_comm_* call ("libnccl.so.2",
+// or the path in MMP_NCCL_LIB), so the library still loads -- and its CPU
+// tests run -- on a host without NCCL or a GPU.  In a process that already
+// loaded NCCL (e.g. through torch), dlopen returns that copy.  nccl.h is
+// used for its types only.
+//
+// The communicator is created non-blocking: every call that NCCL reports
+// as still in progress is polled on the host with a deadline (the init
+// timeout passed to mmp_comm_init), and a communicator that does not become
+// ready in time is aborted and reported as MMP_E_COMM, so a rank that never
+// joins, or a peer that died, ends in an error instead of a hang.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <mutex>
+#include <string>
+
+#include "mmp_internal.h"
+
+namespace {
+
+struct NcclApi {
+  bool loaded = false;
+  void *handle = nullptr;
+  ncclResult_t (*GetVersion)(int *) = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Broadcast)(const void *, void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi g_api;
+std::mutex g_api_mu;
+
+struct CommState {
+  ncclComm_t comm = nullptr;
+  int rank = -1;
+  int nranks = 0;
+  double timeout_s = 120.0;
+};
+constexpr int kMaxDev = 64;
+CommState g_comm[kMaxDev];
+std::mutex g_comm_mu;
+
+double now_s() {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+template <class F>
+bool sym(void *h, const char *name, F &out) {
+  out = reinterpret_cast<F>(dlsym(h, name));
+  return out != nullptr;
+}
+
+int load_api() {
+  std::lock_guard<std::mutex> lk(g_api_mu);
+  if (g_api.loaded) return MMP_OK;
+  const char *env = getenv("MMP_NCCL_LIB");
+  const char *cands[] = {env, "libnccl.so.2", "libnccl.so"};
+  void *h = nullptr;
+  std::string tried;
+  for (const char *c : cands) {
+    if (!c || !*c) continue;
+    h = dlopen(c, RTLD_NOW | RTLD_GLOBAL);
+    if (h) break;
+    tried += std::string(" ") + c;
+  }
+  if (!h) return mmp::set_error(MMP_E_COMM, "NCCL not found (tried" + tried + "); set MMP_NCCL_LIB");
+  bool ok = sym(h, "ncclGetVersion", g_api.GetVersion) && sym(h, "ncclGetUniqueId", g_api.GetUniqueId) &&
+            sym(h, "ncclCommInitRankConfig", g_api.CommInitRankConfig) &&
+            sym(h, "ncclCommDestroy", g_api.CommDestroy) && sym(h, "ncclCommAbort", g_api.CommAbort) &&
+            sym(h, "ncclCommGetAsyncError", g_api.CommGetAsyncError) &&
+            sym(h, "ncclAllReduce", g_api.AllReduce) && sym(h, "ncclAllGather", g_api.AllGather) &&
+            sym(h, "ncclBroadcast", g_api.Broadcast) && sym(h, "ncclGroupStart", g_api.GroupStart) &&
+            sym(h, "ncclGroupEnd", g_api.GroupEnd) && sym(h, "ncclGetErrorString", g_api.GetErrorString);
+  if (!ok) {
+    dlclose(h);
+    return mmp::set_error(MMP_E_COMM, "the NCCL library lacks a required symbol (NCCL >= 2.14 needed)");
+  }
+  g_api.handle = h;
+  g_api.loaded = true;
+  return MMP_OK;
+}
+
+int nccl_error(ncclResult_t r, const char *what) {
+  std::string m = std::string(what) + ": " + (g_api.GetErrorString ? g_api.GetErrorString(r) : "NCCL error");
+  return mmp::set_error(MMP_E_COMM, m);
+}
+
+CommState *cur_comm(int *rc) {
+  int dev = mmp::current_device();
+  if (dev < 0 || dev >= kMaxDev) {
+    *rc = mmp::set_error(MMP_E_ARG, "device out of range");
+    return nullptr;
+  }
+  CommState *c = &g_comm[dev];
+  if (!c->comm) {
+    *rc = mmp::set_error(MMP_E_COMM, "no communicator on this device: call mmp_comm_init first");
+    return nullptr;
+  }
+  *rc = MMP_OK;
+  return c;
+}
+
+// Poll a non-blocking communicator until NCCL reports it ready, an error, or
+// the deadline passes (then abort it: pending NCCL kernels stop).
+int wait_ready(CommState *c, ncclResult_t r, const char *what) {
+  if (r == ncclSuccess) return MMP_OK;
+  if (r != ncclInProgress) return nccl_error(r, what);
+  const double t0 = now_s();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t q = g_api.CommGetAsyncError(c->comm, &st);
+    if (q != ncclSuccess) return nccl_error(q, what);
+    if (st == ncclSuccess) return MMP_OK;
+    if (st != ncclInProgress) return nccl_error(st, what);
+    if (now_s() - t0 > c->timeout_s) {
+      g_api.CommAbort(c->comm);
+      c->comm = nullptr;
+      c->rank = -1;
+      c->nranks = 0;
+      return mmp::set_error(MMP_E_COMM, std::string(what) + ": timed out; communicator aborted");
+    }
+    usleep(200);
+  }
+}
+
+bool nccl_type(int dt, ncclDataType_t *t) {
+  switch (dt) {
+    case MMP_BOOL: case MMP_INT8: *t = ncclInt8; return true;
+    case MMP_UINT8: *t = ncclUint8; return true;
+    case MMP_INT32: *t = ncclInt32; return true;
+    case MMP_UINT32: *t = ncclUint32; return true;
+    case MMP_INT64: *t = ncclInt64; return true;
+    case MMP_UINT64: *t = ncclUint64; return true;
+    case MMP_FLOAT16: *t = ncclFloat16; return true;
+    case MMP_FLOAT32: *t = ncclFloat32; return true;
+    case MMP_FLOAT64: *t = ncclFloat64; return true;
+    default: return false;
+  }
+}
+
+bool nccl_op(int op, ncclRedOp_t *o) {
+  switch (op) {
+    case MMP_COMM_SUM: *o = ncclSum; return true;
+    case MMP_COMM_PROD: *o = ncclProd; return true;
+    case MMP_COMM_MAX: *o = ncclMax; return true;
+    case MMP_COMM_MIN: *o = ncclMin; return true;
+    default: return false;
+  }
+}
+
+}  // namespace
+
+extern "C" int mmp_comm_unique_id(void *id) {
+  if (!id) return mmp::set_error(MMP_E_ARG, "null id buffer");
+  int rc = load_api();
+  if (rc) return rc;
+  static_assert(sizeof(ncclUniqueId) == MMP_COMM_ID_BYTES, "ncclUniqueId size");
+  ncclUniqueId u;
+  ncclResult_t r = g_api.GetUniqueId(&u);
+  if (r != ncclSuccess) return nccl_error(r, "ncclGetUniqueId");
+  memcpy(id, &u, sizeof u);
+  return MMP_OK;
+}
+
+extern "C" int mmp_comm_init(int nranks, int rank, const void *id, double timeout_s) {
+  if (nranks < 1 || rank < 0 || rank >= nranks) return mmp::set_error(MMP_E_ARG, "bad rank / nranks");
+  if (!id) return mmp::set_error(MMP_E_ARG, "null unique id");
+  if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "call mmp_init on this device first");
+  int rc = load_api();
+  if (rc) return rc;
+  int dev = mmp::current_device();
+  if (dev < 0 || dev >= kMaxDev) return mmp::set_error(MMP_E_ARG, "device out of range");
+  std::lock_guard<std::mutex> lk(g_comm_mu);
+  CommState *c = &g_comm[dev];
+  if (c->comm) return mmp::set_error(MMP_E_ARG, "a communicator already exists on this device");
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof u);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  c->timeout_s = timeout_s > 0 ? timeout_s : 120.0;
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = g_api.CommInitRankConfig(&comm, nranks, u, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, "ncclCommInitRankConfig");
+  c->comm = comm;
+  c->rank = rank;
+  c->nranks = nranks;
+  return wait_ready(c, r, "ncclCommInitRankConfig");
+}
+
+extern "C" int mmp_comm_rank(int *rank, int *nranks) {
+  int rc;
+  CommState *c = cur_comm(&rc);
+  if (!c) return rc;
+  if (rank) *rank = c->rank;
+  if (nranks) *nranks = c->nranks;
+  return MMP_OK;
+}
+
+extern "C" int mmp_comm_destroy(void) {
+  int dev = mmp::current_device();
+  if (dev < 0 || dev >= kMaxDev) return mmp::set_error(MMP_E_ARG, "device out of range");
+  std::lock_guard<std::mutex> lk(g_comm_mu);
+  CommState *c = &g_comm[dev];
+  if (!c->comm) return MMP_OK;
+  // the stream's collectives must be done before the communicator goes
+  cudaStream_t st = mmp::stream();
+  if (st) MMP_CUDA_TRY(cudaStreamSynchronize(st));
+  ncclResult_t r = g_api.CommDestroy(c->comm);
+  c->comm = nullptr;
+  c->rank = -1;
+  c->nranks = 0;
+  if (r != ncclSuccess) return nccl_error(r, "ncclCommDestroy");
+  return MMP_OK;
+}
+
+extern "C" int mmp_comm_abort(void) {
+  int dev = mmp::current_device();
+  if (dev < 0 || dev >= kMaxDev) return mmp::set_error(MMP_E_ARG, "device out of range");
+  std::lock_guard<std::mutex> lk(g_comm_mu);
+  CommState *c = &g_comm[dev];
+  if (!c->comm) return MMP_OK;
+  ncclResult_t r = g_api.CommAbort(c->comm);
+  c->comm = nullptr;
+  c->rank = -1;
+  c->nranks = 0;
+  if (r != ncclSuccess) return nccl_error(r, "ncclCommAbort");
+  return MMP_OK;
+}
+
+extern "C" int mmp_allreduce(const void *send, void *recv, size_t count, int dtype, int op) {
+  int rc;
+  CommState *c = cur_comm(&rc);
+  if (!c) return rc;
+  ncclDataType_t t;
+  ncclRedOp_t o;
+  if (!nccl_type(dtype, &t)) return mmp::set_error(MMP_E_ARG, "dtype not supported by the collective");
+  if (!nccl_op(op, &o)) return mmp::set_error(MMP_E_ARG, "bad collective op");
+  if (count && (!send || !recv)) return mmp::set_error(MMP_E_ARG, "null pointer");
+  return wait_ready(c, g_api.AllReduce(send, recv, count, t, o, c->comm, mmp::stream()), "ncclAllReduce");
+}
+
+extern "C" int mmp_allgather(const void *send, void *recv, size_t count, int dtype) {
+  int rc;
+  CommState *c = cur_comm(&rc);
+  if (!c) return rc;
+  ncclDataType_t t;
+  if (!nccl_type(dtype, &t)) return mmp::set_error(MMP_E_ARG, "dtype not supported by the collective");
+  if (count && (!send || !recv)) return mmp::set_error(MMP_E_ARG, "null pointer");
+  return wait_ready(c, g_api.AllGather(send, recv, count, t, c->comm, mmp::stream()), "ncclAllGather");
+}
+
+extern "C" int mmp_broadcast(const void *send, void *recv, size_t count, int dtype, int root) {
+  int rc;
+  CommState *c = cur_comm(&rc);
+  if (!c) return rc;
+  ncclDataType_t t;
+  if (!nccl_type(dtype, &t)) return mmp::set_error(MMP_E_ARG, "dtype not supported by the collective");
+  if (root < 0 || root >= c->nranks) return mmp::set_error(MMP_E_ARG, "bad root rank");
+  if (count && !recv) return mmp::set_error(MMP_E_ARG, "null pointer");
+  return wait_ready(c, g_api.Broadcast(send, recv, count, t, root, c->comm, mmp::stream()), "ncclBroadcast");
+}
+
+extern "C" int mmp_group_start(void) {
+  int rc = load_api();
+  if (rc) return rc;
+  ncclResult_t r = g_api.GroupStart();
+  if (r != ncclSuccess) return nccl_error(r, "ncclGroupStart");
+  return MMP_OK;
+}
+
+extern "C" int mmp_group_end(void) {
+  int rc = load_api();
+  if (rc) return rc;
+  ncclResult_t r = g_api.GroupEnd();
+  if (r == ncclSuccess) return MMP_OK;
+  int dev = mmp::current_device();
+  if (r == ncclInProgress && dev >= 0 && dev < kMaxDev && g_comm[dev].comm)
+    return wait_ready(&g_comm[dev], r, "ncclGroupEnd");
+  return nccl_error(r, "ncclGroupEnd");
+}
+
+// Wait until every collective and kernel enqueued on this device's stream
+// has finished, but give up after timeout_s seconds: then abort the
+// communicator (NCCL stops its kernels that wait on a dead peer) and
+// return MMP_E_COMM.  A synchronise that cannot hang on a lost rank.
+extern "C" int mmp_comm_synchronize(double timeout_s) {
+  int rc;
+  CommState *c = cur_comm(&rc);
+  if (!c) return rc;
+  cudaStream_t st = mmp::stream();
+  const double t0 = now_s();
+  const double limit = timeout_s > 0 ? timeout_s : c->timeout_s;
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return MMP_OK;
+    if (e != cudaErrorNotReady) return mmp::cuda_error(e, "cudaStreamQuery");
+    ncclResult_t as = ncclSuccess;
+    g_api.CommGetAsyncError(c->comm, &as);
+    if (as != ncclSuccess && as != ncclInProgress) {
+      g_api.CommAbort(c->comm);
+      c->comm = nullptr;
+      c->rank = -1;
+      c->nranks = 0;
+      return nccl_error(as, "communicator failed; aborted");
+    }
+    if (now_s() - t0 > limit) {
+      g_api.CommAbort(c->comm);
+      c->comm = nullptr;
+      c->rank = -1;
+      c->nranks = 0;
+      return mmp::set_error(MMP_E_COMM, "collectives did not finish in time (a rank is gone?); communicator aborted");
+    }
+    usleep(50);
+  }
+}
+
+extern "C" int mmp_nccl_version(int *version) {
+  if (!version) return mmp::set_error(MMP_E_ARG, "null pointer");
+  int rc = load_api();
+  if (rc) return rc;
+  ncclResult_t r = g_api.GetVersion(version);
+  if (r != ncclSuccess) return nccl_error(r, "ncclGetVersion");
+  return MMP_OK;
+}

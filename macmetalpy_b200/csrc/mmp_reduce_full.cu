@@ -9,7 +9,11 @@ namespace mmp {
 
 template <int OPC, class T>
 struct FullRun {
-  static int run(const void *x, long long n, int out_dt, void *out, double ddof, mmp_partial *part) {
+  // `part` (host) receives the merged partial after a synchronisation;
+  // `dev_part` (device), when set, receives it on the stream instead, and
+  // `out` may then be NULL (the scalar result goes to scratch).
+  static int run(const void *x, long long n, int out_dt, void *out, double ddof, mmp_partial *part,
+                 PartialOut *dev_part) {
     if constexpr (!RedSupported<OPC, T>::value) {
       return set_error(MMP_E_UNSUPPORTED, "nan-reduction of a non-float dtype");
     } else {
@@ -33,7 +37,9 @@ struct FullRun {
       unsigned *tickets = nullptr;
       int rc = scratch(acc_bytes + sizeof(PartialOut), &scr, &tickets);
       if (rc) return rc;
-      PartialOut *dpart = part ? (PartialOut *)((char *)scr + acc_bytes) : nullptr;
+      PartialOut *slot = (PartialOut *)((char *)scr + acc_bytes);
+      PartialOut *dpart = dev_part ? dev_part : (part ? slot : nullptr);
+      if (!out) out = slot;  // result unused: any 8 bytes of scratch
       L ld;
       ld.x = (const T *)x;
       ld.aligned = ((uintptr_t)x % 16) == 0;
@@ -69,5 +75,31 @@ extern "C" int mmp_reduce(int op, int dtype, const void *x, int64_t n, int out_d
     partial->ival = 0;
     partial->index = -1;
   }
-  return mmp::dispatch_op<mmp::FullRun>(op, dtype, x, (long long)n, out_dtype, out, ddof, partial);
+  return mmp::dispatch_op<mmp::FullRun>(op, dtype, x, (long long)n, out_dtype, out, ddof, partial,
+                                        (PartialOut *)nullptr);
+}
+
+namespace mmpd {
+// A shard's argmax / argmin index is local to the shard: move it to the
+// global flat index (absent results, index -1, stay -1).
+__global__ void partial_index_base_kernel(PartialOut *p, long long base) {
+  if (threadIdx.x == 0 && p->index >= 0) p->index += base;
+}
+}  // namespace mmpd
+
+extern "C" int mmp_reduce_partial(int op, int dtype, const void *x, int64_t n, int64_t index_base,
+                                  mmp_partial *dev_partial) {
+  if (n < 0) return mmp::set_error(MMP_E_ARG, "negative element count");
+  if ((n > 0 && !x) || !dev_partial) return mmp::set_error(MMP_E_ARG, "null pointer");
+  if (((uintptr_t)dev_partial) % 8) return mmp::set_error(MMP_E_ARG, "partial not 8-byte aligned");
+  if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "call mmp_init first");
+  PartialOut *dp = (PartialOut *)dev_partial;
+  int rc = mmp::dispatch_op<mmp::FullRun>(op, dtype, x, (long long)n, (int)MMP_FLOAT64, (void *)nullptr, 0.0,
+                                          (mmp_partial *)nullptr, dp);
+  if (rc) return rc;
+  if ((op == MMP_R_ARGMAX || op == MMP_R_ARGMIN) && index_base != 0) {
+    partial_index_base_kernel<<<1, 32, 0, mmp::stream()>>>(dp, (long long)index_base);
+    MMP_LAUNCH_CHECK("partial_index_base_kernel");
+  }
+  return MMP_OK;
 }

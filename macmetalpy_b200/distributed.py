@@ -1,99 +1,128 @@
 """Block-distributed arrays over the GPUs of one box (one process per GPU).
 
-The reference is single-device; this is the scale-out the B200 build adds
-for arrays above a size threshold.  Rows (axis 0, or the flat index of a
-1-D array) are split into contiguous blocks, one per rank, with the
-remainder spread over the first ranks.  Each rank holds its block as an
-ordinary ``macmetalpy_b200.ndarray`` and runs the single-GPU kernels on it;
-only the exchange steps use collectives (``torch.distributed`` over NCCL /
-NVLink, one communicator per process group):
+The reference is single-device (``MetalBackend``,
+``src/macmetalpy/_metal_backend.py:186-204``); this is the scale-out the
+B200 build adds for arrays above a size threshold.  Rows (axis 0, or the
+flat index of a 1-D array) are split into contiguous blocks, one per rank,
+with the remainder spread over the first ranks.  Each rank holds its block
+as an ordinary ``macmetalpy_b200.ndarray`` and runs the single-GPU kernels on
+it; the exchange steps are the library's own C-ABI collectives
+(``mmp_allgather`` / ``mmp_allreduce`` / ``mmp_broadcast`` over NCCL on the
+library stream), and every merge runs on the device:
 
 * elementwise / ufuncs: shard-local, no collective;
-* sum / mean / nansum / nanmean: each shard's exact partial (float64 sum or
-  int64 sum, and the count) -> ``all_reduce`` (SUM);
-* var / std: each shard's (count, S1, S2, shift) -> ``all_gather`` -> Chan's
-  pairwise merge in rank order (deterministic);
-* argmax / argmin: each shard's (value, global index) -> ``all_gather`` ->
-  the first extreme wins, NaN first (numpy's rule);
-* max / min: ``all_gather`` of the shard extremes (NaN propagates);
-* axis-1 reductions and axis-1 cumsum: shard-local (rows never span ranks);
-* axis-0 reductions: float64 per-column partials -> ``all_reduce`` (SUM);
-* 1-D cumsum: shard totals -> ``all_gather`` -> exclusive prefix of the
-  lower ranks -> one local scan with that carry (one read, one write);
-* matmul: A row-sharded, B broadcast from rank 0 (``broadcast``), C
-  row-sharded.
+* full reductions (sum, mean, var, std, max, min, argmax, argmin, nansum,
+  nanmean, nanvar, nanstd, prod): each shard writes its partial to device
+  memory (``mmp_reduce_partial``), the partials are all-gathered in rank
+  order, and ``mmp_merge_partials`` folds them with the reduction's own
+  arithmetic (var: shifted moments moved to one shift; argmax: numpy's
+  first occurrence, NaN first).  The result is a 0-d device array on every
+  rank; argmax / argmin return a Python int, as the reference does;
+* axis-1 reductions and axis-1 scans: shard-local (rows never span ranks);
+* axis-0 reductions: float64 (or int64) per-column partials ->
+  ``mmp_allreduce`` (SUM) -> cast on the device;
+* 1-D cumsum: shard partial -> all-gather -> the merge of the lower ranks'
+  partials is the carry (on the device) -> one local scan with that carry;
+* matmul: A row-sharded, B broadcast in place from rank 0, C row-sharded.
 
-The library and torch share one current stream, so kernels and NCCL
-collectives are ordered on the device without host synchronisation.  The
-merge helpers (``merge_moments``, ``pick_arg``, ``exclusive_prefix``,
-``row_partition``) are pure functions, tested on CPU with ``gloo`` ranks.
+No step reads a partial back to the host; kernels and collectives share one
+stream, so nothing synchronises between them.  The only control-plane step is
+the hand-over of the communicator id at ``init`` (``_rendezvous``).
 """
 
 from __future__ import annotations
 
 import ctypes
-import math
 import os
 from dataclasses import dataclass
 
 import numpy as np
 
-__all__ = [
-    "init", "row_partition", "DistArray", "merge_moments", "pick_arg", "exclusive_prefix", "world", "rank",
-]
+__all__ = ["init", "finalize", "row_partition", "DistArray", "world", "rank", "barrier", "max_over_ranks",
+           "synchronize"]
 
-_state = {"init": False, "dist": None, "device": "cpu"}
+PARTIAL_BYTES = 48  # sizeof(mmp_partial)
+_state = {"init": False, "rank": 0, "world": 1, "parts": None, "timeout": 120.0}
 
 
-def init(backend: str | None = None, timeout_s: float = 120.0):
-    """Join (or create) the default process group and bind this process's
-    GPU.  Uses the RANK / WORLD_SIZE / LOCAL_RANK / MASTER_* environment."""
-    import datetime
+def _cb():
+    from . import _cuda_backend as cb
 
-    import torch
-    import torch.distributed as dist
+    return cb
 
-    if not dist.is_initialized():
-        if backend is None:
-            backend = "nccl" if torch.cuda.is_available() else "gloo"
-        kw = {}
-        if backend == "nccl":
-            local = int(os.environ.get("LOCAL_RANK", "0"))
-            torch.cuda.set_device(local)
-            kw["device_id"] = torch.device("cuda", local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
-    _state["dist"] = dist
-    _state["init"] = True
-    _state["device"] = "cuda" if dist.get_backend() == "nccl" else "cpu"
-    if _state["device"] == "cuda":
-        from . import _cuda_backend as cb
 
-        cb.CudaBackend()
-        cur = torch.cuda.current_stream()
-        if cur.cuda_stream == 0:
-            # torch is on the legacy default stream: make the library's own
-            # (non-blocking) stream torch's current stream instead
-            h = ctypes.c_void_p()
-            cb.check(cb.lib.mmp_get_stream(ctypes.byref(h)), "get stream")
-            torch.cuda.set_stream(torch.cuda.ExternalStream(h.value, device=torch.cuda.current_device()))
-        else:
-            cb.check(cb.lib.mmp_set_stream(ctypes.c_void_p(cur.cuda_stream)), "set stream")
-    return dist
+def init(timeout_s: float = 120.0):
+    """Bind this process's GPU (``LOCAL_RANK``) and join the communicator of
+    ``WORLD_SIZE`` ranks as ``RANK`` (``MASTER_ADDR`` / ``MASTER_PORT`` carry
+    the id hand-over).  A rank that does not arrive within ``timeout_s``
+    ends the others' ``init`` with ``RuntimeError``."""
+    from ._rendezvous import exchange_root_bytes
+
+    if _state["init"]:
+        return
+    # in-switch reduction (NVLS) stays off: the exchanges here are small, and
+    # a rank that dies while bound to a multicast object disturbs its peers
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    r = int(os.environ.get("RANK", "0"))
+    w = int(os.environ.get("WORLD_SIZE", "1"))
+    cb = _cb()
+    cb.CudaBackend()  # mmp_init(LOCAL_RANK)
+    uid = ctypes.create_string_buffer(128)
+    if r == 0:
+        cb.check(cb.lib.mmp_comm_unique_id(uid), "mmp_comm_unique_id")
+    got = exchange_root_bytes(uid.raw, r, w, timeout_s)
+    uid = ctypes.create_string_buffer(got, 128)
+    cb.check(cb.lib.mmp_comm_init(w, r, uid, float(timeout_s)), "mmp_comm_init")
+    _state.update(init=True, rank=r, world=w, timeout=float(timeout_s))
+    _state["parts"] = cb.DeviceBuffer(PARTIAL_BYTES * (w + 1))
+
+
+def finalize():
+    """Destroy the communicator (after the stream's work is done)."""
+    if not _state["init"]:
+        return
+    cb = _cb()
+    cb.check(cb.lib.mmp_comm_destroy(), "mmp_comm_destroy")
+    _state.update(init=False, rank=0, world=1, parts=None)
 
 
 def world() -> int:
-    d = _state["dist"]
-    return d.get_world_size() if d is not None and d.is_initialized() else 1
+    return _state["world"]
 
 
 def rank() -> int:
-    d = _state["dist"]
-    return d.get_rank() if d is not None and d.is_initialized() else 0
+    return _state["rank"]
 
 
-# ---------------------------------------------------------------------------
-# pure helpers (no GPU)
-# ---------------------------------------------------------------------------
+def synchronize(timeout_s: float = 0.0):
+    """Wait for this rank's stream; a collective that cannot finish (a lost
+    rank) aborts the communicator and raises instead of hanging."""
+    cb = _cb()
+    if _state["init"]:
+        cb.check(cb.lib.mmp_comm_synchronize(float(timeout_s)), "synchronize")
+    cb.CudaBackend().synchronize()
+
+
+def barrier():
+    """Every rank's stream has reached this point (a one-word all-reduce)."""
+    from .creation import zeros
+
+    t = zeros((1,), dtype=np.int32)
+    cb = _cb()
+    cb.check(cb.lib.mmp_allreduce(ctypes.c_void_p(t._ptr), ctypes.c_void_p(t._ptr), 1, cb.dtype_code(np.int32),
+                                  0), "barrier")
+    synchronize()
+
+
+def max_over_ranks(v: float) -> float:
+    """The largest of every rank's host value (device all-reduce, MAX)."""
+    from .creation import array
+
+    t = array(np.array([v], dtype=np.float64))
+    cb = _cb()
+    cb.check(cb.lib.mmp_allreduce(ctypes.c_void_p(t._ptr), ctypes.c_void_p(t._ptr), 1,
+                                  cb.dtype_code(np.float64), 2), "max_over_ranks")
+    return float(t.get()[0])
 
 
 def row_partition(n: int, world_size: int) -> list[tuple[int, int]]:
@@ -108,100 +137,32 @@ def row_partition(n: int, world_size: int) -> list[tuple[int, int]]:
     return out
 
 
-def merge_moments(parts) -> tuple[float, float, float]:
-    """Merge per-shard (count, S1, S2, shift) with S1 = sum(x - shift) and
-    S2 = sum((x - shift)^2) into (count, mean, M2) by Chan et al.'s pairwise
-    update, in rank order."""
-    n_tot, mean_tot, m2_tot = 0.0, 0.0, 0.0
-    for cnt, s1, s2, k in parts:
-        cnt = float(cnt)
-        if cnt == 0:
-            continue
-        mean = k + s1 / cnt
-        m2 = max(s2 - s1 * s1 / cnt, 0.0)
-        if n_tot == 0:
-            n_tot, mean_tot, m2_tot = cnt, mean, m2
-            continue
-        delta = mean - mean_tot
-        n_new = n_tot + cnt
-        mean_tot = mean_tot + delta * cnt / n_new
-        m2_tot = m2_tot + m2 + delta * delta * n_tot * cnt / n_new
-        n_tot = n_new
-    return n_tot, mean_tot, m2_tot
+def _gathered_partials(local, kind: str, index_base: int) -> int:
+    """All ranks' partials of ``kind`` over ``local``, rank order, on the
+    device; returns the address of the first (the array holds world())."""
+    from . import reductions
+
+    cb = _cb()
+    buf = _state["parts"]
+    own = buf.ptr
+    src = local._ensure_contiguous() if local.size else local
+    cb.check(cb.lib.mmp_reduce_partial(reductions.OPC[kind], cb.dtype_code(src.dtype),
+                                       ctypes.c_void_p(src._ptr if src.size else 0), int(src.size),
+                                       int(index_base), ctypes.c_void_p(own)), f"partial {kind}")
+    cb.check(cb.lib.mmp_allgather(ctypes.c_void_p(own), ctypes.c_void_p(own + PARTIAL_BYTES), PARTIAL_BYTES,
+                                  cb.dtype_code(np.uint8)), f"allgather {kind}")
+    return own + PARTIAL_BYTES
 
 
-def pick_arg(parts, maximum: bool = True) -> int:
-    """Global argmax/argmin from per-shard (value, global_index, present):
-    the larger (smaller) value wins, NaN beats every number, ties keep the
-    lower index (numpy's first occurrence)."""
-    best = None
-    for v, i, present in parts:
-        if not present:
-            continue
-        v = float(v)
-        i = int(i)
-        if best is None:
-            best = (v, i)
-            continue
-        bv, bi = best
-        vn, bn = math.isnan(v), math.isnan(bv)
-        if vn or bn:
-            if vn and bn:
-                take = i < bi
-            else:
-                take = vn
-        elif v != bv:
-            take = (v > bv) if maximum else (v < bv)
-        else:
-            take = i < bi
-        if take:
-            best = (v, i)
-    return -1 if best is None else best[1]
+def _merge(kind: str, dtype, parts_ptr: int, nparts: int, odt, ddof: float = 0.0):
+    from . import reductions
 
-
-def exclusive_prefix(totals, r: int, prod: bool = False):
-    """Combination of the totals of ranks 0..r-1 (the carry of rank r)."""
-    acc = 1 if prod else 0
-    for t in totals[:r]:
-        acc = acc * t if prod else acc + t
-    return acc
-
-
-# ---------------------------------------------------------------------------
-# collectives on small host vectors
-# ---------------------------------------------------------------------------
-
-
-def _t(x, dtype):
-    import torch
-
-    return torch.as_tensor(np.asarray(x), dtype=dtype, device=_state["device"])
-
-
-def allgather_rows(vec, dtype=None) -> np.ndarray:
-    """(world, len(vec)) array of every rank's ``vec``."""
-    import torch
-
-    dist = _state["dist"]
-    dt = dtype or torch.float64
-    t = _t(vec, dt).reshape(-1)
-    out = [torch.empty_like(t) for _ in range(world())]
-    dist.all_gather(out, t)
-    return np.stack([o.cpu().numpy() for o in out])
-
-
-def allreduce_sum(vec, dtype=None) -> np.ndarray:
-    import torch
-
-    dist = _state["dist"]
-    t = _t(vec, dtype or torch.float64).reshape(-1)
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return t.cpu().numpy()
-
-
-# ---------------------------------------------------------------------------
-# distributed array
-# ---------------------------------------------------------------------------
+    cb = _cb()
+    res = reductions._scalar_result(np.dtype(odt))
+    cb.check(cb.lib.mmp_merge_partials(reductions.OPC[kind], cb.dtype_code(dtype), ctypes.c_void_p(parts_ptr),
+                                       int(nparts), cb.dtype_code(odt), ctypes.c_void_p(res._buffer.ptr),
+                                       float(ddof), None), f"merge {kind}")
+    return res
 
 
 @dataclass
@@ -239,17 +200,24 @@ class DistArray:
         return cls(local, (global_rows,) + tuple(local.shape[1:]), s, e)
 
     def gather(self) -> np.ndarray:
-        """The whole array on the host (every rank)."""
+        """The whole array on the host of every rank (device all-gather of
+        the padded blocks, then one read-back)."""
+        from .creation import empty, zeros
+
+        cb = _cb()
         parts = row_partition(self.global_shape[0], world())
         maxrows = max(e - s for s, e in parts)
-        loc = self.local.get()
-        pad = np.zeros((maxrows,) + loc.shape[1:], dtype=loc.dtype)
-        pad[: loc.shape[0]] = loc
-        rows = allgather_rows(pad.reshape(-1).view(np.uint8), dtype=_uint8())
-        out = []
-        for (s, e), r in zip(parts, rows):
-            out.append(r.view(loc.dtype).reshape((maxrows,) + loc.shape[1:])[: e - s])
-        return np.concatenate(out, axis=0)
+        inner = tuple(self.global_shape[1:])
+        dt = np.dtype(self.dtype)
+        pad = zeros((maxrows,) + inner, dtype=dt)
+        if self.local.size:
+            pad[: self.stop - self.start] = self.local
+        nbytes = pad.size * dt.itemsize
+        allb = empty((world() * maxrows,) + inner, dtype=dt)
+        cb.check(cb.lib.mmp_allgather(ctypes.c_void_p(pad._ptr), ctypes.c_void_p(allb._ptr), nbytes,
+                                      cb.dtype_code(np.uint8)), "gather")
+        host = allb.get().reshape((world(), maxrows) + inner)
+        return np.concatenate([host[r, : e - s] for r, (s, e) in enumerate(parts)], axis=0)
 
     # -- elementwise (shard-local)
     def map(self, fn, *others) -> "DistArray":
@@ -263,12 +231,22 @@ class DistArray:
     def __floordiv__(self, o): return self.map(lambda a, b: a // b, o)
     def __mod__(self, o): return self.map(lambda a, b: a % b, o)
 
-    # -- reductions
-    def _partial(self, kind):
+    # -- full reductions: device partial -> all-gather -> device merge
+    def _flat_base(self) -> int:
+        rows = max(self.stop - self.start, 1)
+        return self.start * (int(self.local.size) // rows) if self.local.size else 0
+
+    def _full(self, kind: str, ddof: float = 0.0):
         from . import reductions
 
-        _, p = reductions._reduce(self.local, kind, None, partial=True)
-        return p
+        k = kind
+        if self.dtype.kind != "f" and kind.startswith("nan"):
+            k = kind[3:]  # no NaN in integer arrays (nan_ops.py:132-134)
+        if self.local.size == 0 and world() == 1 and k in reductions._NO_IDENTITY:
+            raise ValueError(f"zero-size array to reduction operation {reductions._NO_IDENTITY[k]} "
+                             "which has no identity")
+        parts = _gathered_partials(self.local, k, self._flat_base())
+        return _merge(k, self.dtype, parts, world(), reductions.out_dtype(k, self.dtype), ddof)
 
     def sum(self, axis=None):
         from . import reductions
@@ -276,127 +254,88 @@ class DistArray:
         if axis in (1, -1) and len(self.global_shape) == 2:
             return DistArray(reductions.sum(self.local, axis=1), self.global_shape[:1], self.start, self.stop)
         if axis == 0 and len(self.global_shape) == 2:
-            from .creation import asarray
-            loc = reductions.sum(self.local.astype(np.float64) if self.dtype.kind == "f" else self.local, axis=0)
-            tot = allreduce_sum(loc.get(), _torch_dt(loc.dtype))
-            return asarray(tot.astype(reductions.out_dtype("sum", self.dtype)))
-        p = self._partial("sum")
-        if self.dtype.kind in "iub":
-            return int(allreduce_sum([p.ival], _int64())[0])
-        return float(allreduce_sum([p.s1])[0])
+            cb = _cb()
+            wide = np.float64 if self.dtype.kind == "f" else (np.uint64 if self.dtype.kind == "u" else np.int64)
+            loc = reductions.sum(self.local, axis=0, dtype=wide) if self.local.size else \
+                reductions.sum(self.local, axis=0).astype(wide)
+            cb.check(cb.lib.mmp_allreduce(ctypes.c_void_p(loc._ptr), ctypes.c_void_p(loc._ptr), int(loc.size),
+                                          cb.dtype_code(wide), 0), "allreduce axis 0")
+            return loc.astype(reductions.out_dtype("sum", self.dtype))
+        return self._full("sum")
 
     def mean(self):
-        p = self._partial("sum")
-        v = allreduce_sum([p.s1 if self.dtype.kind == "f" else float(p.ival), float(p.count)])
-        return v[0] / v[1]
+        return self._full("mean")
+
+    def prod(self):
+        return self._full("prod")
 
     def nansum(self):
-        p = self._partial("nansum")
-        return float(allreduce_sum([p.s1])[0])
+        return self._full("nansum")
 
     def nanmean(self):
-        p = self._partial("nanmean")
-        v = allreduce_sum([p.s1, float(p.count)])
-        return v[0] / v[1] if v[1] > 0 else float("nan")
+        return self._full("nanmean")
 
     def var(self, ddof=0):
-        p = self._partial("var")
-        parts = allgather_rows([float(p.count), p.s1, p.s2, p.shift])
-        n, _, m2 = merge_moments(parts)
-        return m2 / max(n - ddof, 0) if n - ddof > 0 else float("inf") if m2 > 0 else float("nan")
+        return self._full("var", ddof)
 
     def std(self, ddof=0):
-        return math.sqrt(self.var(ddof))
+        return self._full("std", ddof)
 
-    def _arg(self, kind):
-        n_local = int(np.prod(self.local.shape))
-        if n_local:
-            from . import reductions
+    def nanvar(self, ddof=0):
+        return self._full("nanvar", ddof)
 
-            li = int(getattr(reductions, kind)(self.local))
-            v = float(self.local.reshape(-1)[li].get())
-            gi = self.start * (n_local // max(self.stop - self.start, 1)) + li
-            row = [v, float(gi), 1.0]
-        else:
-            row = [0.0, -1.0, 0.0]
-        parts = allgather_rows(row)
-        return pick_arg(parts, maximum=(kind == "argmax"))
-
-    def argmax(self):
-        return self._arg("argmax")
-
-    def argmin(self):
-        return self._arg("argmin")
+    def nanstd(self, ddof=0):
+        return self._full("nanstd", ddof)
 
     def max(self):
-        from . import reductions
-
-        v = float(reductions.max(self.local).get()) if self.local.size else -math.inf
-        vals = allgather_rows([v])[:, 0]
-        return float(np.max(vals)) if not np.isnan(vals).any() else float("nan")
+        return self._full("max")
 
     def min(self):
-        from . import reductions
+        return self._full("min")
 
-        v = float(reductions.min(self.local).get()) if self.local.size else math.inf
-        vals = allgather_rows([v])[:, 0]
-        return float(np.min(vals)) if not np.isnan(vals).any() else float("nan")
+    def argmax(self) -> int:
+        return int(self._full("argmax").get())
+
+    def argmin(self) -> int:
+        return int(self._full("argmin").get())
 
     # -- scans
     def cumsum(self, axis=None) -> "DistArray":
-        from . import _cuda_backend as cb
         from . import reductions
-        from .creation import array
+        from .ndarray import ndarray
 
         if axis in (1, -1) and len(self.global_shape) == 2:
             return DistArray(reductions.cumsum(self.local, axis=1), self.global_shape, self.start, self.stop)
-        if len(self.global_shape) != 1:
-            raise NotImplementedError("distributed cumsum: 1-D or axis=1 of 2-D")
-        isint = self.dtype.kind in "iub"
-        if isint:
-            tot = int(reductions.sum(self.local).get()) if self.local.size else 0
-            totals = allgather_rows([tot], _int64())[:, 0]
-            carry = int(exclusive_prefix([int(t) for t in totals], rank()))
-            c = array(np.array([carry], dtype=np.uint64 if self.dtype.kind == "u" else np.int64))
+        if len(self.global_shape) != 1 and axis is not None:
+            raise NotImplementedError("distributed cumsum: 1-D, axis=1 of 2-D, or axis=None")
+        local = self.local.reshape(-1) if len(self.global_shape) != 1 else self.local
+        kind = self.dtype.kind
+        carry_dt = np.float64 if kind == "f" else (np.uint64 if kind == "u" else np.int64)
+        parts = _gathered_partials(local, "sum", 0)
+        carry = _merge("sum", self.dtype, parts, rank(), carry_dt)  # lower ranks' total
+        if local.size:
+            res = reductions._scan(local, 0, None, carry_ptr=carry._buffer.ptr)
         else:
-            p = self._partial("sum") if self.local.size else None
-            totals = allgather_rows([p.s1 if p else 0.0])[:, 0]
-            c = array(np.array([exclusive_prefix(list(totals), rank())], dtype=np.float64))
-        res = reductions._scan(self.local, 0, None, carry_ptr=c._ptr) if self.local.size else self.local
-        cb.CudaBackend()
+            res = ndarray._empty((0,), reductions.scan_out_dtype(self.dtype))
+        if len(self.global_shape) != 1:  # axis=None of an N-d array: flat result
+            n = int(np.prod(self.global_shape))
+            return DistArray(res, (n,), self._flat_base(), self._flat_base() + int(local.size))
         return DistArray(res, self.global_shape, self.start, self.stop)
 
     # -- matmul: A row-sharded, B broadcast from rank 0
     def matmul(self, b) -> "DistArray":
         """C = A @ B with A row-sharded and B replicated: every rank passes a
         device array of B's shape and dtype; rank 0's contents are broadcast
-        into the others (NCCL), then each rank multiplies its rows."""
-        import torch
-
+        in place into the others' arrays (``mmp_broadcast`` on the library
+        stream, so the local GEMM is ordered after it), then each rank
+        multiplies its rows."""
         from . import linalg_top
 
-        dist = _state["dist"]
+        b = b._ensure_contiguous()
         if world() > 1:
-            tb = torch.as_tensor(b, device="cuda")
-            dist.broadcast(tb, src=0)
+            cb = _cb()
+            cb.check(cb.lib.mmp_broadcast(ctypes.c_void_p(b._ptr), ctypes.c_void_p(b._ptr),
+                                          int(b.size) * np.dtype(b.dtype).itemsize, cb.dtype_code(np.uint8), 0),
+                     "broadcast B")
         c = linalg_top.matmul(self.local, b)
         return DistArray(c, (self.global_shape[0], b.shape[1]), self.start, self.stop)
-
-
-def _torch_dt(dt):
-    import torch
-
-    return {np.dtype(np.float64): torch.float64, np.dtype(np.float32): torch.float32,
-            np.dtype(np.int64): torch.int64, np.dtype(np.uint64): torch.int64}.get(np.dtype(dt), torch.float64)
-
-
-def _int64():
-    import torch
-
-    return torch.int64
-
-
-def _uint8():
-    import torch
-
-    return torch.uint8

@@ -494,3 +494,135 @@ def lexsort(keys):
     """``sorting.lexsort`` (sorting.py:274-278): ``np.lexsort`` (stable, the
     last key primary)."""
     return np.lexsort(keys)
+
+
+# ---------------------------------------------------------------- distributed merge
+# The reference is single-device; its full reductions (ndarray._reduce,
+# ndarray.py:1895-1963; reductions.var, reductions.py:525-584;
+# reductions.argmax, reductions.py:381-418) are what a block-distributed
+# array must reproduce.  These two functions restate, in numpy, the per-shard
+# partial that the GPU writes (mmp_reduce_partial) and the ordered merge that
+# folds the gathered partials (mmp_merge_partials), so that the merge rule is
+# checked on CPU (gloo ranks) and the GPU merge kernel against this.
+
+PARTIAL_FIELDS = ("s1", "s2", "shift", "count", "ival", "index")
+
+
+def shard_partial(op, x, index_base=0):
+    """The partial of one shard: a dict with the fields of ``mmp_partial``.
+    Sums are float64 (floats) or exact int64 (integers); var keeps the shifted
+    moments around the shard's first element; argmax/argmin keep (value,
+    global index), numpy's first occurrence with NaN first."""
+    x = np.asarray(x).reshape(-1)
+    p = dict(s1=0.0, s2=0.0, shift=0.0, count=0, ival=0, index=-1)
+    isf = x.dtype.kind == "f"
+    n = x.size
+    if op in ("sum", "mean"):
+        p["count"] = n
+        if isf:
+            p["s1"] = float(x.astype(np.float64).sum())
+        else:
+            p["ival"] = int(x.astype(np.int64).sum())
+            p["s1"] = float(p["ival"])
+    elif op in ("var", "std"):
+        p["count"] = n
+        if n:
+            k = float(x[0])
+            d = x.astype(np.float64) - k
+            p.update(s1=float(d.sum()), s2=float((d * d).sum()), shift=k)
+    elif op in ("nansum", "nanmean"):
+        ok = ~np.isnan(x)
+        p.update(s1=float(x[ok].astype(np.float64).sum()), count=int(ok.sum()))
+    elif op in ("nanvar", "nanstd"):
+        v = x[~np.isnan(x)].astype(np.float64)
+        if v.size:
+            d = v - v[0]
+            p.update(s1=float(d.sum()), s2=float((d * d).sum()), shift=float(v[0]), count=int(v.size))
+    elif op in ("max", "min"):
+        if n:
+            v = (np.max if op == "max" else np.min)(x)
+            p.update(s1=float(v), ival=0 if isf else int(v), count=n)
+    elif op in ("argmax", "argmin"):
+        p["count"] = n
+        if n:
+            i = int(np.argmax(x) if op == "argmax" else np.argmin(x))
+            p.update(s1=float(x[i]), ival=0 if isf else int(x[i]), index=index_base + i)
+    else:
+        raise ValueError(op)
+    return p
+
+
+def merge_partials(op, parts, isfloat=True, ddof=0.0):
+    """Fold shard partials in rank order into the reduction's result (the
+    restatement of mmp_merge_partials).  var/std: each shard's shifted sums
+    move to the first present shard's shift k_a with d = k_b - k_a,
+    S1 += S1_b + n_b d, S2 += S2_b + d (2 S1_b + n_b d); then
+    var = (S2 - S1^2/n) / (n - ddof)."""
+    n = sum(int(p["count"]) for p in parts)
+    if op in ("sum", "mean"):
+        if isfloat:
+            t = 0.0
+            for p in parts:
+                t += p["s1"]
+        else:
+            t = 0
+            for p in parts:
+                t += int(p["ival"])
+        return t if op == "sum" else (float(t) / n if n else float("nan"))
+    if op in ("nansum", "nanmean"):
+        t = 0.0
+        for p in parts:
+            t += p["s1"]
+        return t if op == "nansum" else (t / n if n else float("nan"))
+    if op in ("var", "std", "nanvar", "nanstd"):
+        s1 = s2 = k = 0.0
+        seen = False
+        for p in parts:
+            if p["count"] <= 0:
+                continue
+            if not seen:
+                s1, s2, k, seen = p["s1"], p["s2"], p["shift"], True
+            else:
+                nb, d = float(p["count"]), p["shift"] - k
+                s2 += p["s2"] + d * (2.0 * p["s1"] + nb * d)
+                s1 += p["s1"] + nb * d
+        m2 = max(s2 - s1 * s1 / n, 0.0) if n else float("nan")
+        dof = n - ddof
+        if op.startswith("nan") and dof <= 0:
+            return float("nan")
+        var = m2 / max(dof, 0) if dof > 0 else (float("inf") if m2 > 0 else float("nan"))
+        return float(np.sqrt(var)) if op.endswith("std") else var
+    if op in ("max", "min"):
+        best = None
+        for p in parts:
+            if p["count"] <= 0:
+                continue
+            v = p["s1"] if isfloat else p["ival"]
+            if best is None:
+                best = v
+            elif isfloat and np.isnan(best):
+                continue  # NaN propagates: the first NaN stays
+            elif (isfloat and np.isnan(v)) or ((v > best) if op == "max" else (v < best)):
+                best = v
+        return best
+    if op in ("argmax", "argmin"):
+        best = None
+        for p in parts:
+            if p["index"] < 0:
+                continue
+            v, i = (p["s1"] if isfloat else p["ival"]), int(p["index"])
+            if best is None:
+                best = (v, i)
+                continue
+            bv, bi = best
+            vn, bn = isfloat and np.isnan(v), isfloat and np.isnan(bv)
+            if vn or bn:
+                take = (i < bi) if (vn and bn) else vn
+            elif v != bv:
+                take = (v > bv) if op == "argmax" else (v < bv)
+            else:
+                take = i < bi
+            if take:
+                best = (v, i)
+        return -1 if best is None else best[1]
+    raise ValueError(op)

@@ -1,10 +1,11 @@
-"""Block-distributed arrays on 2 GPUs over NCCL, against the oracle on the
-whole array: sum / mean / var / argmax / argmin / max / nansum / nanmean
-(all-reduce and all-gather merges), 1-D cumsum with carries (int32 exact,
-float32 within 1e-4), axis-1 reductions and scans (shard-local), matmul
-with B broadcast from rank 0.  Needs two visible GPUs; skipped otherwise.
-Ranks are child processes with a short process-group timeout; NVLS is off
-(plain NCCL rings), as this test only checks results."""
+"""Block-distributed arrays on 2 GPUs over the library's own NCCL
+collectives (C ABI), against the oracle on the whole array: sum / mean /
+var / argmax / argmin / max / nansum / nanmean (device partials, all-gather,
+device merge), 1-D cumsum with device carries (int32 exact, float32 within
+1e-4), axis-0 sums (all-reduce), axis-1 reductions and scans (shard-local),
+matmul with B broadcast from rank 0.  Needs two visible GPUs; skipped
+otherwise.  Ranks are child processes with a short communicator timeout;
+NVLS is off (plain NCCL rings), as this test only checks results."""
 
 import os
 import socket
@@ -41,28 +42,32 @@ def _rank_main(rank, world, port, q):
         from macmetalpy_b200 import distributed as D
         from macmetalpy_b200.creation import array, zeros
 
-        dist = D.init(backend="nccl", timeout_s=60)
+        D.init(timeout_s=60)
         rng = np.random.default_rng(7)
         x = rng.standard_normal(1_000_003).astype(np.float32) + 0.25
         X = D.DistArray.from_global(x)
         x64 = x.astype(np.float64)
-        assert abs(X.sum() - x64.sum()) <= 1e-4 * np.abs(x64).sum()
-        assert abs(X.mean() - x64.mean()) <= 1e-4 * abs(x64.mean())
-        assert abs(X.var() - x64.var()) <= 1e-4 * x64.var()
+        assert abs(float(X.sum()) - x64.sum()) <= 1e-4 * np.abs(x64).sum()
+        assert abs(float(X.mean()) - x64.mean()) <= 1e-4 * abs(x64.mean())
+        assert abs(float(X.var()) - x64.var()) <= 1e-4 * x64.var()
         assert X.argmax() == O.argmax(x)
         assert X.argmin() == int(np.argmin(x))
-        assert X.max() == float(x.max())
+        assert float(X.max()) == float(x.max())
+        xt = x.copy()
+        xt[[3, 900000]] = x.max() + 1  # a tie across the two shards
+        assert D.DistArray.from_global(xt).argmax() == 3
         xn = x.copy()
         xn[rng.choice(x.size, 1000, replace=False)] = np.nan
         XN = D.DistArray.from_global(xn)
-        assert abs(XN.nansum() - np.nansum(xn.astype(np.float64))) <= 1e-4 * np.nansum(np.abs(xn))
-        assert abs(XN.nanmean() - np.nanmean(xn.astype(np.float64))) <= 1e-4 * abs(np.nanmean(xn))
+        assert abs(float(XN.nansum()) - np.nansum(xn.astype(np.float64))) <= 1e-4 * np.nansum(np.abs(xn))
+        assert abs(float(XN.nanmean()) - np.nanmean(xn.astype(np.float64))) <= 1e-4 * abs(np.nanmean(xn))
+        assert XN.argmax() == O.argmax(xn)
         xi = rng.integers(-100, 101, 3_000_017).astype(np.int32)
         XI = D.DistArray.from_global(xi)
-        assert XI.sum() == int(xi.sum(dtype=np.int64))
+        assert int(XI.sum()) == int(xi.sum(dtype=np.int64))
         np.testing.assert_array_equal(XI.cumsum().gather(), O.cumsum(xi))
         xf = rng.uniform(0, 1, 2_000_001).astype(np.float32)
-        got = XF = D.DistArray.from_global(xf).cumsum().gather()
+        got = D.DistArray.from_global(xf).cumsum().gather()
         ref = O.cumsum_f64(xf)
         assert np.max(np.abs(got - ref) / ref) <= 1e-4
         m = rng.standard_normal((1001, 515)).astype(np.float32)
@@ -80,8 +85,8 @@ def _rank_main(rank, world, port, q):
         C = A.matmul(Bl).gather()
         r = O.matmul_f64(a, b)
         assert np.linalg.norm(C - r) / np.linalg.norm(r) <= 1e-5
-        dist.barrier()
-        dist.destroy_process_group()
+        D.barrier()
+        D.finalize()
         q.put((rank, "ok"))
     except Exception:
         import traceback
