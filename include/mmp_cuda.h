@@ -261,10 +261,12 @@ int mmp_merge_partials(int op, int dtype, const mmp_partial *dev_parts, int npar
  * pointers; count is in elements of dtype (bool is sent as 1-byte words).
  * A call that does not complete within the communicator's timeout aborts
  * it and returns MMP_E_COMM. */
-#define MMP_COMM_ID_BYTES 128
+#define MMP_COMM_ID_BYTES 256
 enum mmp_comm_op { MMP_COMM_SUM = 0, MMP_COMM_PROD = 1, MMP_COMM_MAX = 2, MMP_COMM_MIN = 3 };
 int mmp_nccl_version(int *version);
-/* Rank 0 creates the id and hands the 128 bytes to every rank out of band. */
+/* Rank 0 creates the id (MMP_COMM_ID_BYTES: two NCCL ids, one for a
+ * bounded bootstrap, one for the data-plane communicator) and hands the
+ * bytes to every rank out of band. */
 int mmp_comm_unique_id(void *id);
 /* Join the communicator of nranks ranks as `rank`, on the current device
  * (after mmp_init).  Blocks until every rank joined or timeout_s passed. */

@@ -1,7 +1,7 @@
-"""Out-of-band hand-over of the communicator id (128 bytes, rank 0 -> all).
+"""Out-of-band hand-over of the communicator id (rank 0 -> all ranks).
 
 This is the only control-plane step of the multi-GPU path: NCCL needs every
-rank to hold the same ``ncclUniqueId`` before ``mmp_comm_init``.  Two
+rank to hold the same ids (``MMP_COMM_ID_BYTES``) before ``mmp_comm_init``.  Two
 transports:
 
 * torch's ``TCPStore`` when torch is importable.  Under ``torchrun`` the
@@ -9,8 +9,9 @@ transports:
   (``TORCHELASTIC_USE_AGENT_STORE=True``) and every rank connects to it as a
   client; otherwise rank 0 hosts the store.  torch is used as a key-value
   store only: no tensor and no process group is created.
-* a plain TCP socket otherwise: rank 0 listens on ``MASTER_ADDR:MASTER_PORT``
-  (or ``MMP_RDZV_PORT``), the other ranks connect and read the bytes.
+* a plain TCP socket otherwise (or with ``MMP_RDZV=socket``): rank 0 listens
+  on ``MASTER_ADDR:MASTER_PORT`` (``MASTER_PORT + 1`` under torchrun's agent
+  store, or ``MMP_RDZV_PORT``), the other ranks connect and read the bytes.
 
 Both give up after ``timeout_s`` with ``TimeoutError``, so a rank that never
 arrives ends the others with an error instead of a hang.
@@ -27,12 +28,38 @@ __all__ = ["exchange_root_bytes"]
 _generation = [0]
 
 
+def _agent_store() -> bool:
+    return os.environ.get("TORCHELASTIC_USE_AGENT_STORE", "").lower() == "true"
+
+
 def _addr_port() -> tuple[str, int]:
     addr = os.environ.get("MASTER_ADDR", "127.0.0.1")
-    port = os.environ.get("MMP_RDZV_PORT") or os.environ.get("MASTER_PORT")
-    if not port:
+    port = os.environ.get("MASTER_PORT")
+    if not port and not os.environ.get("MMP_RDZV_PORT"):
         raise RuntimeError("MASTER_PORT (or MMP_RDZV_PORT) must be set for a multi-rank communicator")
-    return addr, int(port)
+    return addr, int(port or 0)
+
+
+def _socket_port(port: int) -> int:
+    # under torchrun the launcher's store already listens on MASTER_PORT
+    if os.environ.get("MMP_RDZV_PORT"):
+        return int(os.environ["MMP_RDZV_PORT"])
+    return port + 1 if _agent_store() else port
+
+
+def transport() -> str:
+    """"store" (torch's TCPStore) or "socket".  Deciding imports torch when
+    it is present: call this before NCCL is opened, so that a torch in the
+    process loads its own NCCL first and the library's dlopen then returns
+    that same copy (torch does not import against an older NCCL that is
+    already loaded)."""
+    if os.environ.get("MMP_RDZV", "") == "socket":
+        return "socket"
+    try:
+        import torch.distributed  # noqa: F401
+    except ImportError:
+        return "socket"
+    return "store"
 
 
 def _via_store(payload, rank, world, timeout_s, nbytes):
@@ -41,7 +68,7 @@ def _via_store(payload, rank, world, timeout_s, nbytes):
     from torch.distributed import TCPStore  # key-value store only
 
     addr, port = _addr_port()
-    agent = os.environ.get("TORCHELASTIC_USE_AGENT_STORE", "").lower() == "true"
+    agent = _agent_store()
     kw = {} if agent else {"multi_tenant": True}
     store = TCPStore(addr, port, world, is_master=(rank == 0 and not agent),
                      timeout=datetime.timedelta(seconds=timeout_s), **kw)
@@ -76,6 +103,7 @@ def _recv_exact(s, n):
 
 def _via_socket(payload, rank, world, timeout_s, nbytes):
     addr, port = _addr_port()
+    port = _socket_port(port)
     deadline = time.monotonic() + timeout_s
     if rank == 0:
         srv = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
@@ -110,16 +138,17 @@ def _via_socket(payload, rank, world, timeout_s, nbytes):
         return _recv_exact(s, nbytes)
 
 
-def exchange_root_bytes(payload, rank: int, world: int, timeout_s: float = 120.0, nbytes: int = 128) -> bytes:
-    """Rank 0 passes ``payload`` (``nbytes`` bytes); every rank returns it."""
+def exchange_root_bytes(payload, rank: int, world: int, timeout_s: float = 120.0, nbytes: int = 128,
+                        how: str | None = None) -> bytes:
+    """Rank 0 passes ``payload`` (``nbytes`` bytes, or a callable that makes
+    them, called on rank 0 after the transport is chosen); every rank
+    returns those bytes."""
+    how = how or transport()
+    if rank == 0 and callable(payload):
+        payload = payload()
     if world <= 1:
         return bytes(payload)
     _generation[0] += 1
-    try:
-        import torch.distributed  # noqa: F401
-        have_store = True
-    except Exception:
-        have_store = False
-    if have_store and os.environ.get("MMP_RDZV", "") != "socket":
+    if how == "store":
         return _via_store(payload, rank, world, timeout_s, nbytes)
     return _via_socket(payload, rank, world, timeout_s, nbytes)

@@ -14,11 +14,12 @@
 // loaded NCCL (e.g. through torch), dlopen returns that copy.  nccl.h is
 // used for its types only.
 //
-// The communicator is created non-blocking: every call that NCCL reports
-// as still in progress is polled on the host with a deadline (the init
-// timeout passed to mmp_comm_init), and a communicator that does not become
-// ready in time is aborted and reported as MMP_E_COMM, so a rank that never
-// joins, or a peer that died, ends in an error instead of a hang.
+// Joining is bounded: a non-blocking bootstrap communicator is polled on the
+// host with a deadline (the timeout passed to mmp_comm_init) and aborted if
+// it is not ready in time (MMP_E_COMM), so a rank that never joins ends in an
+// error instead of a hang.  The data plane then uses a blocking communicator
+// split from it; mmp_comm_synchronize bounds the wait for its collectives and
+// aborts both communicators when a peer is gone.
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -55,8 +56,17 @@ struct NcclApi {
 NcclApi g_api;
 std::mutex g_api_mu;
 
+// `comm` carries the data plane and is blocking: a collective call returns
+// once its kernel is enqueued.  (In NCCL's non-blocking mode every call is
+// handed to a new host thread and returns ncclInProgress, which cost
+// ~150 us per collective here.)  `boot` is a non-blocking communicator made
+// first from the first of the two ids: creating it can be polled with a
+// deadline, so a rank that never joins ends init with an error; the
+// blocking one is then created (second id) among ranks that are all
+// present, and `boot` is released.
 struct CommState {
   ncclComm_t comm = nullptr;
+  ncclComm_t boot = nullptr;
   int rank = -1;
   int nranks = 0;
   double timeout_s = 120.0;
@@ -64,6 +74,15 @@ struct CommState {
 constexpr int kMaxDev = 64;
 CommState g_comm[kMaxDev];
 std::mutex g_comm_mu;
+
+void drop(CommState *c, bool abort) {
+  if (c->comm) (abort ? g_api.CommAbort : g_api.CommDestroy)(c->comm);
+  if (c->boot) g_api.CommAbort(c->boot);
+  c->comm = nullptr;
+  c->boot = nullptr;
+  c->rank = -1;
+  c->nranks = 0;
+}
 
 double now_s() {
   timespec ts;
@@ -128,26 +147,32 @@ CommState *cur_comm(int *rc) {
 }
 
 // Poll a non-blocking communicator until NCCL reports it ready, an error, or
-// the deadline passes (then abort it: pending NCCL kernels stop).
-int wait_ready(CommState *c, ncclResult_t r, const char *what) {
+// the deadline passes (then abort everything: pending NCCL kernels stop).
+int wait_comm(CommState *c, ncclComm_t comm, ncclResult_t r, const char *what) {
   if (r == ncclSuccess) return MMP_OK;
   if (r != ncclInProgress) return nccl_error(r, what);
   const double t0 = now_s();
-  for (;;) {
+  for (int it = 0;; ++it) {
     ncclResult_t st = ncclSuccess;
-    ncclResult_t q = g_api.CommGetAsyncError(c->comm, &st);
+    ncclResult_t q = g_api.CommGetAsyncError(comm, &st);
     if (q != ncclSuccess) return nccl_error(q, what);
     if (st == ncclSuccess) return MMP_OK;
-    if (st != ncclInProgress) return nccl_error(st, what);
+    if (st != ncclInProgress) {
+      drop(c, true);
+      return nccl_error(st, what);
+    }
     if (now_s() - t0 > c->timeout_s) {
-      g_api.CommAbort(c->comm);
-      c->comm = nullptr;
-      c->rank = -1;
-      c->nranks = 0;
+      drop(c, true);
       return mmp::set_error(MMP_E_COMM, std::string(what) + ": timed out; communicator aborted");
     }
-    usleep(200);
+    if (it > 1000) usleep(100);
   }
+}
+
+// A blocking call's status (the data-plane communicator is blocking).
+int check_call(ncclResult_t r, const char *what) {
+  if (r == ncclSuccess) return MMP_OK;
+  return nccl_error(r, what);
 }
 
 bool nccl_type(int dt, ncclDataType_t *t) {
@@ -181,11 +206,13 @@ extern "C" int mmp_comm_unique_id(void *id) {
   if (!id) return mmp::set_error(MMP_E_ARG, "null id buffer");
   int rc = load_api();
   if (rc) return rc;
-  static_assert(sizeof(ncclUniqueId) == MMP_COMM_ID_BYTES, "ncclUniqueId size");
-  ncclUniqueId u;
-  ncclResult_t r = g_api.GetUniqueId(&u);
-  if (r != ncclSuccess) return nccl_error(r, "ncclGetUniqueId");
-  memcpy(id, &u, sizeof u);
+  static_assert(2 * sizeof(ncclUniqueId) == MMP_COMM_ID_BYTES, "ncclUniqueId size");
+  for (int k = 0; k < 2; ++k) {  // bootstrap id, data-plane id
+    ncclUniqueId u;
+    ncclResult_t r = g_api.GetUniqueId(&u);
+    if (r != ncclSuccess) return nccl_error(r, "ncclGetUniqueId");
+    memcpy((char *)id + k * sizeof u, &u, sizeof u);
+  }
   return MMP_OK;
 }
 
@@ -205,13 +232,33 @@ extern "C" int mmp_comm_init(int nranks, int rank, const void *id, double timeou
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
   c->timeout_s = timeout_s > 0 ? timeout_s : 120.0;
-  ncclComm_t comm = nullptr;
-  ncclResult_t r = g_api.CommInitRankConfig(&comm, nranks, u, rank, &cfg);
-  if (r != ncclSuccess && r != ncclInProgress) return nccl_error(r, "ncclCommInitRankConfig");
-  c->comm = comm;
   c->rank = rank;
   c->nranks = nranks;
-  return wait_ready(c, r, "ncclCommInitRankConfig");
+  ncclComm_t boot = nullptr;
+  ncclResult_t r = g_api.CommInitRankConfig(&boot, nranks, u, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    c->rank = -1;
+    c->nranks = 0;
+    return nccl_error(r, "ncclCommInitRankConfig");
+  }
+  c->boot = boot;
+  rc = wait_comm(c, boot, r, "ncclCommInitRankConfig");
+  if (rc) return rc;
+  // every rank is present: create the blocking data-plane communicator
+  ncclUniqueId u2;
+  memcpy(&u2, (const char *)id + sizeof(ncclUniqueId), sizeof u2);
+  ncclConfig_t cfg2 = NCCL_CONFIG_INITIALIZER;
+  cfg2.blocking = 1;
+  ncclComm_t data = nullptr;
+  r = g_api.CommInitRankConfig(&data, nranks, u2, rank, &cfg2);
+  if (r != ncclSuccess || !data) {
+    drop(c, true);
+    return nccl_error(r, "ncclCommInitRankConfig (data plane)");
+  }
+  g_api.CommAbort(boot);  // no work was ever enqueued on it
+  c->boot = nullptr;
+  c->comm = data;
+  return MMP_OK;
 }
 
 extern "C" int mmp_comm_rank(int *rank, int *nranks) {
@@ -234,8 +281,7 @@ extern "C" int mmp_comm_destroy(void) {
   if (st) MMP_CUDA_TRY(cudaStreamSynchronize(st));
   ncclResult_t r = g_api.CommDestroy(c->comm);
   c->comm = nullptr;
-  c->rank = -1;
-  c->nranks = 0;
+  drop(c, true);  // the boot communicator has no work in flight
   if (r != ncclSuccess) return nccl_error(r, "ncclCommDestroy");
   return MMP_OK;
 }
@@ -246,11 +292,7 @@ extern "C" int mmp_comm_abort(void) {
   std::lock_guard<std::mutex> lk(g_comm_mu);
   CommState *c = &g_comm[dev];
   if (!c->comm) return MMP_OK;
-  ncclResult_t r = g_api.CommAbort(c->comm);
-  c->comm = nullptr;
-  c->rank = -1;
-  c->nranks = 0;
-  if (r != ncclSuccess) return nccl_error(r, "ncclCommAbort");
+  drop(c, true);
   return MMP_OK;
 }
 
@@ -263,7 +305,7 @@ extern "C" int mmp_allreduce(const void *send, void *recv, size_t count, int dty
   if (!nccl_type(dtype, &t)) return mmp::set_error(MMP_E_ARG, "dtype not supported by the collective");
   if (!nccl_op(op, &o)) return mmp::set_error(MMP_E_ARG, "bad collective op");
   if (count && (!send || !recv)) return mmp::set_error(MMP_E_ARG, "null pointer");
-  return wait_ready(c, g_api.AllReduce(send, recv, count, t, o, c->comm, mmp::stream()), "ncclAllReduce");
+  return check_call(g_api.AllReduce(send, recv, count, t, o, c->comm, mmp::stream()), "ncclAllReduce");
 }
 
 extern "C" int mmp_allgather(const void *send, void *recv, size_t count, int dtype) {
@@ -273,7 +315,7 @@ extern "C" int mmp_allgather(const void *send, void *recv, size_t count, int dty
   ncclDataType_t t;
   if (!nccl_type(dtype, &t)) return mmp::set_error(MMP_E_ARG, "dtype not supported by the collective");
   if (count && (!send || !recv)) return mmp::set_error(MMP_E_ARG, "null pointer");
-  return wait_ready(c, g_api.AllGather(send, recv, count, t, c->comm, mmp::stream()), "ncclAllGather");
+  return check_call(g_api.AllGather(send, recv, count, t, c->comm, mmp::stream()), "ncclAllGather");
 }
 
 extern "C" int mmp_broadcast(const void *send, void *recv, size_t count, int dtype, int root) {
@@ -284,7 +326,7 @@ extern "C" int mmp_broadcast(const void *send, void *recv, size_t count, int dty
   if (!nccl_type(dtype, &t)) return mmp::set_error(MMP_E_ARG, "dtype not supported by the collective");
   if (root < 0 || root >= c->nranks) return mmp::set_error(MMP_E_ARG, "bad root rank");
   if (count && !recv) return mmp::set_error(MMP_E_ARG, "null pointer");
-  return wait_ready(c, g_api.Broadcast(send, recv, count, t, root, c->comm, mmp::stream()), "ncclBroadcast");
+  return check_call(g_api.Broadcast(send, recv, count, t, root, c->comm, mmp::stream()), "ncclBroadcast");
 }
 
 extern "C" int mmp_group_start(void) {
@@ -299,11 +341,8 @@ extern "C" int mmp_group_end(void) {
   int rc = load_api();
   if (rc) return rc;
   ncclResult_t r = g_api.GroupEnd();
-  if (r == ncclSuccess) return MMP_OK;
-  int dev = mmp::current_device();
-  if (r == ncclInProgress && dev >= 0 && dev < kMaxDev && g_comm[dev].comm)
-    return wait_ready(&g_comm[dev], r, "ncclGroupEnd");
-  return nccl_error(r, "ncclGroupEnd");
+  if (r != ncclSuccess) return nccl_error(r, "ncclGroupEnd");
+  return MMP_OK;
 }
 
 // Wait until every collective and kernel enqueued on this device's stream
@@ -324,17 +363,11 @@ extern "C" int mmp_comm_synchronize(double timeout_s) {
     ncclResult_t as = ncclSuccess;
     g_api.CommGetAsyncError(c->comm, &as);
     if (as != ncclSuccess && as != ncclInProgress) {
-      g_api.CommAbort(c->comm);
-      c->comm = nullptr;
-      c->rank = -1;
-      c->nranks = 0;
+      drop(c, true);
       return nccl_error(as, "communicator failed; aborted");
     }
     if (now_s() - t0 > limit) {
-      g_api.CommAbort(c->comm);
-      c->comm = nullptr;
-      c->rank = -1;
-      c->nranks = 0;
+      drop(c, true);
       return mmp::set_error(MMP_E_COMM, "collectives did not finish in time (a rank is gone?); communicator aborted");
     }
     usleep(50);

@@ -42,6 +42,7 @@ __all__ = ["init", "finalize", "row_partition", "DistArray", "world", "rank", "b
            "synchronize"]
 
 PARTIAL_BYTES = 48  # sizeof(mmp_partial)
+ID_BYTES = 256  # MMP_COMM_ID_BYTES
 _state = {"init": False, "rank": 0, "world": 1, "parts": None, "timeout": 120.0}
 
 
@@ -56,7 +57,7 @@ def init(timeout_s: float = 120.0):
     ``WORLD_SIZE`` ranks as ``RANK`` (``MASTER_ADDR`` / ``MASTER_PORT`` carry
     the id hand-over).  A rank that does not arrive within ``timeout_s``
     ends the others' ``init`` with ``RuntimeError``."""
-    from ._rendezvous import exchange_root_bytes
+    from ._rendezvous import exchange_root_bytes, transport
 
     if _state["init"]:
         return
@@ -65,13 +66,17 @@ def init(timeout_s: float = 120.0):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     r = int(os.environ.get("RANK", "0"))
     w = int(os.environ.get("WORLD_SIZE", "1"))
+    how = transport()  # before NCCL is opened (see _rendezvous.transport)
     cb = _cb()
     cb.CudaBackend()  # mmp_init(LOCAL_RANK)
-    uid = ctypes.create_string_buffer(128)
-    if r == 0:
+
+    def make_id():
+        uid = ctypes.create_string_buffer(ID_BYTES)
         cb.check(cb.lib.mmp_comm_unique_id(uid), "mmp_comm_unique_id")
-    got = exchange_root_bytes(uid.raw, r, w, timeout_s)
-    uid = ctypes.create_string_buffer(got, 128)
+        return uid.raw
+
+    got = exchange_root_bytes(make_id, r, w, timeout_s, nbytes=ID_BYTES, how=how)
+    uid = ctypes.create_string_buffer(got, ID_BYTES)
     cb.check(cb.lib.mmp_comm_init(w, r, uid, float(timeout_s)), "mmp_comm_init")
     _state.update(init=True, rank=r, world=w, timeout=float(timeout_s))
     _state["parts"] = cb.DeviceBuffer(PARTIAL_BYTES * (w + 1))
