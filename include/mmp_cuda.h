@@ -179,7 +179,8 @@ int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y,
  * buffers, or code holding that framework's allocator lock.  Same arguments
  * and results as mmp_scan.  No counterpart in the reference (it has no such
  * callers).  The look-back state lives in a fixed device array of this
- * library (about 4 MiB per GPU that loads it, kept until exit), so scans
+ * library (16 bytes per tile: about 3.2 MiB per GPU that loads it, kept
+ * until exit), so scans
  * longer than MMP_NOALLOC_SCAN_TILES tiles of 4096 elements per row-set
  * (outer * ceil(k / 4096)) are rejected with MMP_E_ARG.  Calls share the
  * array: calls that may overlap on the GPU race and must be serialised by

@@ -24,6 +24,7 @@ ScanState g_scan[64];
 
 int scan_state(long long tiles, void **desc, unsigned **counter, unsigned *epoch) {
   int dev = current_device();
+  if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
   ScanState &s = g_scan[dev];
   cudaStream_t st = stream();
   if ((size_t)tiles > s.tiles) {
@@ -185,8 +186,8 @@ struct ScanRun {
       return MMP_OK;
     }
     long long tpr = (k + STILE - 1) / STILE;
+    if (rows > 0x7fffffffll / tpr) return set_error(MMP_E_ARG, "scan too large");  // before rows * tpr can wrap
     long long total = rows * tpr;
-    if (total > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
     int vec_ok = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (k % 16 == 0);
     if (tpr >= kLongRowTiles && rows * k >= kLongRowElements) return long_rows(x, y, rows, k, tpr, total, cin, vec_ok);
     void *desc;
@@ -233,16 +234,17 @@ extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y
 //
 // The array holds the state of at most MMP_NOALLOC_SCAN_TILES tiles of
 // 4096 elements; larger scans are rejected with MMP_E_ARG.  Every GPU that
-// loads the library keeps the array (about 4 MiB) until the process exits.
+// loads the library keeps the array (about 3.2 MiB) until the process exits.
 // All calls share it: calls that can overlap on the GPU (different streams
 // or devices sharing nothing else) race on it and must be serialised by the
 // caller.  The first call on each device looks up the array's address with
 // cudaGetSymbolAddress; make that first call before any stream capture.
 // The caller must have called mmp_init on the device.
 // ---------------------------------------------------------------------------
-// Look-back state of mmp_scan_noalloc: 16-byte tile descriptors, then the
-// tile counter.
-static __device__ __align__(256) unsigned char g_noalloc_scan[(size_t)MMP_NOALLOC_SCAN_TILES * 20 + 256];
+// Look-back state of mmp_scan_noalloc: one 16-byte descriptor per tile
+// (TileDesc: an 8-byte value and an 8-byte flag), then the 4-byte tile
+// counter in the 256-byte tail.
+static __device__ __align__(256) unsigned char g_noalloc_scan[(size_t)MMP_NOALLOC_SCAN_TILES * 16 + 256];
 
 namespace mmp {
 namespace {
@@ -275,16 +277,18 @@ struct ScanNoallocRun {
       return set_error(MMP_E_ARG, "scan output dtype must be the numpy accumulation type");
     if (inner > 1 || k < STILE / 4)  // these shapes need no scratch at all
       return ScanRun<PRODI, T>::run(xv, out_dt, yv, outer, k, inner, carry);
+    static_assert(sizeof(TileDesc<C>) == 16, "the counter sits after kNoallocTiles 16-byte descriptors");
     const long long tpr = (k + STILE - 1) / STILE;
-    const long long total = outer * tpr;
-    if (total > (long long)kNoallocTiles) {
+    // compare before multiplying: outer * tpr could wrap for absurd extents
+    if (outer > (long long)kNoallocTiles / tpr) {
       char msg[200];
       snprintf(msg, sizeof msg,
-               "mmp_scan_noalloc: %lld tiles of %d elements exceed the fixed scratch of %zu tiles; "
-               "use mmp_scan",
-               total, STILE, kNoallocTiles);
+               "mmp_scan_noalloc: %lld rows of %lld tiles of %d elements exceed the fixed scratch of %zu "
+               "tiles; use mmp_scan",
+               outer, tpr, STILE, kNoallocTiles);
       return set_error(MMP_E_ARG, msg);
     }
+    const long long total = outer * tpr;
     unsigned char *base = nullptr;
     int rc = noalloc_state(&base);
     if (rc) return rc;

@@ -1,9 +1,11 @@
 """Math functions (mirrors ``src/macmetalpy/math_ops.py:15-103,540-548``).
 
 Every function builds a lazy fused node (``ndarray._elementwise``).
-``mod``/``remainder`` is ONE fused op with numpy's divmod semantics; the
-reference computes it as three kernels ``x1 - floor_divide(x1, x2) * x2``
-(``math_ops.py:540-548``), which differs from numpy for floats.
+``mod``/``remainder`` (and ``%``) compute the reference's own composite
+``x1 - floor_divide(x1, x2) * x2`` (``math_ops.py:540-548``), each step
+rounded to the dtype as the reference's three kernels round it, but as ONE
+fused kernel (``csrc/mmp_fused_ops.cuh``); for floats this is not numpy's
+``remainder``, and the golden vectors recorded from the reference pin it.
 ``dot`` of 1-D arrays is a fused multiply + sum reduction (the reference's
 ``_reduce_dot``, ``ndarray.py:1965-2013``); 2-D ``dot`` is ``matmul``.
 """

@@ -1,7 +1,8 @@
 """Generate the golden vectors in ``golden_v1.npz`` from the REFERENCE itself.
 
-Run in a container that has the reference checked out (read-only) at
-``$MMP_REFERENCE`` (default ``/root/reference``); the GPU box never runs this.
+Run in a container that has the reference checked out (read-only); its
+path is the first argument or ``$MMP_REFERENCE`` (required: there is no
+default); the GPU box never runs this.
 The reference refuses to import off macOS (``src/macmetalpy/__init__.py:5-6``)
 and its Metal path cannot run on Linux, so the script sets
 ``sys.platform = "darwin"`` only while importing, then raises every CPU/GPU
@@ -14,7 +15,8 @@ branch: for it the script records ``np.matmul``, the function the
 reference's ``cp.matmul`` CPU branch calls (``linalg_top.py:99-102``).
 
 Every input is seeded (numpy ``default_rng``) and shaped like the BASELINE
-configs at reduced size.  Usage: ``python tests/golden/make_golden.py``.
+configs at reduced size.  Usage:
+``python tests/golden/make_golden.py <reference checkout>``.
 """
 
 from __future__ import annotations
@@ -26,10 +28,12 @@ import warnings
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("MMP_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MMP_REFERENCE", "")
 
 
 def import_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "src", "macmetalpy")):
+        raise SystemExit("pass the reference checkout as the first argument or in $MMP_REFERENCE")
     sys.path.insert(0, os.path.join(REF, "src"))
     saved = sys.platform
     sys.platform = "darwin"

@@ -7,7 +7,11 @@ that runs while that framework holds its allocator lock.  It keeps its
 look-back state in a fixed array inside the library instead of scratch
 from the memory pool.  Here it must give the same results as mmp_scan on
 two calls in a row (the second call reuses the array the first one left
-behind), and refuse a scan larger than its fixed array.
+behind), allocate nothing -- the device's default memory pool, which every
+library allocation draws from, holds the same number of bytes before and
+after a call whose shape is larger than any scan made before it, so the
+library's growable look-back state would have had to grow -- and refuse a
+scan larger than its fixed array.
 
 The file sorts last so that a run stopping at its first failure has run
 every other test before this one."""
@@ -73,3 +77,37 @@ def test_noalloc_scan_rejects_more_than_its_array(cp):
                                  1, too_long, 1, None)
     assert rc == -2
     assert b"exceed" in cb.lib.mmp_last_error()
+
+
+def _pool_used_bytes():
+    """Bytes in use in the current device's default memory pool (the pool
+    every allocation of the library comes from), through the driver API."""
+    from cuda.bindings import driver as drv
+
+    err, dev = drv.cuCtxGetDevice()
+    assert err == drv.CUresult.CUDA_SUCCESS
+    err, pool = drv.cuDeviceGetDefaultMemPool(dev)
+    assert err == drv.CUresult.CUDA_SUCCESS
+    err, used = drv.cuMemPoolGetAttribute(pool, drv.CUmemPool_attribute.CU_MEMPOOL_ATTR_USED_MEM_CURRENT)
+    assert err == drv.CUresult.CUDA_SUCCESS
+    return int(used)
+
+
+def test_noalloc_scan_allocates_nothing(cp):
+    from macmetalpy_b200 import _cuda_backend as cb
+
+    # 25 x 2048 = 51200 tiles of 4096: beyond the look-back state any scan of
+    # this test suite leaves behind, within the fixed array (209715 tiles)
+    rows, k = 25, 1 << 23
+    rng = np.random.default_rng(9)
+    x = cp.array(rng.integers(-100, 101, (rows, k)).astype(np.int32))
+    y = cp.empty((rows, k), dtype=np.int64)
+    _scan(cb.lib, cb.lib.mmp_scan_noalloc, x, y, MMP_INT64, 1, 4 * 4096)  # first call on the device
+    cp.synchronize()
+    before = _pool_used_bytes()
+    _scan(cb.lib, cb.lib.mmp_scan_noalloc, x, y, MMP_INT64, rows, k)
+    cp.synchronize()
+    assert _pool_used_bytes() == before
+    got = y.get()
+    np.testing.assert_array_equal(got, np.cumsum(x.get(), axis=1, dtype=np.int64))
+
