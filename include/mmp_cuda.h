@@ -133,6 +133,9 @@ int mmp_event_elapsed_ms(void *start, void *end, float *ms);
 int mmp_stream_create(void **stream);          /* non-blocking stream */
 int mmp_stream_destroy(void *stream);
 int mmp_stream_synchronize(void *stream);
+/* *busy = 1 while work enqueued on the stream has not finished, else 0 (the
+ * reference's MetalBackend._has_pending, _metal_backend.py:341-372). */
+int mmp_stream_query(void *stream, int *busy);
 int mmp_stream_wait_event(void *stream, void *event);
 int mmp_event_record_on(void *event, void *stream);
 int mmp_h2d_async(void *dst, const void *src, size_t bytes, void *stream);

@@ -87,6 +87,7 @@ SIGNATURES = {
     "mmp_stream_create": (_int, [ctypes.POINTER(_vp)]),
     "mmp_stream_destroy": (_int, [_vp]),
     "mmp_stream_synchronize": (_int, [_vp]),
+    "mmp_stream_query": (_int, [_vp, ctypes.POINTER(_int)]),
     "mmp_stream_wait_event": (_int, [_vp, _vp]),
     "mmp_event_record_on": (_int, [_vp, _vp]),
     "mmp_h2d_async": (_int, [_vp, _vp, _sz, _vp]),

@@ -354,6 +354,20 @@ int mmp_stream_synchronize(void *stream) {
   return MMP_OK;
 }
 
+int mmp_stream_query(void *stream, int *busy) {
+  if (!busy) return set_error(MMP_E_ARG, "null pointer");
+  int rc = ensure_ready();
+  if (rc) return rc;
+  cudaError_t e = cudaStreamQuery(stream_or_lib(stream));
+  if (e == cudaErrorNotReady) {
+    *busy = 1;
+    return MMP_OK;
+  }
+  if (e != cudaSuccess) return cuda_error(e, "cudaStreamQuery");
+  *busy = 0;
+  return MMP_OK;
+}
+
 int mmp_stream_wait_event(void *stream, void *event) {
   if (!event) return set_error(MMP_E_ARG, "event is NULL");
   int rc = ensure_ready();
