@@ -10,34 +10,38 @@ means "compute in float32", which is how the reference resolves dtypes
 
 from __future__ import annotations
 
-import threading
 from typing import Literal
 
 __all__ = ["MacMetalConfig", "get_config", "set_config"]
 
+_CONFIG = None  # the one instance, made below at import
+
 
 class MacMetalConfig:
-    """Process-wide configuration singleton."""
+    """The process's configuration.  Its one instance is made when this
+    module is imported (under Python's import lock, so no lock of its own);
+    calling the class returns that instance, as the reference's singleton
+    does."""
 
-    _instance: "MacMetalConfig | None" = None
-    _lock = threading.Lock()
+    __slots__ = ("float64_behavior", "warn_on_downcast", "default_float_dtype", "fast_math")
 
     def __new__(cls) -> "MacMetalConfig":
-        with cls._lock:
-            if cls._instance is None:
-                inst = super().__new__(cls)
-                inst.float64_behavior = "cpu_fallback"
-                inst.warn_on_downcast = True
-                inst.default_float_dtype = "float32"
-                inst.fast_math = False
-                cls._instance = inst
-            return cls._instance
+        if _CONFIG is not None:
+            return _CONFIG
+        inst = super().__new__(cls)
+        inst.float64_behavior = "cpu_fallback"
+        inst.warn_on_downcast = True
+        inst.default_float_dtype = "float32"
+        inst.fast_math = False
+        return inst
+
+
+_CONFIG = MacMetalConfig()
 
 
 def get_config() -> MacMetalConfig:
-    """Return the global configuration singleton."""
-    inst = MacMetalConfig._instance  # fast path: no lock once created
-    return inst if inst is not None else MacMetalConfig()
+    """Return the global configuration."""
+    return _CONFIG
 
 
 def set_config(

@@ -197,9 +197,12 @@ class DeviceBuffer:
     __slots__ = ("ptr", "nbytes", "__weakref__")
 
     def __init__(self, nbytes: int):
-        CudaBackend()
-        self.nbytes = int(nbytes)
-        self.ptr = CudaBackend().malloc(self.nbytes)
+        if CudaBackend._instance is None:
+            CudaBackend()
+        self.nbytes = n = int(nbytes)
+        p = ctypes.c_void_p()
+        check(lib.mmp_malloc(n if n > 0 else 1, ctypes.byref(p)), "mmp_malloc")
+        self.ptr = p.value
 
     def __del__(self):
         p = getattr(self, "ptr", None)

@@ -54,6 +54,7 @@ __all__ = [
 _MAX_DEPTH = 16
 _MAX_NDIM = 8
 _BLOCK = 256
+_BLOCK3 = (ctypes.c_uint * 3)(_BLOCK, 1, 1)
 
 _CSRC = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
 
@@ -63,8 +64,39 @@ _CSRC = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc")
 # ---------------------------------------------------------------------------
 
 
+# Every node also carries, from its construction:
+#   _sig    -- the structure of its graph (op names and dtypes, leaves by
+#              kind only): the identity of the generated code up to the
+#              leaves' data layout;
+#   _leaves -- its leaf nodes (inputs and scalars) in the post-order the
+#              planner visits them, repeats included.
+# A repeated expression then finds its compiled kernel and launch template
+# from (_sig, the leaves' sharing pattern and layouts) without walking the
+# graph again.  Graphs whose leaf list would pass _MAX_LEAVES (heavy sharing
+# doubles it per level) carry None and take the full planner.
+_MAX_LEAVES = 64
+
+
+def _join_leaves(*parts):
+    n = 0
+    for p in parts:
+        if p is None:
+            return None
+        n += len(p)
+    if n > _MAX_LEAVES:
+        return None
+    out = parts[0]
+    for p in parts[1:]:
+        out = out + p
+    return out
+
+
+def _dt(x):
+    return x if isinstance(x, np.dtype) else np.dtype(x)
+
+
 class FusionNode:
-    __slots__ = ("_shape", "_dtype", "_depth")
+    __slots__ = ("_shape", "_dtype", "_depth", "_sig", "_leaves")
 
 
 class InputNode(FusionNode):
@@ -77,6 +109,8 @@ class InputNode(FusionNode):
         self._shape = array._shape
         self._dtype = array._dtype
         self._depth = 0
+        self._sig = ("in", self._dtype)
+        self._leaves = (self,)
 
 
 class ScalarNode(FusionNode):
@@ -89,6 +123,8 @@ class ScalarNode(FusionNode):
         self._value = np.asarray(value).astype(self._dtype)[()]
         self._shape = ()
         self._depth = 0
+        self._sig = ("sc", self._dtype)
+        self._leaves = (self,)
 
 
 class UnaryOpNode(FusionNode):
@@ -100,10 +136,13 @@ class UnaryOpNode(FusionNode):
     def __init__(self, op_name, input_node, shape, dtype, in_dtype=None):
         self._op_name = op_name
         self._input = input_node
-        self._in_dtype = np.dtype(in_dtype) if in_dtype is not None else np.dtype(dtype)
-        self._shape = tuple(shape)
-        self._dtype = np.dtype(dtype)
+        self._dtype = _dt(dtype)
+        self._in_dtype = _dt(in_dtype) if in_dtype is not None else self._dtype
+        self._shape = shape if shape.__class__ is tuple else tuple(shape)
         self._depth = input_node._depth + 1
+        self._leaves = input_node._leaves
+        self._sig = None if self._leaves is None else \
+            ("un", op_name, self._dtype, self._in_dtype, input_node._sig)
 
 
 class BinaryOpNode(FusionNode):
@@ -116,10 +155,13 @@ class BinaryOpNode(FusionNode):
         self._op_name = op_name
         self._lhs = lhs
         self._rhs = rhs
-        self._shape = tuple(shape)
-        self._dtype = np.dtype(dtype)
-        self._in_dtype = np.dtype(in_dtype) if in_dtype is not None else self._dtype
+        self._shape = shape if shape.__class__ is tuple else tuple(shape)
+        self._dtype = _dt(dtype)
+        self._in_dtype = _dt(in_dtype) if in_dtype is not None else self._dtype
         self._depth = max(lhs._depth, rhs._depth) + 1
+        self._leaves = _join_leaves(lhs._leaves, rhs._leaves)
+        self._sig = None if self._leaves is None else \
+            ("bin", op_name, self._dtype, self._in_dtype, lhs._sig, rhs._sig)
 
 
 class SelectNode(FusionNode):
@@ -134,6 +176,8 @@ class SelectNode(FusionNode):
         self._shape = tuple(shape)
         self._dtype = np.dtype(dtype)
         self._depth = max(cond._depth, x._depth, y._depth) + 1
+        self._leaves = _join_leaves(cond._leaves, x._leaves, y._leaves)
+        self._sig = None if self._leaves is None else ("sel", self._dtype, cond._sig, x._sig, y._sig)
 
 
 class CastNode(FusionNode):
@@ -144,6 +188,8 @@ class CastNode(FusionNode):
         self._shape = input_node._shape
         self._dtype = np.dtype(dtype)
         self._depth = input_node._depth + 1
+        self._leaves = input_node._leaves
+        self._sig = None if self._leaves is None else ("cast", self._dtype, input_node._sig)
 
 
 # ---------------------------------------------------------------------------
@@ -201,11 +247,27 @@ _MATH2 = {
 
 _CMP = {"lt_op": "<", "le_op": "<=", "gt_op": ">", "ge_op": ">=", "eq_op": "==", "ne_op": "!="}
 
+
 # bool predicates on the loop value (numpy: NaN is true, only zero is false)
 _LOGIC = {"logical_and_op": "&&", "logical_or_op": "||", "logical_xor_op": "!="}
 _BITS = {"bitwise_and_op": "&", "bitwise_or_op": "|", "bitwise_xor_op": "^"}
 _PRED = {"isnan_op": "mmpd::isnan_", "isinf_op": "mmpf::isinf_", "isfinite_op": "mmpf::isfinite_",
          "signbit_op": "mmpf::signbit_"}
+
+# Ops whose generated code is a library math call, a comparison, a select,
+# a bit operation or one of the rn_* operations: an expression made only of
+# these is compiled with --fmad=true (contraction inside the math library,
+# which CUDA's documented error bounds assume).  Every other op -- the
+# division family (floor_divide, mod, fmod), pow, logaddexp(2), hypot,
+# atan2, heaviside, nextafter -- has helpers whose exactness relies on each
+# + and * being rounded on its own, so expressions with them keep
+# --fmad=false.
+_FMAD_SAFE = frozenset(
+    set(_MATH1) | {"neg_op", "negative_op", "positive_op", "abs_op", "sign_op", "square_op", "degrees_op",
+                   "radians_op", "isnan_op", "isinf_op", "isfinite_op", "signbit_op", "logical_not_op",
+                   "invert_op", "reciprocal_op", "add_op", "sub_op", "mul_op", "div_op", "max_op",
+                   "min_op", "fmax_op", "fmin_op", "copysign_op", "left_shift_op", "right_shift_op"}
+    | set(_CMP) | set(_LOGIC) | set(_BITS))
 
 
 def _is_float(dt) -> bool:
@@ -235,15 +297,15 @@ def _unary_expr(op: str, dt, x: str) -> str:
     if op == "sign_op":
         return f"mmpf::sign_<{R}>({x})"
     if op == "square_op":
-        return f"({x} * {x})"
+        return f"mmpf::rn_mul({x}, {x})" if f else f"({x} * {x})"
     if op == "reciprocal_op":
         return f"({R}(1) / {x})" if f else f"({x} == {R}(0) ? {R}(0) : ({R})({R}(1) / {x}))"
     if op == "degrees_op":
         c = np.array(180.0, dt) / np.array(np.pi, dt) if dt != np.float16 else np.float32(180) / np.float32(np.pi)
-        return f"({x} * {_float_literal(float(c), dt if dt != np.float16 else np.dtype(np.float32))})"
+        return f"mmpf::rn_mul({x}, {_float_literal(float(c), dt if dt != np.float16 else np.dtype(np.float32))})"
     if op == "radians_op":
         c = np.array(np.pi, dt) / np.array(180.0, dt) if dt != np.float16 else np.float32(np.pi) / np.float32(180)
-        return f"({x} * {_float_literal(float(c), dt if dt != np.float16 else np.dtype(np.float32))})"
+        return f"mmpf::rn_mul({x}, {_float_literal(float(c), dt if dt != np.float16 else np.dtype(np.float32))})"
     if op == "cast":
         return x
     if op in _PRED:
@@ -268,11 +330,11 @@ def _binary_expr(op: str, dt, a: str, b: str) -> str:
     f = _is_float(dt)
     isbool = dt == np.bool_
     if op == "add_op":
-        return f"({a} || {b})" if isbool else f"({a} + {b})"
+        return f"({a} || {b})" if isbool else (f"mmpf::rn_add({a}, {b})" if f else f"({a} + {b})")
     if op == "sub_op":
-        return f"({a} - {b})"
+        return f"mmpf::rn_sub({a}, {b})" if f else f"({a} - {b})"
     if op == "mul_op":
-        return f"({a} && {b})" if isbool else f"({a} * {b})"
+        return f"({a} && {b})" if isbool else (f"mmpf::rn_mul({a}, {b})" if f else f"({a} * {b})")
     if op == "div_op":
         return f"({a} / {b})"
     if op == "floor_divide_op":
@@ -387,6 +449,7 @@ class _Plan:
         self.topo = []  # per node, its part of the code key (built during the walk)
         self._visit(root)
         self.vec = vec
+        self.fmad = all(t[0] not in ("un", "bin") or t[1] in _FMAD_SAFE for t in self.topo)
         self._layout()
 
     def _visit(self, node):
@@ -464,7 +527,7 @@ class _Plan:
     def key(self):
         kinds = tuple((k, a._dtype) for k, a in zip(self.kinds, self.inputs))
         return (tuple(self.topo), kinds, self.nd if self.strided else 0, self.idx64, self.vec,
-                bool(get_config().fast_math))
+                bool(get_config().fast_math), self.fmad)
 
 
 # ---------------------------------------------------------------------------
@@ -770,7 +833,7 @@ _cache_lock = threading.Lock()
 _CUDA_INC = None
 
 
-def _options() -> bytes:
+def _options(fmad: bool = False) -> bytes:
     global _CUDA_INC
     if _CUDA_INC is None:
         cands = [os.environ.get("CUDA_HOME", ""), "/usr/local/cuda"]
@@ -778,28 +841,28 @@ def _options() -> bytes:
                           if c and os.path.exists(os.path.join(c, "include", "cuda_fp16.h"))),
                          "/usr/local/cuda/include")
     opts = ["--gpu-architecture=sm_100a", "-std=c++17", f"-I{_CSRC}", f"-I{_CUDA_INC}",
-            "--fmad=false", "-lineinfo", "-default-device"]
+            "--fmad=true" if fmad else "--fmad=false", "-lineinfo", "-default-device"]
     if get_config().fast_math:
         opts.append("--use_fast_math")
     return "\n".join(opts).encode()
 
 
-def compile_kernel(src: str, name: str) -> int:
+def compile_kernel(src: str, name: str, fmad: bool = False) -> int:
     """NVRTC-compile ``src`` and return the handle of kernel ``name``."""
     fn = ctypes.c_void_p()
     log = ctypes.create_string_buffer(1 << 16)
-    rc = _cb.lib.mmp_compile(src.encode(), name.encode(), _options(), ctypes.byref(fn), log, len(log))
+    rc = _cb.lib.mmp_compile(src.encode(), name.encode(), _options(fmad), ctypes.byref(fn), log, len(log))
     if rc != 0:
         msg = _cb.lib.mmp_last_error().decode(errors="replace")
         raise RuntimeError(f"fused kernel compile failed: {msg}\n--- source ---\n{src}")
     return fn.value
 
 
-def _get(key, make_src, name):
+def _get(key, make_src, name, fmad=False):
     with _cache_lock:
         fn = _cache.get(key)
     if fn is None:
-        fn = compile_kernel(make_src(), name)
+        fn = compile_kernel(make_src(), name, fmad)
         with _cache_lock:
             _cache[key] = fn
     return fn
@@ -820,23 +883,142 @@ def _ctype_scalar(v, dt):
     return m(v.item() if hasattr(v, "item") else v)
 
 
-def _loader_args(plan: _Plan) -> list:
-    a = []
-    for k, arr in enumerate(plan.inputs):
-        a.append(ctypes.c_void_p(arr._ptr))
+def _arg_template(plan: _Plan) -> list:
+    """The loader's kernel arguments with the per-call values left as
+    markers -- ("in", k): input k's pointer, ("sc", j, dtype): scalar j --
+    and everything that follows from the layout built once."""
+    t = []
+    for k in range(len(plan.inputs)):
+        t.append(("in", k))
         if plan.kinds[k] in ("sv", "sb", "sg"):
             for s in plan.cstrides[k]:
-                a.append(ctypes.c_longlong(int(s)))
-    for s in plan.scalars:
-        a.append(_ctype_scalar(s._value, s._dtype))
+                t.append(ctypes.c_longlong(int(s)))
+    for j, sc in enumerate(plan.scalars):
+        t.append(("sc", j, sc._dtype))
     if plan.strided:
         for d in plan.cshape:
             m, sh = _fastdiv(int(d))
-            a.append(ctypes.c_longlong(int(d)))
-            a.append(ctypes.c_uint(m))
-            a.append(ctypes.c_uint(sh))
-    a.append(ctypes.c_int(1 if plan.vec_ok else 0))
-    return a
+            t.append(ctypes.c_longlong(int(d)))
+            t.append(ctypes.c_uint(m))
+            t.append(ctypes.c_uint(sh))
+    t.append(ctypes.c_int(1 if plan.vec_ok else 0))
+    return t
+
+
+def _fill(template, inputs, scalars) -> list:
+    out = []
+    for x in template:
+        if x.__class__ is tuple:
+            if x[0] == "in":
+                out.append(ctypes.c_void_p(inputs[x[1]]._ptr))
+            else:
+                out.append(_ctype_scalar(scalars[x[1]]._value, x[2]))
+        else:
+            out.append(x)
+    return out
+
+
+def _loader_args(plan: _Plan) -> list:
+    return _fill(_arg_template(plan), plan.inputs, plan.scalars)
+
+
+# ---------------------------------------------------------------------------
+# launch templates: a repeated expression skips the planner
+# ---------------------------------------------------------------------------
+
+_tmpl: dict = {}
+_TMPL_MAX = 4096
+
+
+def _leaf_key(node, V):
+    """(distinct inputs, distinct scalars, key part) from the node's leaf
+    list: the inputs are deduplicated by view (pointer, shape, strides,
+    dtype) and the scalars by node, in first-occurrence order -- the order
+    the planner assigns their kernel slots -- and the key records which
+    leaf is which slot and each input's layout (what the planner's layout
+    classification reads)."""
+    ins, scal, pat = [], [], []
+    ikeys, sids = {}, {}
+    for lf in node._leaves:
+        if lf.__class__ is InputNode:
+            a = lf._array
+            k = (a._ptr, a._shape, a._strides, a._dtype)
+            slot = ikeys.get(k)
+            if slot is None:
+                slot = ikeys[k] = len(ins)
+                ins.append(a)
+            pat.append(slot)
+        else:
+            slot = sids.get(id(lf))
+            if slot is None:
+                slot = sids[id(lf)] = len(scal)
+                scal.append(lf)
+            pat.append(-1 - slot)
+    lay = tuple((a._shape, a._strides, a._dtype, a._ptr % (V * a._dtype.itemsize) == 0) for a in ins)
+    return ins, scal, (tuple(pat), lay)
+
+
+def _same_slots(plan: _Plan, ins, scal) -> bool:
+    return (len(plan.inputs) == len(ins) and all(p is q for p, q in zip(plan.inputs, ins))
+            and len(plan.scalars) == len(scal) and all(p is q for p, q in zip(plan.scalars, scal)))
+
+
+class _FullReduceLaunch:
+    """A fused full reduction ready to launch again: the kernel, its grid
+    and one argument array whose per-call slots (input pointers, scalar
+    values, output, ddof, scratch) are rewritten under a lock before each
+    launch (the launch copies the values, so the array is free right
+    after)."""
+
+    __slots__ = ("fn", "grid", "n", "args", "ptrs", "dyn", "lock")
+
+    def __init__(self, fn, grid, n, template):
+        self.fn = fn
+        self.grid = (ctypes.c_uint * 3)(int(grid), 1, 1)
+        self.n = n
+        objs, dyn = [], []
+        for x in template:
+            if x.__class__ is tuple:
+                if x[0] == "in":
+                    o = ctypes.c_void_p(0)
+                    dyn.append((o, "in", x[1], None))
+                else:
+                    o = _ctype_scalar(0, x[2])
+                    dyn.append((o, "sc", x[1], np.dtype(x[2])))
+                objs.append(o)
+            else:
+                objs.append(x)
+        self.dyn = dyn
+        tail = [ctypes.c_longlong(n), ctypes.c_void_p(0), ctypes.c_int(0), ctypes.c_double(0.0),
+                ctypes.c_void_p(0), ctypes.c_void_p(0), ctypes.c_void_p(0)]
+        self.args = objs + tail
+        self.ptrs = (ctypes.c_void_p * len(self.args))(*[ctypes.addressof(o) for o in self.args])
+        self.lock = threading.Lock()
+
+    def launch(self, ins, scal, out_ptr, code, ddof, scr, tick, part):
+        with self.lock:
+            for o, kind, slot, dt in self.dyn:
+                if kind == "in":
+                    o.value = ins[slot]._ptr
+                elif dt == np.float16:
+                    o.value = int(np.asarray(scal[slot]._value, np.float16).view(np.uint16))
+                else:
+                    o.value = scal[slot]._value.item()
+            a = self.args
+            a[-6].value = out_ptr
+            a[-5].value = code
+            a[-4].value = ddof
+            a[-3].value = scr
+            a[-2].value = tick
+            a[-1].value = part
+            _cb.check(_cb.lib.mmp_launch(ctypes.c_void_p(self.fn), self.grid, _BLOCK3, 0, self.ptrs),
+                      "fused kernel launch")
+
+
+def _remember(key, value):
+    if len(_tmpl) >= _TMPL_MAX:
+        _tmpl.clear()
+    _tmpl[key] = value
 
 
 def _launch(fn, grid, args, block=_BLOCK):
@@ -889,7 +1071,7 @@ def run_elementwise(node, out_ptr: int, out_shape, out_strides=None) -> None:
     if not out_strided and out_ptr % (V * node._dtype.itemsize) != 0:
         plan.vec_ok = False
     key = ("ew", plan.key(), out_strided, V)
-    fn = _get(key, lambda: _ew_source(plan, out_strided), "mmp_fused_ew")
+    fn = _get(key, lambda: _ew_source(plan, out_strided), "mmp_fused_ew", plan.fmad)
     args = _loader_args(plan) + [ctypes.c_void_p(out_ptr), ctypes.c_longlong(plan.n)]
     if out_strided:
         args += [ctypes.c_longlong(int(s)) for s in out_strides]
@@ -929,40 +1111,48 @@ def run_reduce(node, shape, opc: int, out_ptr: int, out_dt, ddof: float = 0.0,
     """
     T = node._dtype
     V = _RED_V[T.itemsize]
-    plan = _Plan(node, shape, V)
-    be = _cb.CudaBackend()
     code = MMP_CODES[np.dtype(out_dt)]
     if axis_split is None:
-        n = plan.n
-        key = ("red", opc, plan.key())
+        t = tkey = None
+        if node._leaves is not None:
+            ins, scal, lk = _leaf_key(node, V)
+            tkey = ("red", opc, node._sig, lk, tuple(shape), bool(get_config().fast_math))
+            t = _tmpl.get(tkey)
+        if t is None:
+            plan = _Plan(node, shape, V)
+            n = plan.n
+            key = ("red", opc, plan.key())
 
-        def src():
-            return _red_source(plan, opc, "full", 1)
+            def src():
+                return _red_source(plan, opc, "full", 1)
 
-        fn = _get(key, src, "mmp_fused_reduce")
-        per = _BLOCK * V * 4
-        grid = max(1, min((n + per - 1) // per, _resident_blocks(fn)))
-        acc_bytes = 64 * grid
+            fn = _get(key, src, "mmp_fused_reduce", plan.fmad)
+            per = _BLOCK * V * 4
+            grid = max(1, min((n + per - 1) // per, _resident_blocks(fn)))
+            t = _FullReduceLaunch(fn, grid, n, _arg_template(plan))
+            if tkey is not None and _same_slots(plan, ins, scal):
+                _remember(tkey, t)
+            ins, scal = plan.inputs, plan.scalars
+        acc_bytes = 64 * t.grid[0]
         scr = ctypes.c_void_p()
         tick = ctypes.c_void_p()
         _cb.check(_cb.lib.mmp_scratch(acc_bytes + 256, ctypes.byref(scr), ctypes.byref(tick)))
         part_ptr = (scr.value + acc_bytes) if want_partial else 0
-        args = _loader_args(plan) + [ctypes.c_longlong(n), ctypes.c_void_p(out_ptr), ctypes.c_int(code),
-                                     ctypes.c_double(ddof), ctypes.c_void_p(scr.value),
-                                     ctypes.c_void_p(tick.value), ctypes.c_void_p(part_ptr)]
-        _launch(fn, (grid,), args, block=_BLOCK)
+        t.launch(ins, scal, out_ptr, code, float(ddof), scr.value, tick.value, part_ptr)
         if want_partial:
             p = _cb.MmpPartial()
             _cb.check(_cb.lib.mmp_d2h(ctypes.byref(p), ctypes.c_void_p(part_ptr), ctypes.sizeof(p)))
             return p
         return None
+    plan = _Plan(node, shape, V)
+    be = _cb.CudaBackend()
     outer, kk, inner = (int(v) for v in axis_split)
     sms = be.sm_count
     if inner == 1:
         rows = outer
         kind = "rows_block" if (kk >= 2048 or rows < sms * 4) else "rows_warp"
         key = ("red", opc, kind, plan.key())
-        fn = _get(key, lambda: _red_source(plan, opc, kind, 1), "mmp_fused_reduce")
+        fn = _get(key, lambda: _red_source(plan, opc, kind, 1), "mmp_fused_reduce", plan.fmad)
         grid = min(rows, sms * 8) if kind == "rows_block" else min((rows + 7) // 8, sms * 8)
         args = _loader_args(plan) + [ctypes.c_longlong(rows), ctypes.c_longlong(kk), ctypes.c_void_p(out_ptr),
                                      ctypes.c_int(code), ctypes.c_double(ddof)]
@@ -983,7 +1173,7 @@ def run_reduce(node, shape, opc: int, out_ptr: int, out_dt, ddof: float = 0.0,
     tick = ctypes.c_void_p()
     _cb.check(_cb.lib.mmp_scratch(S * outer * inner * 32 + 256, ctypes.byref(scr), ctypes.byref(tick)))
     key = ("red", opc, "cols", cv, plan.key())
-    fn = _get(key, lambda: _red_source(plan, opc, "cols", cv), "mmp_fused_reduce")
+    fn = _get(key, lambda: _red_source(plan, opc, "cols", cv), "mmp_fused_reduce", plan.fmad)
     args = _loader_args(plan) + [ctypes.c_longlong(outer), ctypes.c_longlong(kk), ctypes.c_longlong(inner),
                                  ctypes.c_longlong(kchunk), ctypes.c_void_p(out_ptr), ctypes.c_int(code),
                                  ctypes.c_double(ddof), ctypes.c_void_p(scr.value), ctypes.c_void_p(tick.value)]

@@ -22,7 +22,7 @@ from .ndarray import ndarray
 
 __all__ = [
     "array", "asarray", "asanyarray", "ascontiguousarray", "empty", "empty_like", "zeros", "zeros_like",
-    "ones", "ones_like", "full", "full_like", "arange", "linspace", "asnumpy", "eye", "identity",
+    "ones", "ones_like", "full", "full_like", "arange", "linspace", "asnumpy", "eye", "identity", "copy", "expand_dims",
 ]
 
 
@@ -129,3 +129,27 @@ def eye(N, M=None, k=0, dtype=None) -> ndarray:
 
 def identity(n, dtype=None) -> ndarray:
     return eye(n, dtype=dtype)
+
+
+def copy(a, order="K") -> ndarray:
+    """A device copy of ``a`` (math_ops copy in the reference)."""
+    return asarray(a).copy()
+
+
+def expand_dims(a, axis) -> ndarray:
+    """View of ``a`` with length-1 axes inserted at ``axis`` (an int or a
+    tuple, numpy's normalisation of negative positions)."""
+    a = asarray(a)
+    axes = (axis,) if isinstance(axis, int) else tuple(axis)
+    nd = a.ndim + len(axes)
+    norm = sorted(ax % nd if -nd <= ax < nd else _bad_axis(ax, nd) for ax in axes)
+    if len(set(norm)) != len(norm):
+        raise ValueError("repeated axis")
+    for ax in norm:
+        a = a.expand_dims(ax)
+    return a
+
+
+def _bad_axis(ax, nd):
+    raise np.exceptions.AxisError(ax, nd)
+

@@ -24,6 +24,17 @@
 namespace mmpf {
 using mmpd::isnan_;
 
+// ---- separately rounded + - * of the generated code.  The compiler never
+// contracts these into an fma, whatever --fmad says, so a fused expression
+// rounds every user-level operation as numpy does; expressions whose other
+// ops are all library calls can then be compiled with --fmad=true.
+__device__ __forceinline__ float rn_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double rn_add(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float rn_sub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ double rn_sub(double a, double b) { return __dsub_rn(a, b); }
+__device__ __forceinline__ float rn_mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double rn_mul(double a, double b) { return __dmul_rn(a, b); }
+
 // ---- math dispatch on float / double.  float32 functions whose CUDA
 // error bound is above 2 ulp (tan, sinh, cosh, asinh, acosh, atanh, pow,
 // atan2, hypot) are evaluated in double and rounded once.

@@ -55,8 +55,8 @@ def matmul(x1, x2, out=None, *, mode: str = "auto", **kwargs):
     M, K = a.shape[-2:]
     K2, N = b.shape[-2:]
     if K != K2:
-        raise ValueError(f"matmul: Input operand 1 has a mismatch in its core dimension 0 "
-                         f"(size {K2} is different from {K})")
+        # the reference's message (ndarray.py:1426-1429), which its tests match
+        raise ValueError(f"matmul shape mismatch: ({M},{K}) @ ({K2},{N})")
     batch_shape = broadcast_shapes(a.shape[:-2], b.shape[:-2])
     B = math.prod(batch_shape) if batch_shape else 1
     a = _rowmajor(a)

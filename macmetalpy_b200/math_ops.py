@@ -19,7 +19,7 @@ from .ndarray import ndarray
 __all__ = [
     "sqrt", "exp", "log", "abs", "absolute", "fabs", "power", "negative", "positive", "sign", "square",
     "sin", "cos", "tan", "arcsin", "arccos", "arctan", "sinh", "cosh", "tanh", "log2", "log10",
-    "floor", "ceil", "mod", "remainder", "dot", "where", "clip", "divmod",
+    "floor", "ceil", "mod", "remainder", "dot", "where", "clip", "divmod", "around", "round", "round_",
 ]
 
 
@@ -126,3 +126,38 @@ def clip(a, a_min=None, a_max=None, out=None, **kwargs):
         out[...] = r
         return out
     return r
+
+
+def around(a, decimals=0, out=None):
+    """Round to ``decimals`` places (math_ops.py, numpy's ``around``): for
+    floats ``rint(a * 10**d) / 10**d`` (``a / 10**-d`` then ``* 10**-d`` for
+    negative d), each step in the array's dtype as numpy evaluates it; for
+    integers a copy when d >= 0, else the same steps in float64 and a cast
+    back."""
+    from .creation import asarray
+
+    a = asarray(a)
+    d = int(decimals)
+    if a.dtype.kind in "iub":
+        if d >= 0:
+            r = a.copy()
+        else:
+            f = float(10 ** (-d))  # numpy rounds integers in float64, then casts back
+            r = (ndarray._elementwise("rint_op", a.astype(np.float64) / f) * f).astype(a.dtype)
+    elif d == 0:
+        r = ndarray._elementwise("rint_op", a)
+    elif d > 0:
+        f = float(10 ** d)
+        r = ndarray._elementwise("rint_op", a * f) / f
+    else:
+        f = float(10 ** (-d))
+        r = ndarray._elementwise("rint_op", a / f) * f
+    if out is not None:
+        out[...] = r
+        return out
+    return r
+
+
+round = around
+round_ = around
+

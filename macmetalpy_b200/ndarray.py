@@ -59,6 +59,8 @@ def _c_contiguous_strides(shape) -> Tuple[int, ...]:
 
 from ._config import get_config  # noqa: E402
 
+_CFG = get_config()
+
 _RES_CACHE: dict = {}
 _STRIDES_CACHE: dict = {}
 
@@ -69,7 +71,7 @@ def _operand_spec(x):
     if isinstance(x, ndarray):
         return x._dtype
     if isinstance(x, (bool, np.bool_)) and not isinstance(x, np.generic):
-        return bool
+        return np.dtype(np.bool_)  # a Python bool is not a weak scalar (NEP 50)
     if isinstance(x, np.generic):
         return x.dtype
     if isinstance(x, numbers.Integral):
@@ -83,7 +85,7 @@ def _operand_spec(x):
 
 def _resolve(op_name: str, specs: tuple):
     """(loop_dtype, out_dtype) for an elementwise op after resolve_dtype."""
-    cfg = get_config()
+    cfg = _CFG
     key = (op_name, specs, cfg.float64_behavior, cfg.default_float_dtype)
     r = _RES_CACHE.get(key)
     if r is not None:
@@ -95,6 +97,54 @@ def _resolve(op_name: str, specs: tuple):
     r = (loop, out)
     _RES_CACHE[key] = r
     return r
+
+
+_SCALAR_TYPES = (bool, int, float)
+
+
+def _elementwise_fast(op_name, operands):
+    """The common case of ``ndarray._elementwise`` in one pass, or None.
+
+    Taken when every operand is an ndarray or a Python / numpy scalar, the
+    array operands share one shape, no operand needs a cast to the loop
+    dtype, and no operand graph reaches the depth cap; anything else goes
+    the general way (same result, more checks)."""
+    specs = []
+    shape = None
+    for o in operands:
+        if o.__class__ is ndarray:
+            if shape is None:
+                shape = o._shape
+            elif o._shape != shape:
+                return None
+            specs.append(o._dtype)
+        elif o.__class__ in _SCALAR_TYPES:
+            specs.append(np.dtype(np.bool_) if o.__class__ is bool else o.__class__)
+        elif isinstance(o, np.generic):
+            specs.append(o.dtype)
+        else:
+            return None
+    if shape is None:
+        return None
+    loop, out = _resolve(op_name, tuple(specs))
+    nodes = []
+    for o in operands:
+        if o.__class__ is ndarray:
+            nd = o._fusion_node
+            if nd is None:
+                nd = _fu.InputNode(o)
+            elif nd._depth + 1 > _fu._MAX_DEPTH:
+                return None
+            if nd._dtype != loop:
+                return None
+        else:
+            nd = _fu.ScalarNode(o, loop)
+        nodes.append(nd)
+    if len(nodes) == 1:
+        node = _fu.UnaryOpNode(op_name, nodes[0], shape, out, in_dtype=loop)
+    else:
+        node = _fu.BinaryOpNode(op_name, nodes[0], nodes[1], shape, out, in_dtype=loop)
+    return ndarray._lazy(node)
 
 
 class ndarray:
@@ -324,16 +374,26 @@ class ndarray:
     def item(self, *args):
         return self.get().item(*args)
 
+    # Python scalar conversions: size-1 arrays only, with the reference's
+    # messages (ndarray.py:2464-2495)
+    def _one(self):
+        if self.size != 1:
+            raise TypeError("only size-1 arrays can be converted to Python scalars")
+        return self.get().reshape(-1)[0]
+
     def __float__(self):
-        return float(self.get())
+        return float(self._one())
 
     def __int__(self):
-        return int(self.get())
+        return int(self._one())
+
+    def __complex__(self):
+        return complex(self._one())
 
     def __index__(self):
         if self._dtype.kind not in "iub":
             raise TypeError("only integer arrays can be used as an index")
-        return int(self.get())
+        return int(self._one())
 
     def __bool__(self):
         if self.size != 1:
@@ -573,6 +633,11 @@ class ndarray:
 
     @staticmethod
     def _elementwise(op_name: str, *operands) -> "ndarray":
+        # fast path: every operand an ndarray or a Python / numpy scalar, the
+        # array operands of one shape, no cast and no depth flush needed
+        fast = _elementwise_fast(op_name, operands)
+        if fast is not None:
+            return fast
         ops = []
         specs = []
         shape = None
@@ -623,8 +688,8 @@ class ndarray:
         return ndarray._elementwise(op_name, self)
 
     def _binary_op(self, other, op_name: str) -> "ndarray":
-        if op_name == "pow_op" and not isinstance(other, ndarray) and np.ndim(other) == 0 \
-                and self._dtype.kind == "f":
+        if op_name == "pow_op" and not isinstance(other, ndarray) and self._dtype.kind == "f" \
+                and (isinstance(other, (numbers.Number, np.generic)) or np.ndim(other) == 0):
             e = float(other)
             if e == 2.0:  # numpy's fast scalar power: x**2 is square(x)
                 return ndarray._elementwise("square_op", self)

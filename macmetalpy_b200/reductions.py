@@ -35,7 +35,7 @@ from .ndarray import ndarray
 
 __all__ = [
     "sum", "prod", "mean", "var", "std", "max", "min", "amax", "amin", "argmax", "argmin",
-    "any", "all", "cumsum", "cumprod",
+    "any", "all", "cumsum", "cumprod", "ptp", "diff", "average",
 ]
 
 OPC = {
@@ -321,3 +321,105 @@ def cumsum(a, axis=None, dtype=None, out=None):
 def cumprod(a, axis=None, dtype=None, out=None):
     """Inclusive cumulative product."""
     return _scan(a, 1, axis, dtype, out)
+
+
+# ---------------------------------------------------------------------------
+# range, differences, weighted mean (reductions.py:707-847 in the reference,
+# which hands them to numpy below its size thresholds); here every one is
+# device work built from the reductions and fused elementwise ops above.
+
+
+def ptp(a, axis=None, out=None, keepdims=False):
+    """max - min along ``axis`` (reductions.py:784-803): two device
+    reductions and one fused subtract."""
+    a = _asarray(a)
+    return _finish(max(a, axis=axis, keepdims=keepdims) - min(a, axis=axis, keepdims=keepdims), out)
+
+
+def diff(a, n=1, axis=-1, prepend=np._NoValue, append=np._NoValue):
+    """n-th discrete difference along ``axis`` (reductions.py:707-781):
+    ``a[1:] - a[:-1]`` on strided views, fused, n times; ``prepend`` /
+    ``append`` are broadcast to one slab along ``axis`` and joined on the
+    device first (numpy's rules)."""
+    from .creation import asarray, empty
+
+    a = _asarray(a)
+    if n < 0:
+        raise ValueError(f"order must be non-negative but got {n}")
+    if a.ndim == 0:
+        raise ValueError("diff requires input that is at least one dimensional")
+    ax = axis % a.ndim
+    if prepend is not np._NoValue or append is not np._NoValue:
+        parts = []
+        for extra, first in ((prepend, True), (append, False)):
+            if extra is np._NoValue:
+                continue
+            e = asarray(extra)
+            if e.ndim == 0:  # a scalar becomes a slab of length 1 along axis
+                shp = list(a.shape)
+                shp[ax] = 1
+                e = e.reshape((1,) * a.ndim).broadcast_to(tuple(shp))
+            parts.append((first, e))
+        pre = [e for f, e in parts if f]
+        post = [e for f, e in parts if not f]
+        seq = pre + [a] + post
+        dt = np.result_type(*[x.dtype for x in seq])
+        tot = builtins.sum(x.shape[ax] for x in seq)
+        shp = list(a.shape)
+        shp[ax] = tot
+        joined = empty(tuple(shp), dtype=dt)
+        pos = 0
+        for x in seq:
+            idx = [slice(None)] * a.ndim
+            idx[ax] = slice(pos, pos + x.shape[ax])
+            joined[tuple(idx)] = x
+            pos += x.shape[ax]
+        a = joined
+    hi = [slice(None)] * a.ndim
+    lo = [slice(None)] * a.ndim
+    hi[ax] = slice(1, None)
+    lo[ax] = slice(None, -1)
+    hi, lo = tuple(hi), tuple(lo)
+    for _ in range(n):
+        if a.dtype == np.bool_:
+            a = a[hi] != a[lo]  # numpy: not_equal for booleans
+        else:
+            a = a[hi] - a[lo]
+    return a
+
+
+def average(a, axis=None, weights=None, returned=False, keepdims=False):
+    """Weighted mean (reductions.py:823-846): ``sum(a * w) / sum(w)`` on the
+    device, with 1-D weights laid along ``axis`` as numpy does; without
+    weights, ``mean``.  ``returned`` also gives the sum of the weights."""
+    from .creation import asarray, full
+
+    a = _asarray(a)
+    if weights is None:
+        avg = mean(a, axis=axis, keepdims=keepdims)
+        if returned:
+            cnt = a.size if axis is None else math.prod(
+                a.shape[i] for i in ((axis,) if isinstance(axis, int) else axis))
+            return avg, full(avg.shape, cnt, dtype=avg.dtype)
+        return avg
+    w = asarray(weights)
+    if w.shape != a.shape:
+        if axis is None:
+            raise TypeError("Axis must be specified when shapes of a and weights differ.")
+        if w.ndim != 1:
+            raise TypeError("1D weights expected when shapes of a and weights differ.")
+        ax = axis % a.ndim
+        if w.shape[0] != a.shape[ax]:
+            raise ValueError("Length of weights not compatible with specified axis.")
+        shp = [1] * a.ndim
+        shp[ax] = w.shape[0]
+        w = w.reshape(tuple(shp))
+    rdt = np.result_type(a.dtype, w.dtype, np.float64 if a.dtype.kind in "iub" else a.dtype)
+    rdt = resolve_dtype(rdt)
+    aw = a.astype(rdt) * w.astype(rdt)
+    wfull = w.astype(rdt) if w.shape == a.shape else w.astype(rdt).broadcast_to(a.shape)
+    scl = sum(wfull, axis=axis, keepdims=keepdims)
+    avg = sum(aw, axis=axis, keepdims=keepdims) / scl
+    if returned:
+        return avg, scl
+    return avg
