@@ -191,6 +191,19 @@ class CudaBackend:
         return p.value or 0
 
 
+# Blocks of at most _SMALL bytes (0-d reduction results, scalars, partials)
+# are recycled through a free list instead of a stream-ordered
+# cudaMallocAsync / cudaFreeAsync pair per call (two driver calls that cost
+# more than the small kernel that fills the block).  Reuse is ordered like
+# the pool's own: a block goes back on the list when its last Python owner
+# is gone, and whatever the library enqueues next on the same stream runs
+# after every earlier use of it.  The process drives one device (the
+# backend singleton's), so one list serves.
+_SMALL = 256
+_SMALL_KEEP = 4096
+_small_free: list = []
+
+
 class DeviceBuffer:
     """Owns one device allocation; freed (stream-ordered) when collected."""
 
@@ -200,6 +213,12 @@ class DeviceBuffer:
         if CudaBackend._instance is None:
             CudaBackend()
         self.nbytes = n = int(nbytes)
+        if n <= _SMALL:
+            try:
+                self.ptr = _small_free.pop()
+                return
+            except IndexError:
+                n = _SMALL
         p = ctypes.c_void_p()
         check(lib.mmp_malloc(n if n > 0 else 1, ctypes.byref(p)), "mmp_malloc")
         self.ptr = p.value
@@ -207,11 +226,14 @@ class DeviceBuffer:
     def __del__(self):
         p = getattr(self, "ptr", None)
         if p:
+            self.ptr = None
+            if self.nbytes <= _SMALL and len(_small_free) < _SMALL_KEEP:
+                _small_free.append(p)
+                return
             try:
                 lib.mmp_free(ctypes.c_void_p(p))
             except Exception:
                 pass
-            self.ptr = None
 
 
 class Event:

@@ -201,3 +201,27 @@ def test_one_row_chunked_ragged(cp):
     assert np.max(np.abs(gf - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
     s = rng.choice(np.array([-1, 1], np.int32), n)
     np.testing.assert_array_equal(cp.cumprod(cp.array(s)).get(), np.cumprod(s.astype(np.int64)))
+
+
+# The chunked long-row scan with the smallest chunks (one tile per block per
+# chunk, MMP_SCAN_RANGE=1): every block crosses dozens of chunk boundaries,
+# rows start inside chunks and inside a block's range, and the carry of a
+# 1-D scan enters at tile 0.
+@pytest.mark.parametrize("rows,k", [(1, (1 << 24) + 3 * 4096 + 32), (40, 16 * 4096 + 16), (5, (1 << 22) + 4096)])
+def test_chunked_scan_many_chunks(cp, rows, k, monkeypatch):
+    from macmetalpy_b200 import reductions
+
+    monkeypatch.setenv("MMP_SCAN_RANGE", "1")
+    rng = np.random.default_rng(rows + k)
+    x = rng.integers(-(1 << 31), (1 << 31) - 1, (rows, k), dtype=np.int64).astype(np.int32)
+    got = cp.cumsum(cp.array(x), axis=1)
+    np.testing.assert_array_equal(got.get(), O.cumsum(x, axis=1))
+    xf = rng.standard_normal((rows, k)).astype(np.float32)
+    gf = cp.cumsum(cp.array(xf), axis=1).get()
+    ref = O.cumsum_f64(xf, axis=1)
+    floor = np.finfo(np.float32).eps * np.abs(xf.astype(np.float64)).sum(axis=1, keepdims=True)
+    assert np.max(np.abs(gf - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
+    if rows == 1:
+        c = cp.array(np.array([555], np.int64))
+        g1 = reductions._scan(cp.array(x.reshape(-1)), 0, None, carry_ptr=c._ptr).get()
+        np.testing.assert_array_equal(g1, 555 + np.cumsum(x.reshape(-1), dtype=np.int64))
