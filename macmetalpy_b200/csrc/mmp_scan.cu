@@ -6,7 +6,6 @@
 #include "mmp_scan.cuh"
 
 #include <cstdio>
-#include <cstdlib>
 
 using namespace mmpd;
 
@@ -97,32 +96,6 @@ int stream_blocks_per_sm(int *out) {
   return MMP_OK;
 }
 
-// Resident blocks per SM of scan_chunked_kernel (shared memory raised past
-// the 48 KB default once per device): its cooperative grid is exactly what
-// fits, so every block is resident and the arrival waits always end.
-template <class T, class O, bool PROD>
-int chunked_blocks_per_sm(int *out) {
-  static int per_sm[64];
-  const int dev = current_device();
-  if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
-  if (!per_sm[dev]) {
-    MMP_CUDA_TRY(cudaFuncSetAttribute(scan_chunked_kernel<T, O, PROD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      StreamSmem<T, O>()));
-    int n = 0;
-    MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_chunked_kernel<T, O, PROD>, SBLOCK,
-                                                               StreamSmem<T, O>()));
-    if (n < 1) return set_error(MMP_E_CUDA, "scan_chunked_kernel does not fit on an SM");
-    per_sm[dev] = n;
-  }
-  *out = per_sm[dev];
-  return MMP_OK;
-}
-
-// Input bytes per chunk of the chunked scan: two chunks (the one being
-// scanned again and the next one being summed) stay in the 126 MB L2 next
-// to the output stream, which is written evict-first.
-constexpr long long kChunkBytes = 24ll << 20;
-
 }  // namespace
 
 // Rows of at least kLongRowTiles tiles, in scans of at least
@@ -142,49 +115,10 @@ struct ScanRun {
   typedef typename ScanOut<T>::type O;
   typedef typename ScanTypes<T>::carry_t CT;
 
-  // One cooperative launch of scan_chunked_kernel (aligned long rows).
-  static int chunked(const T *x, O *y, long long rows, long long k, long long tpr, long long total, const CT *cin) {
-    constexpr bool PROD = PRODI != 0;
-    cudaStream_t st = stream();
-    int per_sm = 0;
-    int rc = chunked_blocks_per_sm<T, O, PROD>(&per_sm);
-    if (rc) return rc;
-    int G = sm_count() * per_sm;
-    if ((long long)G > total) G = (int)total;
-    const long long tile_bytes = (long long)STILE * (long long)sizeof(T);
-    long long range = kChunkBytes / (tile_bytes * G);
-    if (const char *env = getenv("MMP_SCAN_RANGE")) range = atoll(env);
-    if (range < 1) range = 1;
-    if (range > CHUNK_MAX_RANGE) range = CHUNK_MAX_RANGE;
-    const long long CTt = (long long)G * range;
-    const long long nch = (total + CTt - 1) / CTt;
-    const size_t sum_bytes = ((size_t)nch * (size_t)G * sizeof(SegTotal<CT>) + 255) & ~(size_t)255;
-    void *state = nullptr;
-    MMP_CUDA_TRY(cudaMallocAsync(&state, sum_bytes + (size_t)nch * sizeof(unsigned), st));
-    SegTotal<CT> *bsum = (SegTotal<CT> *)state;
-    unsigned *cnt = (unsigned *)((char *)state + sum_bytes);
-    cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t)nch * sizeof(unsigned), st);
-    if (e == cudaSuccess) {
-      int rng = (int)range;
-      int *err = device_error_word();
-      void *args[] = {(void *)&x, (void *)&y, (void *)&rows, (void *)&k, (void *)&tpr, (void *)&total,
-                      (void *)&rng, (void *)&bsum, (void *)&cnt, (void *)&cin, (void *)&err};
-      e = cudaLaunchCooperativeKernel((const void *)scan_chunked_kernel<T, O, PROD>, dim3((unsigned)G),
-                                      dim3(SBLOCK), args, (size_t)StreamSmem<T, O>(), st);
-    }
-    rc = e == cudaSuccess ? MMP_OK : cuda_error(e, "scan_chunked_kernel");
-    cudaFreeAsync(state, st);
-    return rc;
-  }
-
   static int long_rows(const T *x, O *y, long long rows, long long k, long long tpr, long long total,
                        const CT *cin, int vec_ok) {
     constexpr bool PROD = PRODI != 0;
     cudaStream_t st = stream();
-    if (vec_ok) {
-      const char *env = getenv("MMP_SCAN_CHUNKED");
-      if (!env || atoi(env) != 0) return chunked(x, y, rows, k, tpr, total, cin);
-    }
     CT *agg = nullptr;
     MMP_CUDA_TRY(cudaMallocAsync((void **)&agg, (size_t)total * 2 * sizeof(CT), st));
     CT *incl = agg + total;

@@ -602,257 +602,6 @@ __global__ void __launch_bounds__(SBLOCK, LookbackMinBlocks<T>::value) scan_carr
   cp_async_wait_all();
 }
 
-// ---------------------------------------------------------------------------
-// Chunked reduce-then-scan: one persistent, cooperative launch for long
-// aligned rows, reading the input from HBM once.
-//
-// Reduce-then-scan in three launches reads the input twice from HBM (16 B
-// moved per int32 -> int64 element instead of 12): a 4 GB input is long gone
-// from the 126 MB L2 when the second pass reads it.  Here the row-major
-// sequence of tiles is cut into chunks of G * range tiles (G = the grid,
-// range = tiles per block per chunk, about 20-30 MB of input per chunk), and
-// every block runs
-//     A(0), A(1), B(0), A(2), B(1), ..., A(n-1), B(n-2), B(n-1)
-// on its own `range` consecutive tiles of each chunk:
-//   A(c): one warp per tile sums the tile (the HBM read; the lines stay in
-//         L2), the block folds its tiles into a segmented range total and
-//         publishes it, then counts itself in chunk c's arrival counter;
-//   B(c): waits until every block has done A(c) -- each did so before its
-//         own A(c+1), so the wait is nearly always already over -- folds the
-//         published totals into its range's exclusive prefix (every block
-//         folds all of them, in one fixed order, into the carry of the next
-//         chunk, so all blocks hold bitwise the same carry), then scans its
-//         tiles again, reading them from L2 with cp.async one tile ahead, and
-//         streams the outputs out.
-// Nothing else waits: no tile waits on a look-back chain.  Rows: a tile that
-// starts a row is a "head"; totals are pairs (value since the last head,
-// whether a head was seen) combined by (a, b) -> (b.h ? b.v : a.v + b.v,
-// a.h | b.h), so one sweep serves one long row or many rows.  A 1-D carry_in
-// is the prefix of tile 0 (which is then no head).  The arrival wait is
-// bounded: when it runs out the device error word is set to 7 and the block
-// carries on (wrong values, no hang).
-
-template <class C>
-struct __align__(16) SegTotal {
-  C v;
-  unsigned long long h;
-};
-
-template <bool PROD, class C>
-__device__ __forceinline__ SegTotal<C> seg_combine(const SegTotal<C> &a, const SegTotal<C> &b) {
-  SegTotal<C> r;
-  r.v = b.h ? b.v : ScanOp<PROD>::op(a.v, b.v);
-  r.h = a.h | b.h;
-  return r;
-}
-
-template <class C>
-__device__ __forceinline__ void seg_store(SegTotal<C> *p, const SegTotal<C> &t) {
-  unsigned long long bits;
-  memcpy(&bits, &t.v, 8);
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(bits), "l"(t.h) : "memory");
-}
-template <class C>
-__device__ __forceinline__ SegTotal<C> seg_load(const SegTotal<C> *p) {
-  unsigned long long bits, h;
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(bits), "=l"(h) : "l"(p) : "memory");
-  SegTotal<C> t;
-  memcpy(&t.v, &bits, 8);
-  t.h = h;
-  return t;
-}
-template <class C>
-__device__ __forceinline__ SegTotal<C> seg_shfl_down(const SegTotal<C> &t, int d) {
-  SegTotal<C> r;
-  r.v = __shfl_down_sync(0xffffffffu, t.v, d);
-  r.h = __shfl_down_sync(0xffffffffu, t.h, d);
-  return r;
-}
-
-constexpr int CHUNK_MAX_RANGE = 16;  // tiles per block per chunk
-
-// Sum (or product) of one tile by one warp, in the carry type, with loads
-// that leave the lines in L2 (the tile is read again from there).  All
-// lanes return the total.
-template <class T, bool PROD>
-__device__ __forceinline__ typename ScanTypes<T>::carry_t warp_tile_total(const T *__restrict__ x, long long start,
-                                                                           long long count) {
-  typedef typename ScanTypes<T>::local_t A;
-  typedef typename ScanTypes<T>::carry_t C;
-  typedef ScanOp<PROD> Op;
-  constexpr int VE = 16 / (int)sizeof(T);
-  constexpr int NVT = STILE / (32 * VE);
-  constexpr int BATCH = 8;
-  static_assert(NVT % BATCH == 0, "whole batches per tile");
-  const int lane = threadIdx.x & 31;
-  C acc = Op::template id<C>();
-  if (count == STILE) {
-    const T *p = x + start + lane * VE;
-#pragma unroll 1
-    for (int q = 0; q < NVT; q += BATCH) {
-      Vec<T, VE> b[BATCH];
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u) {
-        const int4 raw = __ldcg(reinterpret_cast<const int4 *>(p + (long long)(q + u) * 32 * VE));
-        b[u] = *reinterpret_cast<const Vec<T, VE> *>(&raw);
-      }
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u)
-#pragma unroll
-        for (int e = 0; e < VE; ++e) acc = Op::op(acc, (C)to_local<A, T>(b[u].v[e]));
-    }
-  } else {
-    for (long long i = lane; i < count; i += 32) acc = Op::op(acc, (C)to_local<A, T>(x[start + i]));
-  }
-#pragma unroll
-  for (int d = 16; d >= 1; d >>= 1) acc = Op::op(acc, __shfl_xor_sync(0xffffffffu, acc, d));
-  return acc;
-}
-
-// Blocks per SM the chunked kernel is compiled for: as many as its shared
-// memory (two input tiles and the output stage) lets fit, at most 4.
-template <class T, class O>
-struct ChunkMinBlocks {
-  static constexpr int fit = (220 * 1024) / StreamSmem<T, O>();
-  static constexpr int value = fit < 1 ? 1 : (fit > 4 ? 4 : fit);
-};
-
-template <class T, class O, bool PROD>
-__global__ void __launch_bounds__(SBLOCK, (ChunkMinBlocks<T, O>::value)) scan_chunked_kernel(
-    const T *__restrict__ x, O *__restrict__ y, long long rows, long long k, long long tpr, long long total,
-    int range, SegTotal<typename ScanTypes<T>::carry_t> *__restrict__ bsum, unsigned *__restrict__ cnt,
-    const typename ScanTypes<T>::carry_t *carry_in, int *err) {
-  typedef typename ScanTypes<T>::carry_t C;
-  typedef ScanOp<PROD> Op;
-  constexpr int TB = STILE * (int)sizeof(T);
-  __shared__ C s_warp[SBLOCK / 32];
-  __shared__ C s_agg[2][CHUNK_MAX_RANGE];  // tile totals of chunks c (being scanned) and c + 1
-  __shared__ SegTotal<C> s_run;            // exclusive prefix of this block's range
-  __shared__ SegTotal<C> s_carry;          // every chunk before the one being scanned
-  extern __shared__ __align__(128) unsigned char s_mem[];  // StreamSmem<T, O>() bytes
-  unsigned char *s_out = s_mem + 2 * TB;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  const int G = (int)gridDim.x, b = (int)blockIdx.x;
-  const long long CT = (long long)G * range;
-  const long long nch = (total + CT - 1) / CT;
-  const bool use_carry = carry_in != nullptr && rows == 1;
-  SegTotal<C> ident;
-  ident.v = Op::template id<C>();
-  ident.h = 0ull;
-  if (tid == 0) {
-    s_carry.v = use_carry ? (C)(*carry_in) : Op::template id<C>();
-    s_carry.h = use_carry ? 1ull : 0ull;
-  }
-
-#pragma unroll 1
-  for (long long c = -1; c < nch; ++c) {
-    // ---- A(c + 1): sum this block's tiles of the next chunk
-    const long long ca = c + 1;
-    if (ca < nch) {
-      const long long lo = ca * CT + (long long)b * range;
-      long long hi = lo + range;
-      const long long cend = (ca + 1) * CT < total ? (ca + 1) * CT : total;
-      if (hi > cend) hi = cend;
-      const int nt = lo < hi ? (int)(hi - lo) : 0;
-      for (int i = w; i < nt; i += SBLOCK / 32) {
-        const long long t = lo + i;
-        const long long row = t / tpr, j = t - row * tpr;
-        long long count = k - j * STILE;
-        if (count > STILE) count = STILE;
-        const C a = warp_tile_total<T, PROD>(x, row * k + j * STILE, count);
-        if (lane == 0) s_agg[ca & 1][i] = a;
-      }
-      __syncthreads();
-      if (tid == 0) {
-        SegTotal<C> p = ident;
-        for (int i = 0; i < nt; ++i) {
-          const long long t = lo + i;
-          SegTotal<C> q;
-          q.v = s_agg[ca & 1][i];
-          q.h = ((t % tpr) == 0 && !(t == 0 && use_carry)) ? 1ull : 0ull;
-          p = seg_combine<PROD>(p, q);
-        }
-        seg_store(bsum + ca * G + b, p);
-        __threadfence();
-        atomicAdd(cnt + ca, 1u);
-      }
-    }
-    if (c < 0) continue;
-    // ---- B(c): scan this block's tiles of chunk c from their known prefix
-    const long long lo = c * CT + (long long)b * range;
-    long long hi = lo + range;
-    const long long cend = (c + 1) * CT < total ? (c + 1) * CT : total;
-    if (hi > cend) hi = cend;
-    const int nt = lo < hi ? (int)(hi - lo) : 0;
-    stream_issue<T>(s_mem, x, nt > 0 ? lo : -1, k, tpr);  // independent of the prefix: start it now
-    if (tid == 0) {
-      unsigned ns = 32;
-      for (long long it = 0;; ++it) {
-        unsigned got;
-        asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(got) : "l"(cnt + c) : "memory");
-        if (got >= (unsigned)G) break;
-        if (it >= (1ll << 22)) {
-          atomicExch(err, 7);  // chunked scan arrival wait ran out
-          break;
-        }
-        if (it >= 16) {
-          __nanosleep(ns);
-          if (ns < 1024) ns <<= 1;
-        }
-      }
-      __threadfence();
-    }
-    __syncthreads();
-    if (w == 0) {
-      // every block folds all G totals in one fixed order (per-lane runs,
-      // then an ordered tree over lanes): the carry into the next chunk is
-      // bitwise the same in every block; `pre` stops at this block's range
-      const int per = (G + 31) / 32;
-      SegTotal<C> pre = ident, all = ident;
-      const int e0 = lane * per, e1 = (lane + 1) * per < G ? (lane + 1) * per : G;
-      for (int e = e0; e < e1; ++e) {
-        const SegTotal<C> q = seg_load(bsum + c * G + e);
-        all = seg_combine<PROD>(all, q);
-        if (e < b) pre = seg_combine<PROD>(pre, q);
-      }
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const SegTotal<C> op = seg_shfl_down(pre, d), oa = seg_shfl_down(all, d);
-        if ((lane & (2 * d - 1)) == 0) {
-          pre = seg_combine<PROD>(pre, op);
-          all = seg_combine<PROD>(all, oa);
-        }
-      }
-      if (lane == 0) {
-        const SegTotal<C> cr = s_carry;
-        s_run = seg_combine<PROD>(cr, pre);
-        s_carry = seg_combine<PROD>(cr, all);
-      }
-    }
-    __syncthreads();
-    SegTotal<C> run = s_run;
-#pragma unroll 1
-    for (int i = 0; i < nt; ++i) {
-      const long long t = lo + i;
-      stream_issue<T>(s_mem + (int)((i + 1) & 1) * TB, x, i + 1 < nt ? t + 1 : -1, k, tpr);
-      const bool head = (t % tpr) == 0 && !(t == 0 && use_carry);
-      const C excl = head ? Op::template id<C>() : run.v;
-      SegTotal<C> q;
-      q.v = s_agg[c & 1][i];
-      q.h = head ? 1ull : 0ull;
-      run = seg_combine<PROD>(run, q);
-      const long long row = t / tpr, j = t - row * tpr;
-      long long count = k - j * STILE;
-      if (count > STILE) count = STILE;
-      cp_async_wait1();  // tile t has landed (t + 1 may still be in flight)
-      __syncthreads();
-      scan_staged_tile<T, O, PROD>(s_mem + (int)(i & 1) * TB, s_out, s_warp, row * k + j * STILE, count, excl, y);
-    }
-    __syncthreads();  // s_run / s_carry / s_agg[c & 1] reads are done before they are rewritten
-  }
-  cp_async_wait_all();
-}
-
 // One warp per row for short rows (k < STILE / 4).
 template <class T, class O, bool PROD>
 __global__ void __launch_bounds__(SBLOCK) scan_rows_warp_kernel(const T *__restrict__ x,

@@ -203,15 +203,13 @@ def test_one_row_chunked_ragged(cp):
     np.testing.assert_array_equal(cp.cumprod(cp.array(s)).get(), np.cumprod(s.astype(np.int64)))
 
 
-# The chunked long-row scan with the smallest chunks (one tile per block per
-# chunk, MMP_SCAN_RANGE=1): every block crosses dozens of chunk boundaries,
-# rows start inside chunks and inside a block's range, and the carry of a
-# 1-D scan enters at tile 0.
+# Long rows on the reduce-then-scan path: one long row ending in a partial
+# tile with a carry-in, many rows of exactly 16 tiles plus a ragged tail, and
+# a few rows of 2^22 + 4096 elements.
 @pytest.mark.parametrize("rows,k", [(1, (1 << 24) + 3 * 4096 + 32), (40, 16 * 4096 + 16), (5, (1 << 22) + 4096)])
-def test_chunked_scan_many_chunks(cp, rows, k, monkeypatch):
+def test_long_rows_ragged_and_carry(cp, rows, k):
     from macmetalpy_b200 import reductions
 
-    monkeypatch.setenv("MMP_SCAN_RANGE", "1")
     rng = np.random.default_rng(rows + k)
     x = rng.integers(-(1 << 31), (1 << 31) - 1, (rows, k), dtype=np.int64).astype(np.int32)
     got = cp.cumsum(cp.array(x), axis=1)
