@@ -753,6 +753,60 @@ def _time(cp, fn, iters=5, warm=2):
     return s.elapsed_ms(e) / iters
 
 
+def library_gemm_ceiling():
+    """The library GEMM on this box, in this run: torch.matmul (cuBLAS) at
+    the C5 shapes, TFLOP/s of 2MNK, CUDA events on torch's stream after
+    warm-up.  TF32 (allow_tf32: one TF32 pass, about 1e-3 relative error) is
+    the measured ceiling of the tensor pipe in that format, the denominator
+    of the 3xTF32 kernel's issued-MMA fraction; FP32 (allow_tf32 off) is the
+    library's float32-accurate GEMM; float16 the f16 dense rate.  Inputs are
+    made on the device; nothing here is part of the measured product."""
+    try:
+        import torch
+    except Exception as e:  # pragma: no cover
+        return {"unavailable": f"torch: {e}"}
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    def rate(a, b, flops, iters):
+        for _ in range(2):
+            torch.matmul(a, b)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            torch.matmul(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        return round(flops / (s.elapsed_time(e) / iters / 1e3) / 1e12, 2)
+
+    out = {"how": "torch.matmul (cuBLAS), CUDA events; tf32 = allow_tf32 on, fp32 = off"}
+    old = torch.backends.cuda.matmul.allow_tf32
+    try:
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randn(16384, 16384, device=dev, generator=g) / 128
+        b = torch.randn(16384, 16384, device=dev, generator=g) / 128
+        torch.backends.cuda.matmul.allow_tf32 = True
+        out["f32_16384_tf32"] = rate(a, b, 2 * 16384 ** 3, 3)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        out["f32_16384_fp32"] = rate(a, b, 2 * 16384 ** 3, 2)
+        del a, b
+        a = torch.randn(64, 1024, 1024, device=dev, generator=g) / 32
+        b = torch.randn(64, 1024, 1024, device=dev, generator=g) / 32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        out["f32_batched_tf32"] = rate(a, b, 2 * 64 * 1024 ** 3, 5)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        out["f32_batched_fp32"] = rate(a, b, 2 * 64 * 1024 ** 3, 3)
+        del a, b
+        a = (torch.randn(8192, 8192, device=dev, generator=g) / 90.5).half()
+        b = (torch.randn(8192, 8192, device=dev, generator=g) / 90.5).half()
+        out["f16_8192"] = rate(a, b, 2 * 8192 ** 3, 5)
+        del a, b
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_suite(cp, gen):
     """Per-config throughput (device time, CUDA events) for C1, C3, C4, C5."""
     hbm = float(_peaks()[0]["hbm_gbs"])
@@ -811,25 +865,37 @@ def run_suite(cp, gen):
     tf32_nominal = 1100.0
     bf16_meas = float(_peaks()[0].get("bf16_tflops", 0.0)) or None
 
-    def tflops(flops, ms, tf32=False, f16=False):
+    lib = library_gemm_ceiling()
+    out["c5_library_ceiling"] = lib
+
+    def tflops(flops, ms, tf32=False, f16=False, lib_key=None):
         t = flops / (ms / 1e3) / 1e12
         d = {"tflops": round(t, 2), "ms": round(ms, 3)}
         if tf32:
             d["issued_tflops"] = round(3 * t, 2)
             d["issued_frac_of_tf32_nominal"] = round(3 * t / tf32_nominal, 3)
+            ceil = lib.get(lib_key + "_tf32") if lib_key else None
+            if ceil:
+                d["issued_frac_of_measured_library_tf32"] = round(3 * t / ceil, 3)
+            acc = lib.get(lib_key + "_fp32") if lib_key else None
+            if acc:
+                d["speedup_vs_library_fp32"] = round(t / acc, 2)
         if f16 and bf16_meas:
             d["frac_of_measured_dense"] = round(t / bf16_meas, 3)
+        if f16 and lib.get("f16_8192"):
+            d["frac_of_library_f16"] = round(t / lib["f16_8192"], 3)
         return d
 
     Ma = gen.normal((16384, 16384), 41) * np.float32(1 / 128)
     Mb = gen.normal((16384, 16384), 42) * np.float32(1 / 128)
     Ma, Mb = Ma.copy(), Mb.copy()
-    out["c5_f32_16384"] = tflops(2 * 16384 ** 3, _time(cp, lambda: cp.matmul(Ma, Mb), iters=2, warm=1), tf32=True)
+    out["c5_f32_16384"] = tflops(2 * 16384 ** 3, _time(cp, lambda: cp.matmul(Ma, Mb), iters=2, warm=1), tf32=True,
+                                 lib_key="f32_16384")
     del Ma, Mb
     Ba = (gen.normal((64, 1024, 1024), 43) * np.float32(1 / 32)).copy()
     Bb = (gen.normal((64, 1024, 1024), 44) * np.float32(1 / 32)).copy()
     out["c5_f32_batched_64x1024"] = tflops(2 * 64 * 1024 ** 3, _time(cp, lambda: cp.matmul(Ba, Bb), iters=3),
-                                           tf32=True)
+                                           tf32=True, lib_key="f32_batched")
     del Ba, Bb
     Ha = (gen.normal((8192, 8192), 45) * np.float32(1 / 90.5)).astype(np.float16)
     Hb = (gen.normal((8192, 8192), 46) * np.float32(1 / 90.5)).astype(np.float16)
