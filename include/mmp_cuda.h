@@ -112,7 +112,8 @@ int mmp_synchronize(void);
  * set instead of hanging or writing out of bounds: 0 = no error, 2 = scan
  * look-back wait ran out, 3 = GEMM pipeline wait ran out, 4 = sort scatter
  * offset out of range, 5 = gather / scatter / compaction offset out of
- * range, 6 = the self-test wait ran out (mmp_selftest_bounded_wait). */
+ * range, 6 = the self-test wait ran out (mmp_selftest_bounded_wait),
+ * 8 = a peer's flag did not arrive in mmp_reduce_allranks. */
 int mmp_check_device_error(int *code);
 
 /* ---- timing */
@@ -286,6 +287,24 @@ int mmp_allgather(const void *send, void *recv, size_t count, int dtype);
 int mmp_broadcast(const void *send, void *recv, size_t count, int dtype, int root);
 int mmp_group_start(void);
 int mmp_group_end(void);
+/* ---- fused reduce + exchange over peer memory (no NCCL kernel on the
+ * path).  mmp_comm_peer_init (collective, after mmp_comm_init) makes an
+ * exchange block of MMP_XBLOCK_BYTES on every rank and maps every other
+ * rank's block into this process over CUDA IPC; MMP_E_UNSUPPORTED on every
+ * rank when any rank cannot map its peers (keep the NCCL path then).
+ * mmp_reduce_allranks (collective: every rank calls it with the same op and
+ * dtype, in the same order) reduces this rank's x[0..n) and, in the same
+ * launch, stores the partial into every rank's block over NVLink, raises
+ * its flag there, waits for every rank's flag (bounded: 2 s of device time,
+ * then device error 8 and the missing ranks count as empty) and merges the
+ * partials in rank order, exactly as mmp_merge_partials does, into `out`
+ * (one out_dtype element, device memory) on every rank.  index_base is the
+ * shard's first global flat index (argmax / argmin). */
+#define MMP_XBLOCK_BYTES 16384
+int mmp_comm_peer_init(void);
+int mmp_reduce_allranks(int op, int dtype, const void *x, int64_t n, int64_t index_base, int out_dtype,
+                        void *out, double ddof);
+
 /* Wait for this device's stream, giving up after timeout_s seconds (<= 0:
  * the communicator's timeout): then the communicator is aborted and
  * MMP_E_COMM returned, so a lost rank ends in an error, not a hang. */

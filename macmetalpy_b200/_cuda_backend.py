@@ -110,6 +110,8 @@ SIGNATURES = {
     "mmp_group_start": (_int, []),
     "mmp_group_end": (_int, []),
     "mmp_comm_synchronize": (_int, [ctypes.c_double]),
+    "mmp_comm_peer_init": (_int, []),
+    "mmp_reduce_allranks": (_int, [_int, _int, _vp, _i64, _i64, _int, _vp, ctypes.c_double]),
 }
 
 

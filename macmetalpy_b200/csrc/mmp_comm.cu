@@ -70,12 +70,29 @@ struct CommState {
   int rank = -1;
   int nranks = 0;
   double timeout_s = 120.0;
+  // peer exchange (mmp_comm_peer_init): this rank's exchange block and every
+  // rank's, mapped into this process (own one included)
+  void *xblk = nullptr;
+  void *peer[64] = {};
+  bool peer_ok = false;
+  unsigned long long epoch = 0;
 };
 constexpr int kMaxDev = 64;
 CommState g_comm[kMaxDev];
 std::mutex g_comm_mu;
 
+void drop_peers(CommState *c) {
+  if (!c->peer_ok) return;
+  for (int r = 0; r < c->nranks && r < 64; ++r)
+    if (r != c->rank && c->peer[r]) cudaIpcCloseMemHandle(c->peer[r]);
+  if (c->xblk) cudaFree(c->xblk);
+  for (int r = 0; r < 64; ++r) c->peer[r] = nullptr;
+  c->xblk = nullptr;
+  c->peer_ok = false;
+}
+
 void drop(CommState *c, bool abort) {
+  drop_peers(c);
   if (c->comm) (abort ? g_api.CommAbort : g_api.CommDestroy)(c->comm);
   if (c->boot) g_api.CommAbort(c->boot);
   c->comm = nullptr;
@@ -279,6 +296,10 @@ extern "C" int mmp_comm_destroy(void) {
   // the stream's collectives must be done before the communicator goes
   cudaStream_t st = mmp::stream();
   if (st) MMP_CUDA_TRY(cudaStreamSynchronize(st));
+  // every peer's stores into this rank's exchange block happened before this
+  // rank's last exchange saw their flags, so the block can go once the stream
+  // is done
+  drop_peers(c);
   ncclResult_t r = g_api.CommDestroy(c->comm);
   c->comm = nullptr;
   drop(c, true);  // the boot communicator has no work in flight
@@ -382,3 +403,96 @@ extern "C" int mmp_nccl_version(int *version) {
   if (r != ncclSuccess) return nccl_error(r, "ncclGetVersion");
   return MMP_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Peer exchange blocks: the partials of a distributed reduction cross NVLink
+// as plain stores from the reducing kernel into every rank's block (see
+// mmp_reduce_allranks), instead of an NCCL collective and a merge launch.
+// Each rank cudaMallocs MMP_XBLOCK_BYTES, the IPC handles are all-gathered
+// over the communicator, and every rank maps the others' blocks.  Collective:
+// if any rank cannot map a peer, every rank gets MMP_E_UNSUPPORTED and the
+// exchange stays off (callers keep the NCCL path).
+extern "C" int mmp_comm_peer_init(void) {
+  int rc;
+  CommState *c = cur_comm(&rc);
+  if (!c) return rc;
+  if (c->peer_ok) return MMP_OK;
+  if (c->nranks > 64) return mmp::set_error(MMP_E_UNSUPPORTED, "peer exchange supports at most 64 ranks");
+  cudaStream_t st = mmp::stream();
+  void *blk = nullptr;
+  MMP_CUDA_TRY(cudaMalloc(&blk, MMP_XBLOCK_BYTES));
+  cudaError_t e = cudaMemset(blk, 0, MMP_XBLOCK_BYTES);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, blk);
+  char *dev = nullptr;
+  if (e == cudaSuccess) e = cudaMalloc((void **)&dev, sizeof(h) * (size_t)(c->nranks + 1) + 16);
+  if (e != cudaSuccess) {
+    if (dev) cudaFree(dev);
+    cudaFree(blk);
+    return mmp::cuda_error(e, "peer exchange block");
+  }
+  // all-gather the handles on the device
+  char *hosth = new char[sizeof(h) * (size_t)c->nranks];
+  int ok = 1;
+  e = cudaMemcpyAsync(dev, &h, sizeof h, cudaMemcpyHostToDevice, st);
+  ncclResult_t r = ncclSuccess;
+  if (e == cudaSuccess) r = g_api.AllGather(dev, dev + sizeof h, sizeof h, ncclChar, c->comm, st);
+  if (e == cudaSuccess && r == ncclSuccess)
+    e = cudaMemcpyAsync(hosth, dev + sizeof h, sizeof(h) * (size_t)c->nranks, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess && r == ncclSuccess) e = cudaStreamSynchronize(st);
+  void *peer[64] = {};
+  if (e != cudaSuccess || r != ncclSuccess) ok = 0;
+  for (int q = 0; ok && q < c->nranks; ++q) {
+    if (q == c->rank) {
+      peer[q] = blk;
+      continue;
+    }
+    cudaIpcMemHandle_t hq;
+    memcpy(&hq, hosth + sizeof(h) * (size_t)q, sizeof hq);
+    if (cudaIpcOpenMemHandle(&peer[q], hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      peer[q] = nullptr;
+      ok = 0;
+    }
+  }
+  delete[] hosth;
+  // every rank learns whether all of them mapped all peers (MIN of the flags)
+  int *dok = (int *)(dev + sizeof(h) * (size_t)(c->nranks + 1));
+  int all_ok = 0;
+  cudaError_t e2 = cudaMemcpyAsync(dok, &ok, sizeof ok, cudaMemcpyHostToDevice, st);
+  ncclResult_t r2 = ncclSuccess;
+  if (e2 == cudaSuccess) r2 = g_api.AllReduce(dok, dok, 1, ncclInt32, ncclMin, c->comm, st);
+  if (e2 == cudaSuccess && r2 == ncclSuccess) e2 = cudaMemcpyAsync(&all_ok, dok, sizeof all_ok, cudaMemcpyDeviceToHost, st);
+  if (e2 == cudaSuccess && r2 == ncclSuccess) e2 = cudaStreamSynchronize(st);
+  cudaFree(dev);
+  if (e2 != cudaSuccess || r2 != ncclSuccess || !all_ok) {
+    for (int q = 0; q < c->nranks; ++q)
+      if (q != c->rank && peer[q]) cudaIpcCloseMemHandle(peer[q]);
+    cudaFree(blk);
+    if (r2 != ncclSuccess) return nccl_error(r2, "peer exchange agreement");
+    if (e2 != cudaSuccess) return mmp::cuda_error(e2, "peer exchange agreement");
+    return mmp::set_error(MMP_E_UNSUPPORTED, "a rank could not map its peers' exchange blocks");
+  }
+  for (int q = 0; q < c->nranks; ++q) c->peer[q] = peer[q];
+  c->xblk = blk;
+  c->epoch = 0;
+  c->peer_ok = true;
+  return MMP_OK;
+}
+
+namespace mmp {
+// The current device's exchange blocks and the next exchange epoch (every
+// call takes a new one; all ranks make the same sequence of calls).
+bool peer_table(void **blk, int *rank, int *nranks, unsigned long long *epoch) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDev) return false;
+  CommState *c = &g_comm[dev];
+  if (!c->comm || !c->peer_ok) return false;
+  for (int q = 0; q < c->nranks; ++q) blk[q] = c->peer[q];
+  *rank = c->rank;
+  *nranks = c->nranks;
+  *epoch = ++c->epoch;
+  return true;
+}
+}  // namespace mmp
+

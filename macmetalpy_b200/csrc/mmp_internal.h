@@ -25,6 +25,10 @@ int scratch(size_t bytes, void **ptr, unsigned **tickets);
 int *device_error_word();
 // True once mmp_init has set up the current device (no side effects).
 bool is_ready();
+// The current device's peer exchange blocks (blk[0..nranks), this rank's
+// included) and a fresh exchange epoch; false when mmp_comm_peer_init has
+// not set them up.
+bool peer_table(void **blk, int *rank, int *nranks, unsigned long long *epoch);
 
 }  // namespace mmp
 

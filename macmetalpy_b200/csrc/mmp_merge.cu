@@ -106,9 +106,174 @@ __global__ void merge_partials_kernel(const PartialOut *parts, int nparts, void 
   Op::finish(a, n, out, 0, out_dt, ddof, merged);
 }
 
+// ---- fused reduce + exchange (mmp_reduce_allranks).  Exchange block of a
+// rank: slots [2 parities][64 ranks] of 64 bytes (a partial), then flags
+// [2 parities][64 ranks] of 8 bytes (the epoch of the last store).  Calls
+// alternate parities: a rank can only overwrite parity p again after every
+// rank has finished the call before (their flags of the other parity were
+// needed to get there), so a slot is never rewritten while it is read.
+constexpr int XSLOT = 64;
+constexpr int XFLAG_OFF = 2 * 64 * XSLOT;
+static_assert(XFLAG_OFF + 2 * 64 * 8 <= MMP_XBLOCK_BYTES, "exchange block layout");
+
+struct XPeers {
+  unsigned char *blk[64];
+};
+
+__device__ __forceinline__ void st_sys_v2(void *p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_sys_v2(const void *p, unsigned long long &a, unsigned long long &b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const void *p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+template <int OPC, class T>
+__global__ void __launch_bounds__(RBLOCK) reduce_exchange_kernel(ContigLoader<T> ld, long long n,
+                                                                 long long index_base, void *out, int out_dt,
+                                                                 double ddof, void *scratch, unsigned *ticket,
+                                                                 PartialOut *mine, XPeers peers, int rank,
+                                                                 int nranks, unsigned long long epoch, int *err) {
+  // this rank's partial, by the single-GPU reduction (its finishing block
+  // goes on below; every other block returns)
+  if (!reduce_full_body<OPC, T, ContigLoader<T>>(ld, n, (void *)&mine->shift, MMP_DT_FLOAT64, ddof, scratch,
+                                                 ticket, mine))
+    return;
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  __syncwarp();
+  // lane 0 wrote the partial (Op::finish); every lane takes it
+  unsigned long long f[6];
+  if (lane == 0) {
+    PartialOut p = *mine;
+    if ((OPC == MMP_R_ARGMAX || OPC == MMP_R_ARGMIN) && p.index >= 0) p.index += index_base;
+    memcpy(&f[0], &p.s1, 8);
+    memcpy(&f[1], &p.s2, 8);
+    memcpy(&f[2], &p.shift, 8);
+    f[3] = (unsigned long long)p.count;
+    f[4] = (unsigned long long)p.ival;
+    f[5] = (unsigned long long)p.index;
+  }
+#pragma unroll
+  for (int q = 0; q < 6; ++q) f[q] = __shfl_sync(0xffffffffu, f[q], 0);
+  const int par = (int)(epoch & 1ull);
+  const long long slot_off = (long long)(par * 64 + rank) * XSLOT;
+  const long long flag_off = XFLAG_OFF + (long long)(par * 64 + rank) * 8;
+  // ---- the partial into slot [par][rank] of every rank's block, then the flag
+  for (int r = lane; r < nranks; r += 32) {
+    unsigned char *b = peers.blk[r];
+    st_sys_v2(b + slot_off, f[0], f[1]);
+    st_sys_v2(b + slot_off + 16, f[2], f[3]);
+    st_sys_v2(b + slot_off + 32, f[4], f[5]);
+  }
+  __threadfence_system();  // the slots before any flag, on every peer
+  for (int r = lane; r < nranks; r += 32) {
+    unsigned char *b = peers.blk[r];
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(b + flag_off), "l"(epoch) : "memory");
+  }
+  // ---- wait for every rank's flag in this rank's own block (bounded)
+  unsigned char *own = peers.blk[rank];
+  bool missing = false;
+  for (int r = lane; r < nranks; r += 32) {
+    const void *fp = own + XFLAG_OFF + (long long)(par * 64 + r) * 8;
+    const unsigned long long t0 = now_ns();
+    unsigned ns = 32;
+    while (ld_sys_u64(fp) != epoch) {
+      if (now_ns() - t0 > 2000000000ull) {
+        missing = true;
+        break;
+      }
+      __nanosleep(ns);
+      if (ns < 1024) ns <<= 1;
+    }
+  }
+  // each lane saw some ranks' flags: fence after its observations, then the
+  // warp barrier orders them before lane 0 reads every slot
+  __threadfence_system();
+  __syncwarp();
+  if (__any_sync(0xffffffffu, missing) && lane == 0) atomicExch(err, 8);
+  if (lane != 0) return;
+  // ---- merge in rank order, as mmp_merge_partials
+  typedef RedOp<OPC, T> Op;
+  typename Op::Acc a = Op::init();
+  long long cnt = 0;
+  bool seen = false;
+  for (int r = 0; r < nranks; ++r) {
+    const unsigned char *sp = own + (long long)(par * 64 + r) * XSLOT;
+    unsigned long long g[6];
+    ld_sys_v2(sp, g[0], g[1]);
+    ld_sys_v2(sp + 16, g[2], g[3]);
+    ld_sys_v2(sp + 32, g[4], g[5]);
+    if (ld_sys_u64(own + XFLAG_OFF + (long long)(par * 64 + r) * 8) != epoch) continue;  // never arrived
+    PartialOut p;
+    memcpy(&p.s1, &g[0], 8);
+    memcpy(&p.s2, &g[1], 8);
+    memcpy(&p.shift, &g[2], 8);
+    p.count = (long long)g[3];
+    p.ival = (long long)g[4];
+    p.index = (long long)g[5];
+    MergeFold<OPC, T>::fold(a, p, seen);
+    cnt += p.count;
+  }
+  Op::finish(a, cnt, out, 0, out_dt, ddof, nullptr);
+}
+
 }  // namespace mmpd
 
 namespace mmp {
+
+template <int OPC, class T>
+struct XRun {
+  static int run(const void *x, long long n, long long index_base, int out_dt, void *out, double ddof) {
+    if constexpr (!RedSupported<OPC, T>::value) {
+      return set_error(MMP_E_UNSUPPORTED, "nan-reduction of a non-float dtype");
+    } else {
+      void *blk[64];
+      int rank = 0, nranks = 0;
+      unsigned long long epoch = 0;
+      if (!peer_table(blk, &rank, &nranks, &epoch))
+        return set_error(MMP_E_COMM, "no peer exchange on this device: call mmp_comm_peer_init");
+      cudaStream_t st = stream();
+      if (!st) return set_error(MMP_E_CUDA, "no stream");
+      typedef typename RedOp<OPC, T>::Acc Acc;
+      constexpr int V = VW<T>::value;
+      static int occ = 0;
+      if (!occ) {
+        MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reduce_exchange_kernel<OPC, T>, RBLOCK, 0));
+        if (occ < 1) occ = 1;
+      }
+      long long per_block = (long long)RBLOCK * V * 4;
+      long long want = (n + per_block - 1) / per_block;
+      long long maxb = (long long)sm_count() * occ;
+      long long grid = want < 1 ? 1 : (want > maxb ? maxb : want);
+      size_t acc_bytes = ((size_t)grid * sizeof(Acc) + 255) & ~size_t(255);
+      void *scr = nullptr;
+      unsigned *tickets = nullptr;
+      int rc = scratch(acc_bytes + sizeof(PartialOut), &scr, &tickets);
+      if (rc) return rc;
+      PartialOut *mine = (PartialOut *)((char *)scr + acc_bytes);
+      ContigLoader<T> ld;
+      ld.x = (const T *)x;
+      ld.aligned = ((uintptr_t)x % 16) == 0;
+      XPeers xp;
+      for (int q = 0; q < 64; ++q) xp.blk[q] = q < nranks ? (unsigned char *)blk[q] : nullptr;
+      reduce_exchange_kernel<OPC, T><<<(unsigned)grid, RBLOCK, 0, st>>>(ld, n, (long long)index_base, out, out_dt,
+                                                                       ddof, scr, tickets, mine, xp, rank, nranks,
+                                                                       epoch, device_error_word());
+      MMP_LAUNCH_CHECK("reduce_exchange_kernel");
+      return MMP_OK;
+    }
+  }
+};
 
 template <int OPC, class T>
 struct MergeRun {
@@ -138,3 +303,13 @@ extern "C" int mmp_merge_partials(int op, int dtype, const mmp_partial *dev_part
   return mmp::dispatch_op<mmp::MergeRun>(op, dtype, (const PartialOut *)dev_parts, nparts, out_dtype, out, ddof,
                                          (PartialOut *)dev_merged);
 }
+
+extern "C" int mmp_reduce_allranks(int op, int dtype, const void *x, int64_t n, int64_t index_base, int out_dtype,
+                                   void *out, double ddof) {
+  if (n < 0) return mmp::set_error(MMP_E_ARG, "negative element count");
+  if ((n > 0 && !x) || !out) return mmp::set_error(MMP_E_ARG, "null pointer");
+  if (mmp_dtype_size(out_dtype) == 0) return mmp::set_error(MMP_E_ARG, "bad out dtype");
+  if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "call mmp_init first");
+  return mmp::dispatch_op<mmp::XRun>(op, dtype, x, (long long)n, (long long)index_base, out_dtype, out, ddof);
+}
+

@@ -893,7 +893,7 @@ struct HasGroupDeferred<Op, decltype((void)Op::kGroupDeferred)> {
 };
 
 template <int OPC, class T, class L>
-__device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void *out, int out_dt,
+__device__ __forceinline__ bool reduce_full_body(const L &ld, long long n, void *out, int out_dt,
                                                  double ddof, void *scratch, unsigned *ticket,
                                                  PartialOut *part) {
   typedef RedOp<OPC, T> Op;
@@ -960,7 +960,7 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
   acc = block_reduce<Op, RBLOCK>(acc);
   if (gridDim.x == 1) {
     if (threadIdx.x == 0) Op::finish(acc, n, out, 0, out_dt, ddof, part);
-    return;
+    return true;
   }
   __shared__ int is_last;
   if (threadIdx.x == 0) {
@@ -970,7 +970,7 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
     is_last = (t == gridDim.x - 1);
   }
   __syncthreads();
-  if (!is_last) return;
+  if (!is_last) return false;
   __threadfence();
   Acc m = acc0;
   bool first = true;
@@ -985,6 +985,7 @@ __device__ __forceinline__ void reduce_full_body(const L &ld, long long n, void 
     Op::finish(m, n, out, 0, out_dt, ddof, part);
     *ticket = 0u;
   }
+  return true;
 }
 
 template <int OPC, class T, class L>

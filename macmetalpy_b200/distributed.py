@@ -12,12 +12,16 @@ library stream), and every merge runs on the device:
 
 * elementwise / ufuncs: shard-local, no collective;
 * full reductions (sum, mean, var, std, max, min, argmax, argmin, nansum,
-  nanmean, nanvar, nanstd, prod): each shard writes its partial to device
-  memory (``mmp_reduce_partial``), the partials are all-gathered in rank
-  order, and ``mmp_merge_partials`` folds them with the reduction's own
-  arithmetic (var: shifted moments moved to one shift; argmax: numpy's
-  first occurrence, NaN first).  The result is a 0-d device array on every
-  rank; argmax / argmin return a Python int, as the reference does;
+  nanmean, nanvar, nanstd, prod): one launch (``mmp_reduce_allranks``)
+  reduces the shard, stores its partial into every rank's exchange block
+  over NVLink (peer memory mapped at ``init``), waits for every rank's
+  partial and folds them in rank order with the reduction's own arithmetic
+  (var: shifted moments moved to one shift; argmax: numpy's first
+  occurrence, NaN first).  Where peers cannot be mapped, the shard's
+  partial goes to device memory (``mmp_reduce_partial``), an NCCL
+  all-gather collects them and ``mmp_merge_partials`` folds them.  The
+  result is a 0-d device array on every rank; argmax / argmin return a
+  Python int, as the reference does;
 * axis-1 reductions and axis-1 scans: shard-local (rows never span ranks);
 * axis-0 reductions: float64 (or int64) per-column partials ->
   ``mmp_allreduce`` (SUM) -> cast on the device;
@@ -78,8 +82,17 @@ def init(timeout_s: float = 120.0):
     got = exchange_root_bytes(make_id, r, w, timeout_s, nbytes=ID_BYTES, how=how)
     uid = ctypes.create_string_buffer(got, ID_BYTES)
     cb.check(cb.lib.mmp_comm_init(w, r, uid, float(timeout_s)), "mmp_comm_init")
-    _state.update(init=True, rank=r, world=w, timeout=float(timeout_s))
+    _state.update(init=True, rank=r, world=w, timeout=float(timeout_s), peer=False)
     _state["parts"] = cb.DeviceBuffer(PARTIAL_BYTES * (w + 1))
+    # the fused reduce + exchange over peer memory, when every rank can map
+    # every other rank's exchange block (collective; MMP_PEER_EXCHANGE=0
+    # keeps the NCCL all-gather path)
+    if os.environ.get("MMP_PEER_EXCHANGE", "1") != "0":
+        rc = cb.lib.mmp_comm_peer_init()
+        if rc == 0:
+            _state["peer"] = True
+        elif rc != -4:  # MMP_E_UNSUPPORTED: stay on the NCCL path
+            cb.check(rc, "mmp_comm_peer_init")
 
 
 def finalize():
@@ -250,8 +263,20 @@ class DistArray:
         if self.local.size == 0 and world() == 1 and k in reductions._NO_IDENTITY:
             raise ValueError(f"zero-size array to reduction operation {reductions._NO_IDENTITY[k]} "
                              "which has no identity")
+        odt = reductions.out_dtype(k, self.dtype)
+        if _state.get("peer"):
+            # one launch: this shard's reduction, the partials stored into
+            # every rank's exchange block over NVLink, the merge
+            cb = _cb()
+            src = self.local._ensure_contiguous() if self.local.size else self.local
+            res = reductions._scalar_result(np.dtype(odt))
+            cb.check(cb.lib.mmp_reduce_allranks(reductions.OPC[k], cb.dtype_code(src.dtype),
+                                                ctypes.c_void_p(src._ptr if src.size else 0), int(src.size),
+                                                int(self._flat_base()), cb.dtype_code(odt),
+                                                ctypes.c_void_p(res._buffer.ptr), float(ddof)), f"{kind}")
+            return res
         parts = _gathered_partials(self.local, k, self._flat_base())
-        return _merge(k, self.dtype, parts, world(), reductions.out_dtype(k, self.dtype), ddof)
+        return _merge(k, self.dtype, parts, world(), odt, ddof)
 
     def sum(self, axis=None):
         from . import reductions
