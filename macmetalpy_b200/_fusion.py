@@ -180,6 +180,40 @@ class SelectNode(FusionNode):
         self._sig = None if self._leaves is None else ("sel", self._dtype, cond._sig, x._sig, y._sig)
 
 
+def unary_node(op_name, inp, shape, out_dt, loop_dt):
+    """UnaryOpNode from values that are already normalised (np.dtype
+    objects, a shape tuple): the elementwise fast path's constructor."""
+    n = UnaryOpNode.__new__(UnaryOpNode)
+    n._op_name = op_name
+    n._input = inp
+    n._dtype = out_dt
+    n._in_dtype = loop_dt
+    n._shape = shape
+    n._depth = inp._depth + 1
+    lv = inp._leaves
+    n._leaves = lv
+    n._sig = None if lv is None else ("un", op_name, out_dt, loop_dt, inp._sig)
+    return n
+
+
+def binary_node(op_name, lhs, rhs, shape, out_dt, loop_dt):
+    """BinaryOpNode from normalised values (see unary_node)."""
+    n = BinaryOpNode.__new__(BinaryOpNode)
+    n._op_name = op_name
+    n._lhs = lhs
+    n._rhs = rhs
+    n._dtype = out_dt
+    n._in_dtype = loop_dt
+    n._shape = shape
+    dl, dr = lhs._depth, rhs._depth
+    n._depth = (dl if dl > dr else dr) + 1
+    a, b = lhs._leaves, rhs._leaves
+    lv = a + b if (a is not None and b is not None and len(a) + len(b) <= _MAX_LEAVES) else None
+    n._leaves = lv
+    n._sig = None if lv is None else ("bin", op_name, out_dt, loop_dt, lhs._sig, rhs._sig)
+    return n
+
+
 class CastNode(FusionNode):
     __slots__ = ("_input",)
 

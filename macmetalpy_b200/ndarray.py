@@ -141,9 +141,9 @@ def _elementwise_fast(op_name, operands):
             nd = _fu.ScalarNode(o, loop)
         nodes.append(nd)
     if len(nodes) == 1:
-        node = _fu.UnaryOpNode(op_name, nodes[0], shape, out, in_dtype=loop)
+        node = _fu.unary_node(op_name, nodes[0], shape, out, loop)
     else:
-        node = _fu.BinaryOpNode(op_name, nodes[0], nodes[1], shape, out, in_dtype=loop)
+        node = _fu.binary_node(op_name, nodes[0], nodes[1], shape, out, loop)
     return ndarray._lazy(node)
 
 
