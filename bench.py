@@ -619,13 +619,21 @@ def dist_suite(cp, gen):
         ms = s.elapsed_ms(e) / iters
         return D.max_over_ranks(ms)
 
-    out = {"parity": dist_parity(cp)}
+    out = {"parity": dist_parity(cp), "exchange": "peer" if D._state.get("peer") else "nccl"}
     n = 1 << 28
     x = gen.normal((n,), 21 + 100 * R)
     X = D.DistArray.from_local(x, W * n)
     for name, f in (("sum_f32", X.sum), ("var_f32", X.var), ("argmax_f32", X.argmax)):
         ms = timed(f)
         out[f"dist_{name}"] = {"gbs": round(W * 4 * n / ms / 1e6, 1), "ms": round(ms, 4)}
+        if D._state.get("peer"):
+            # the same op through the NCCL all-gather + device-merge path
+            D._state["peer"] = False
+            try:
+                ms2 = timed(f)
+            finally:
+                D._state["peer"] = True
+            out[f"dist_{name}"]["nccl_path_gbs"] = round(W * 4 * n / ms2 / 1e6, 1)
     M = D.DistArray.from_local(x.reshape(16384, 16384), W * 16384)
     ms = timed(lambda: M.sum(axis=0))
     out["dist_sum_axis0_f32"] = {"gbs": round(W * 4 * n / ms / 1e6, 1), "ms": round(ms, 4)}
