@@ -66,3 +66,23 @@ def test_argument_checks_fail_cleanly():
     assert cb.lib.mmp_event_record_on(None, None) == -2
     assert cb.lib.mmp_h2d_async(None, None, 16, None) == -2
     assert cb.lib.mmp_selftest_bounded_wait(0, None) == -2
+
+
+def test_distributed_entry_points_fail_cleanly_without_a_communicator():
+    """The partial / merge / collective entry points reject bad arguments and
+    report a missing communicator with MMP_E_COMM, without a GPU."""
+    from macmetalpy_b200 import _cuda_backend as cb
+    assert cb.lib.mmp_reduce_partial(0, 10, None, -1, 0, ctypes.c_void_p(64)) == -2
+    assert cb.lib.mmp_reduce_partial(0, 10, ctypes.c_void_p(64), 4, 0, None) == -2
+    assert cb.lib.mmp_merge_partials(0, 10, None, -1, 11, ctypes.c_void_p(64), 0.0, None) == -2
+    assert cb.lib.mmp_merge_partials(0, 10, ctypes.c_void_p(64), 2, 99, ctypes.c_void_p(64), 0.0, None) == -2
+    assert cb.lib.mmp_reduce_allranks(0, 10, None, -1, 0, 11, ctypes.c_void_p(64), 0.0) == -2
+    assert cb.lib.mmp_comm_init(0, 0, None, 1.0) == -2
+    assert cb.lib.mmp_comm_init(2, 2, ctypes.c_void_p(64), 1.0) == -2
+    assert cb.lib.mmp_comm_unique_id(None) == -2
+    # no communicator (and, here, no device): a clean error code, no crash
+    for rc in (cb.lib.mmp_allreduce(ctypes.c_void_p(64), ctypes.c_void_p(64), 1, 10, 0),
+               cb.lib.mmp_allgather(ctypes.c_void_p(64), ctypes.c_void_p(64), 1, 10),
+               cb.lib.mmp_broadcast(ctypes.c_void_p(64), ctypes.c_void_p(64), 1, 10, 0),
+               cb.lib.mmp_comm_peer_init(), cb.lib.mmp_comm_synchronize(0.1)):
+        assert rc in (-2, -6), rc
