@@ -113,7 +113,8 @@ int mmp_synchronize(void);
  * look-back wait ran out, 3 = GEMM pipeline wait ran out, 4 = sort scatter
  * offset out of range, 5 = gather / scatter / compaction offset out of
  * range, 6 = the self-test wait ran out (mmp_selftest_bounded_wait),
- * 8 = a peer's flag did not arrive in mmp_reduce_allranks. */
+ * 8 = a peer's flag did not arrive in mmp_reduce_allranks or
+ * mmp_scan_allranks. */
 int mmp_check_device_error(int *code);
 
 /* ---- timing */
@@ -304,6 +305,17 @@ int mmp_group_end(void);
 int mmp_comm_peer_init(void);
 int mmp_reduce_allranks(int op, int dtype, const void *x, int64_t n, int64_t index_base, int out_dtype,
                         void *out, double ddof);
+/* Inclusive scan (op MMP_S_SUM / MMP_S_PROD) of a 1-D array block-
+ * distributed over the ranks in rank order: this rank's shard x[0..n) into
+ * y[0..n), with the combined totals of the lower ranks' shards as the carry
+ * (the global cumsum / cumprod, reductions.py:661-705, of the concatenated
+ * shards).  Collective over the peer exchange like mmp_reduce_allranks, and
+ * with its bounded wait.  A long aligned shard (n >= 2^24, x and y 16-byte
+ * aligned, n a multiple of 16) exchanges its total from the scan's own tile
+ * aggregates between its launches, so the shard's data is read twice and
+ * written once as in mmp_scan; any other shard reduces and exchanges first.
+ * Shards may be empty (n = 0: x and y unused, the call still takes part). */
+int mmp_scan_allranks(int op, int dtype, const void *x, int out_dtype, void *y, int64_t n);
 
 /* Wait for this device's stream, giving up after timeout_s seconds (<= 0:
  * the communicator's timeout): then the communicator is aborted and

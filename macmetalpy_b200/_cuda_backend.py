@@ -112,6 +112,7 @@ SIGNATURES = {
     "mmp_comm_synchronize": (_int, [ctypes.c_double]),
     "mmp_comm_peer_init": (_int, []),
     "mmp_reduce_allranks": (_int, [_int, _int, _vp, _i64, _i64, _int, _vp, ctypes.c_double]),
+    "mmp_scan_allranks": (_int, [_int, _int, _vp, _int, _vp, _i64]),
 }
 
 

@@ -29,6 +29,12 @@ bool is_ready();
 // included) and a fresh exchange epoch; false when mmp_comm_peer_init has
 // not set them up.
 bool peer_table(void **blk, int *rank, int *nranks, unsigned long long *epoch);
+// Collective: the carry of a distributed scan (the lower ranks' combined
+// shard totals, carry type: float64 / int64 / uint64) into device memory,
+// from the shard's tile aggregates when `agg` is given, else from a full
+// reduction of x[0..n) (mmp_merge.cu).
+int scan_carry_allranks(int prod, int dtype, const void *agg, long long ntiles, const void *x, long long n,
+                        void *carry_out);
 
 }  // namespace mmp
 

@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include "mmp_dispatch.h"
+#include "mmp_scan.cuh"
 
 using namespace mmpd;
 
@@ -137,25 +138,20 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
+// The exchange and merge, run by one full warp of one block.  `p` (valid in
+// lane 0) is this rank's partial; it goes into slot [par][rank] of every
+// rank's block, then the epoch into flag [par][rank]; the warp waits for
+// every rank's flag in its own block (bounded: 2 s, then device error 8 and
+// the missing ranks count as empty) and lane 0 folds the partials of ranks
+// 0 .. upto-1 in rank order and finishes into out (out_dt) -- upto = nranks
+// for a reduction, rank for the carry of a scan.
 template <int OPC, class T>
-__global__ void __launch_bounds__(RBLOCK) reduce_exchange_kernel(ContigLoader<T> ld, long long n,
-                                                                 long long index_base, void *out, int out_dt,
-                                                                 double ddof, void *scratch, unsigned *ticket,
-                                                                 PartialOut *mine, XPeers peers, int rank,
-                                                                 int nranks, unsigned long long epoch, int *err) {
-  // this rank's partial, by the single-GPU reduction (its finishing block
-  // goes on below; every other block returns)
-  if (!reduce_full_body<OPC, T, ContigLoader<T>>(ld, n, (void *)&mine->shift, MMP_DT_FLOAT64, ddof, scratch,
-                                                 ticket, mine))
-    return;
-  if (threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
-  __syncwarp();
-  // lane 0 wrote the partial (Op::finish); every lane takes it
+__device__ __forceinline__ void exchange_merge_warp(const PartialOut &p, const XPeers &peers, int rank, int nranks,
+                                                    int upto, unsigned long long epoch, void *out, int out_dt,
+                                                    double ddof, int *err) {
+  const int lane = threadIdx.x & 31;
   unsigned long long f[6];
   if (lane == 0) {
-    PartialOut p = *mine;
-    if ((OPC == MMP_R_ARGMAX || OPC == MMP_R_ARGMIN) && p.index >= 0) p.index += index_base;
     memcpy(&f[0], &p.s1, 8);
     memcpy(&f[1], &p.s2, 8);
     memcpy(&f[2], &p.shift, 8);
@@ -207,24 +203,82 @@ __global__ void __launch_bounds__(RBLOCK) reduce_exchange_kernel(ContigLoader<T>
   typename Op::Acc a = Op::init();
   long long cnt = 0;
   bool seen = false;
-  for (int r = 0; r < nranks; ++r) {
+  for (int r = 0; r < upto; ++r) {
     const unsigned char *sp = own + (long long)(par * 64 + r) * XSLOT;
     unsigned long long g[6];
     ld_sys_v2(sp, g[0], g[1]);
     ld_sys_v2(sp + 16, g[2], g[3]);
     ld_sys_v2(sp + 32, g[4], g[5]);
     if (ld_sys_u64(own + XFLAG_OFF + (long long)(par * 64 + r) * 8) != epoch) continue;  // never arrived
-    PartialOut p;
-    memcpy(&p.s1, &g[0], 8);
-    memcpy(&p.s2, &g[1], 8);
-    memcpy(&p.shift, &g[2], 8);
-    p.count = (long long)g[3];
-    p.ival = (long long)g[4];
-    p.index = (long long)g[5];
-    MergeFold<OPC, T>::fold(a, p, seen);
-    cnt += p.count;
+    PartialOut q;
+    memcpy(&q.s1, &g[0], 8);
+    memcpy(&q.s2, &g[1], 8);
+    memcpy(&q.shift, &g[2], 8);
+    q.count = (long long)g[3];
+    q.ival = (long long)g[4];
+    q.index = (long long)g[5];
+    MergeFold<OPC, T>::fold(a, q, seen);
+    cnt += q.count;
   }
   Op::finish(a, cnt, out, 0, out_dt, ddof, nullptr);
+}
+
+template <int OPC, class T>
+__global__ void __launch_bounds__(RBLOCK) reduce_exchange_kernel(ContigLoader<T> ld, long long n,
+                                                                 long long index_base, void *out, int out_dt,
+                                                                 double ddof, void *scratch, unsigned *ticket,
+                                                                 PartialOut *mine, XPeers peers, int rank,
+                                                                 int nranks, int upto, unsigned long long epoch,
+                                                                 int *err) {
+  // this rank's partial, by the single-GPU reduction (its finishing block
+  // goes on below; every other block returns)
+  if (!reduce_full_body<OPC, T, ContigLoader<T>>(ld, n, (void *)&mine->shift, MMP_DT_FLOAT64, ddof, scratch,
+                                                 ticket, mine))
+    return;
+  if (threadIdx.x >= 32) return;
+  __syncwarp();
+  PartialOut p;
+  if (threadIdx.x == 0) {  // lane 0 wrote the partial (Op::finish)
+    p = *mine;
+    if ((OPC == MMP_R_ARGMAX || OPC == MMP_R_ARGMIN) && p.index >= 0) p.index += index_base;
+  }
+  exchange_merge_warp<OPC, T>(p, peers, rank, nranks, upto, epoch, out, out_dt, ddof, err);
+}
+
+// The carry of a distributed scan from the shard's tile aggregates (the
+// first launch of the long-row scan): one block sums (multiplies) the
+// aggregates in the carry type, then its first warp exchanges the shard
+// total and folds the lower ranks' totals into carry_out.
+template <class T, bool PROD>
+__global__ void __launch_bounds__(RBLOCK) scan_total_exchange_kernel(const typename ScanTypes<T>::carry_t *agg,
+                                                                     long long ntiles, void *carry_out,
+                                                                     int carry_dt, XPeers peers, int rank,
+                                                                     int nranks, unsigned long long epoch,
+                                                                     int *err) {
+  typedef typename ScanTypes<T>::carry_t C;
+  typedef ScanOp<PROD> SOp;
+  __shared__ C s_part[RBLOCK / 32];
+  C a = SOp::template id<C>();
+  for (long long i = threadIdx.x; i < ntiles; i += RBLOCK) a = SOp::op(a, agg[i]);
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) a = SOp::op(a, __shfl_xor_sync(0xffffffffu, a, d));
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = a;
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  PartialOut p;
+  if (threadIdx.x == 0) {
+    C t = s_part[0];
+#pragma unroll
+    for (int w = 1; w < RBLOCK / 32; ++w) t = SOp::op(t, s_part[w]);  // fixed order
+    p.s1 = (double)t;
+    p.s2 = 0.0;
+    p.shift = 0.0;
+    p.ival = (long long)t;
+    p.count = ntiles;
+    p.index = -1;
+  }
+  exchange_merge_warp<PROD ? MMP_R_PROD : MMP_R_SUM, T>(p, peers, rank, nranks, rank, epoch, carry_out, carry_dt,
+                                                       0.0, err);
 }
 
 }  // namespace mmpd
@@ -233,7 +287,9 @@ namespace mmp {
 
 template <int OPC, class T>
 struct XRun {
-  static int run(const void *x, long long n, long long index_base, int out_dt, void *out, double ddof) {
+  // upto < 0: merge every rank (a reduction); otherwise the ranks below
+  // this one (the carry of a scan)
+  static int run(const void *x, long long n, long long index_base, int out_dt, void *out, double ddof, int upto) {
     if constexpr (!RedSupported<OPC, T>::value) {
       return set_error(MMP_E_UNSUPPORTED, "nan-reduction of a non-float dtype");
     } else {
@@ -268,7 +324,8 @@ struct XRun {
       for (int q = 0; q < 64; ++q) xp.blk[q] = q < nranks ? (unsigned char *)blk[q] : nullptr;
       reduce_exchange_kernel<OPC, T><<<(unsigned)grid, RBLOCK, 0, st>>>(ld, n, (long long)index_base, out, out_dt,
                                                                        ddof, scr, tickets, mine, xp, rank, nranks,
-                                                                       epoch, device_error_word());
+                                                                       upto < 0 ? nranks : rank, epoch,
+                                                                       device_error_word());
       MMP_LAUNCH_CHECK("reduce_exchange_kernel");
       return MMP_OK;
     }
@@ -310,6 +367,49 @@ extern "C" int mmp_reduce_allranks(int op, int dtype, const void *x, int64_t n, 
   if ((n > 0 && !x) || !out) return mmp::set_error(MMP_E_ARG, "null pointer");
   if (mmp_dtype_size(out_dtype) == 0) return mmp::set_error(MMP_E_ARG, "bad out dtype");
   if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "call mmp_init first");
-  return mmp::dispatch_op<mmp::XRun>(op, dtype, x, (long long)n, (long long)index_base, out_dtype, out, ddof);
+  return mmp::dispatch_op<mmp::XRun>(op, dtype, x, (long long)n, (long long)index_base, out_dtype, out, ddof, -1);
 }
+
+namespace mmp {
+
+template <int PRODI, class T>
+struct ScanCarryRun {
+  static int run(const void *agg, long long ntiles, void *carry_out) {
+    typedef typename ScanTypes<T>::carry_t C;
+    void *blk[64];
+    int rank = 0, nranks = 0;
+    unsigned long long epoch = 0;
+    if (!peer_table(blk, &rank, &nranks, &epoch))
+      return set_error(MMP_E_COMM, "no peer exchange on this device: call mmp_comm_peer_init");
+    XPeers xp;
+    for (int q = 0; q < 64; ++q) xp.blk[q] = q < nranks ? (unsigned char *)blk[q] : nullptr;
+    const int cdt = IsFloatT<C>::value ? MMP_FLOAT64 : (IsSigned<C>::value ? MMP_INT64 : MMP_UINT64);
+    scan_total_exchange_kernel<T, PRODI != 0><<<1, RBLOCK, 0, stream()>>>((const C *)agg, ntiles, carry_out, cdt, xp,
+                                                                        rank, nranks, epoch, device_error_word());
+    MMP_LAUNCH_CHECK("scan_total_exchange_kernel");
+    return MMP_OK;
+  }
+};
+
+// The carry of a distributed scan (the combination of the lower ranks'
+// shard totals), by the exchange: from the shard's tile aggregates (`agg`,
+// ntiles values of the carry type) when given, else from a full reduction
+// of x[0..n).  One exchange epoch either way, so ranks whose shards take
+// different paths still meet.
+int scan_carry_allranks(int prod, int dtype, const void *agg, long long ntiles, const void *x, long long n,
+                        void *carry_out) {
+  if (agg) {
+    if (prod) return dispatch_dtype<ScanCarryRun, 1>(dtype, agg, ntiles, carry_out);
+    return dispatch_dtype<ScanCarryRun, 0>(dtype, agg, ntiles, carry_out);
+  }
+  int cdt;
+  switch (dtype) {
+    case MMP_FLOAT16: case MMP_FLOAT32: case MMP_FLOAT64: cdt = MMP_FLOAT64; break;
+    case MMP_UINT16: case MMP_UINT32: case MMP_UINT64: cdt = MMP_UINT64; break;
+    default: cdt = MMP_INT64;
+  }
+  return dispatch_op<XRun>(prod ? MMP_R_PROD : MMP_R_SUM, dtype, x, n, 0ll, cdt, carry_out, 0.0, 0);
+}
+
+}  // namespace mmp
 

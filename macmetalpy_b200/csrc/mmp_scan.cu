@@ -115,12 +115,16 @@ struct ScanRun {
   typedef typename ScanOut<T>::type O;
   typedef typename ScanTypes<T>::carry_t CT;
 
+  // exch_dtype >= 0 (one row, the shard of a distributed scan of that
+  // input dtype): the carry is the lower ranks' combined totals, exchanged
+  // over peer memory from this shard's tile aggregates between the first
+  // launch and the aggregate scan (cin is ignored).
   static int long_rows(const T *x, O *y, long long rows, long long k, long long tpr, long long total,
-                       const CT *cin, int vec_ok) {
+                       const CT *cin, int vec_ok, int exch_dtype = -1) {
     constexpr bool PROD = PRODI != 0;
     cudaStream_t st = stream();
     CT *agg = nullptr;
-    MMP_CUDA_TRY(cudaMallocAsync((void **)&agg, (size_t)total * 2 * sizeof(CT), st));
+    MMP_CUDA_TRY(cudaMallocAsync((void **)&agg, ((size_t)total * 2 + 1) * sizeof(CT), st));
     CT *incl = agg + total;
     long long blocks = (total * 32 + SBLOCK - 1) / SBLOCK;
     const long long maxb = (long long)sm_count() * 8;
@@ -128,6 +132,11 @@ struct ScanRun {
         x, k, tpr, total, agg, vec_ok);
     cudaError_t e = cudaGetLastError();
     int rc = e == cudaSuccess ? MMP_OK : cuda_error(e, "tile_aggregates_kernel");
+    if (exch_dtype >= 0) {
+      CT *carry = agg + 2 * total;
+      if (!rc) rc = scan_carry_allranks(PRODI, exch_dtype, agg, total, nullptr, 0, carry);
+      cin = carry;
+    }
     // the aggregates are scanned per row by this same library (CT is its
     // own accumulation type), with the caller's carry
     if (!rc) rc = ScanRun<PRODI, CT>::run(agg, ScanOut<CT>::code, incl, rows, tpr, 1, cin);
@@ -153,6 +162,26 @@ struct ScanRun {
       }
     }
     cudaFreeAsync(agg, st);
+    return rc;
+  }
+
+  // A 1-D shard of a distributed scan (collective over the peer exchange).
+  static int allranks(int dtype, const void *xv, int out_dt, void *yv, long long n) {
+    if (out_dt != ScanOut<T>::code)
+      return set_error(MMP_E_ARG, "scan output dtype must be the numpy accumulation type");
+    cudaStream_t st = stream();
+    if (!st) return set_error(MMP_E_CUDA, "no stream");
+    const long long tpr = (n + STILE - 1) / STILE;
+    if (tpr > 0x7fffffffll) return set_error(MMP_E_ARG, "scan too large");
+    const int vec_ok = ((uintptr_t)xv % 16 == 0) && ((uintptr_t)yv % 16 == 0) && (n % 16 == 0);
+    if (vec_ok && tpr >= kLongRowTiles && n >= kLongRowElements)
+      return long_rows((const T *)xv, (O *)yv, 1, n, tpr, tpr, nullptr, vec_ok, dtype);
+    // otherwise: the carry by a full reduce + exchange, then the local scan
+    CT *carry = nullptr;
+    MMP_CUDA_TRY(cudaMallocAsync((void **)&carry, sizeof(CT), st));
+    int rc = scan_carry_allranks(PRODI, dtype, nullptr, 0, xv, n, carry);
+    if (!rc && n > 0) rc = run(xv, out_dt, yv, 1, n, 1, carry);
+    cudaFreeAsync(carry, st);
     return rc;
   }
 
@@ -217,6 +246,26 @@ extern "C" int mmp_scan(int op, int dtype, const void *x, int out_dtype, void *y
                                                                   (long long)k, (long long)inner, carry_in);
   if (op == MMP_S_PROD) return mmp::dispatch_dtype<mmp::ScanRun, 1>(dtype, x, out_dtype, y, (long long)outer,
                                                                    (long long)k, (long long)inner, carry_in);
+  return mmp::set_error(MMP_E_ARG, "unsupported scan op");
+}
+
+namespace mmp {
+
+template <int PRODI, class T>
+struct ScanAllRun {
+  static int run(int dtype, const void *x, int out_dt, void *y, long long n) {
+    return ScanRun<PRODI, T>::allranks(dtype, x, out_dt, y, n);
+  }
+};
+
+}  // namespace mmp
+
+extern "C" int mmp_scan_allranks(int op, int dtype, const void *x, int out_dtype, void *y, int64_t n) {
+  if (n < 0) return mmp::set_error(MMP_E_ARG, "negative element count");
+  if (n > 0 && (!x || !y)) return mmp::set_error(MMP_E_ARG, "null pointer");
+  if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "call mmp_init first");
+  if (op == MMP_S_SUM) return mmp::dispatch_dtype<mmp::ScanAllRun, 0>(dtype, dtype, x, out_dtype, y, (long long)n);
+  if (op == MMP_S_PROD) return mmp::dispatch_dtype<mmp::ScanAllRun, 1>(dtype, dtype, x, out_dtype, y, (long long)n);
   return mmp::set_error(MMP_E_ARG, "unsupported scan op");
 }
 

@@ -339,14 +339,25 @@ class DistArray:
         if len(self.global_shape) != 1 and axis is not None:
             raise NotImplementedError("distributed cumsum: 1-D, axis=1 of 2-D, or axis=None")
         local = self.local.reshape(-1) if len(self.global_shape) != 1 else self.local
-        kind = self.dtype.kind
-        carry_dt = np.float64 if kind == "f" else (np.uint64 if kind == "u" else np.int64)
-        parts = _gathered_partials(local, "sum", 0)
-        carry = _merge("sum", self.dtype, parts, rank(), carry_dt)  # lower ranks' total
-        if local.size:
-            res = reductions._scan(local, 0, None, carry_ptr=carry._buffer.ptr)
+        if _state.get("peer"):
+            # one collective call: the lower ranks' totals cross NVLink as peer
+            # stores between the scan's own launches
+            local = local._ensure_contiguous()
+            odt = reductions.scan_out_dtype(self.dtype)
+            res = ndarray._empty(local.shape, odt)
+            cb = _cb()
+            cb.check(cb.lib.mmp_scan_allranks(0, cb.dtype_code(self.dtype), ctypes.c_void_p(local._ptr),
+                                              cb.dtype_code(odt), ctypes.c_void_p(res._ptr), int(local.size)),
+                     "distributed cumsum")
         else:
-            res = ndarray._empty((0,), reductions.scan_out_dtype(self.dtype))
+            kind = self.dtype.kind
+            carry_dt = np.float64 if kind == "f" else (np.uint64 if kind == "u" else np.int64)
+            parts = _gathered_partials(local, "sum", 0)
+            carry = _merge("sum", self.dtype, parts, rank(), carry_dt)  # lower ranks' total
+            if local.size:
+                res = reductions._scan(local, 0, None, carry_ptr=carry._buffer.ptr)
+            else:
+                res = ndarray._empty((0,), reductions.scan_out_dtype(self.dtype))
         if len(self.global_shape) != 1:  # axis=None of an N-d array: flat result
             n = int(np.prod(self.global_shape))
             return DistArray(res, (n,), self._flat_base(), self._flat_base() + int(local.size))

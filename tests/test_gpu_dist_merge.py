@@ -9,7 +9,10 @@
 * the zero-part merge (the carry of rank 0);
 * a one-rank communicator through the C ABI (``distributed.init`` with
   WORLD_SIZE=1): DistArray reductions, cumsum with its device carry and
-  gather, all on the library stream.
+  gather, all on the library stream; with the peer exchange up,
+  ``mmp_scan_allranks`` on both of its paths (a long aligned shard that
+  exchanges its total from the tile aggregates, a ragged one that reduces
+  first), cumprod through the C ABI and an empty shard.
 
 Multi-rank runs are in test_gpu_distributed.py (two GPUs)."""
 
@@ -107,6 +110,37 @@ def test_zero_part_merge_is_identity():
     assert int(out.get()[0]) == 0
 
 
+def _scan_allranks_one_rank(rng):
+    import macmetalpy_b200 as cp
+    from macmetalpy_b200 import _cuda_backend as cb
+    from macmetalpy_b200 import distributed as D
+
+    # long aligned shard: the aggregate-total exchange between the launches
+    n = (1 << 24) + 4096
+    x = (rng.standard_normal(n) + 0.25).astype(np.float32)
+    got = D.DistArray.from_global(x).cumsum().gather()
+    ref = O.cumsum_f64(x)
+    assert np.max(np.abs(got.astype(np.float64) - ref)) <= 1e-6 * np.abs(x).astype(np.float64).sum()
+    xi = rng.integers(-7, 8, n).astype(np.int32)
+    np.testing.assert_array_equal(D.DistArray.from_global(xi).cumsum().gather(), np.cumsum(xi, dtype=np.int64))
+    # ragged and unaligned shards: reduce + exchange, then the local scan
+    for m in (1, 15, 4097, (1 << 20) + 3):
+        xu = rng.integers(0, 1000, m).astype(np.uint16)
+        np.testing.assert_array_equal(D.DistArray.from_global(xu).cumsum().gather(),
+                                      np.cumsum(xu, dtype=np.uint64))
+    # cumprod through the C ABI (no DistArray method): int64 exact
+    xp = rng.choice(np.array([-1, 1, 1, 2], dtype=np.int64), 5000)
+    X = cp.array(xp)
+    Y = cp.empty((5000,), dtype=np.int64)
+    cb.check(cb.lib.mmp_scan_allranks(1, cb.dtype_code(np.int64), ctypes.c_void_p(X._ptr),
+                                      cb.dtype_code(np.int64), ctypes.c_void_p(Y._ptr), 5000), "cumprod")
+    np.testing.assert_array_equal(Y.get(), np.cumprod(xp))
+    # an empty shard still takes part
+    cb.check(cb.lib.mmp_scan_allranks(0, cb.dtype_code(np.float32), None, cb.dtype_code(np.float32), None, 0),
+             "empty")
+    cb.check(cb.lib.mmp_synchronize(), "sync")
+
+
 def test_one_rank_communicator(monkeypatch):
     import socket
 
@@ -132,6 +166,8 @@ def test_one_rank_communicator(monkeypatch):
         XI = D.DistArray.from_global(xi)
         assert int(XI.sum()) == int(xi.sum(dtype=np.int64))
         np.testing.assert_array_equal(XI.cumsum().gather(), np.cumsum(xi, dtype=np.int64))
+        if D._state.get("peer"):
+            _scan_allranks_one_rank(rng)
         m = rng.standard_normal((257, 129)).astype(np.float32)
         M = D.DistArray.from_global(m)
         s0 = M.sum(axis=0).get()

@@ -1,9 +1,11 @@
-"""Block-distributed arrays on 2 GPUs over the library's own NCCL
-collectives (C ABI), against the oracle on the whole array: sum / mean /
-var / argmax / argmin / max / nansum / nanmean (device partials, all-gather,
+"""Block-distributed arrays on 2 GPUs over the library's own collectives
+(C ABI), against the oracle on the whole array: sum / mean / var / argmax /
+argmin / max / nansum / nanmean (the fused reduce + peer exchange when the
+ranks can map each other's memory, else device partials, all-gather and
 device merge), 1-D cumsum with device carries (int32 exact, float32 within
-1e-4), axis-0 sums (all-reduce), axis-1 reductions and scans (shard-local),
-matmul with B broadcast from rank 0.  Needs two visible GPUs; skipped
+1e-4; long aligned shards and shards on different scan paths through
+mmp_scan_allranks), axis-0 sums (all-reduce), axis-1 reductions and scans
+(shard-local), matmul with B broadcast from rank 0.  Needs two visible GPUs; skipped
 otherwise.  Ranks are child processes with a short communicator timeout;
 NVLS is off (plain NCCL rings), as this test only checks results."""
 
@@ -33,6 +35,32 @@ def _port():
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def _long_and_mixed_scans(D, rank):
+    """mmp_scan_allranks with long aligned shards on both ranks (each
+    exchanges its total from its tile aggregates), then with rank 0 on that
+    path and rank 1 on the reduce-first path, and the other way round."""
+    import ctypes
+
+    from macmetalpy_b200 import _cuda_backend as cb
+    from macmetalpy_b200.creation import array, empty
+
+    rng = np.random.default_rng(99)
+    n = 2 * ((1 << 24) + 16)
+    x = (rng.standard_normal(n) + 0.25).astype(np.float32)
+    got = D.DistArray.from_global(x).cumsum().gather()
+    ref = O.cumsum_f64(x)
+    assert np.max(np.abs(got.astype(np.float64) - ref)) <= 1e-6 * np.abs(x).astype(np.float64).sum()
+    for sizes in (((1 << 24) + 16, 1001), (1001, (1 << 24) + 16)):
+        xs = [rng.integers(-9, 10, s).astype(np.int32) for s in sizes]
+        X = array(xs[rank])
+        Y = empty((sizes[rank],), dtype=np.int64)
+        cb.check(cb.lib.mmp_scan_allranks(0, cb.dtype_code(np.int32), ctypes.c_void_p(X._ptr),
+                                          cb.dtype_code(np.int64), ctypes.c_void_p(Y._ptr), sizes[rank]), "scan")
+        want = np.cumsum(np.concatenate(xs), dtype=np.int64)
+        lo = sum(sizes[:rank])
+        np.testing.assert_array_equal(Y.get(), want[lo:lo + sizes[rank]])
 
 
 def _rank_main(rank, world, port, q):
@@ -70,6 +98,8 @@ def _rank_main(rank, world, port, q):
         got = D.DistArray.from_global(xf).cumsum().gather()
         ref = O.cumsum_f64(xf)
         assert np.max(np.abs(got - ref) / ref) <= 1e-4
+        if D._state.get("peer"):
+            _long_and_mixed_scans(D, rank)
         m = rng.standard_normal((1001, 515)).astype(np.float32)
         M = D.DistArray.from_global(m)
         s1 = M.sum(axis=1).gather()
