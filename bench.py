@@ -642,6 +642,14 @@ def dist_suite(cp, gen):
     XI = D.DistArray.from_local(xi, W * n)
     ms = timed(lambda: XI.cumsum())
     out["dist_cumsum_i32"] = {"gbs": round(W * 12 * n / ms / 1e6, 1), "ms": round(ms, 4)}
+    if D._state.get("peer"):
+        # the carry through the NCCL all-gather + device merge, then the scan
+        D._state["peer"] = False
+        try:
+            ms2 = timed(lambda: XI.cumsum())
+        finally:
+            D._state["peer"] = True
+        out["dist_cumsum_i32"]["nccl_path_gbs"] = round(W * 12 * n / ms2 / 1e6, 1)
     del XI, xi
     m = 16384
     s0, e0 = D.row_partition(m, W)[R]

@@ -76,24 +76,27 @@ int set_stage_smem() {
   return MMP_OK;
 }
 
-// Resident blocks per SM of scan_carry_stream_kernel (its shared memory
-// raised past the 48 KB default once per device), for its persistent grid.
-template <class T, class O, bool PROD>
-int stream_blocks_per_sm(int *out) {
-  static int per_sm[64];
+// Resident blocks per SM of a persistent streaming scan kernel (its shared
+// memory raised past the 48 KB default once per device), for its grid.
+template <class K>
+int persistent_blocks_per_sm(K kernel, int smem, int *per_sm, const char *name, int *out) {
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return set_error(MMP_E_ARG, "device out of range");
   if (!per_sm[dev]) {
-    MMP_CUDA_TRY(cudaFuncSetAttribute(scan_carry_stream_kernel<T, O, PROD>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, StreamSmem<T, O>()));
+    MMP_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int n = 0;
-    MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_carry_stream_kernel<T, O, PROD>, SBLOCK,
-                                                               StreamSmem<T, O>()));
-    if (n < 1) return set_error(MMP_E_CUDA, "scan_carry_stream_kernel does not fit on an SM");
+    MMP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, SBLOCK, smem));
+    if (n < 1) return set_error(MMP_E_CUDA, name);
     per_sm[dev] = n;
   }
   *out = per_sm[dev];
   return MMP_OK;
+}
+template <class T, class O, bool PROD>
+int stream_blocks_per_sm(int *out) {
+  static int per_sm[64];
+  return persistent_blocks_per_sm(scan_carry_stream_kernel<T, O, PROD>, StreamSmem<T, O>(), per_sm,
+                                  "scan_carry_stream_kernel does not fit on an SM", out);
 }
 
 }  // namespace

@@ -1,7 +1,7 @@
 """cumsum / cumprod vs the oracle: int32 -> int64 bit-exact across tile
 boundaries (4096-element tiles), float32 within 1e-4 of the float64 scan,
 row (axis=-1) and column (axis=0) scans, the look-back kernel and the
-reduce-then-scan path for long rows, carry-in."""
+reduce-then-scan path for long rows, carry-in, back-to-back long scans."""
 
 import numpy as np
 import pytest
@@ -89,7 +89,7 @@ def test_repeated_calls_reuse_state(cp):
     cp.synchronize()
 
 
-# Rows of at least 64 tiles in scans of at least 2^24 elements take the
+# Rows of at least 16 tiles in scans of at least 2^24 elements take the
 # reduce-then-scan path (tile aggregates, a scan of the aggregates, tile
 # scans with known carries).  Full-range int32 keeps the int64 carries exact;
 # odd k takes the unaligned (scalar) tile path; a ragged last tile per row.
@@ -223,3 +223,29 @@ def test_long_rows_ragged_and_carry(cp, rows, k):
         c = cp.array(np.array([555], np.int64))
         g1 = reductions._scan(cp.array(x.reshape(-1)), 0, None, carry_ptr=c._ptr).get()
         np.testing.assert_array_equal(g1, 555 + np.cumsum(x.reshape(-1), dtype=np.int64))
+
+
+def test_long_scans_back_to_back(cp):
+    """Consecutive long scans of different lengths and types on one stream,
+    read back only at the end: the per-launch aggregate buffers and the
+    look-back state of the aggregate scans do not leak between launches."""
+    rng = np.random.default_rng(5)
+    outs = []
+    for n in ((1 << 24), (1 << 24) + 4096 * 37 + 16, (1 << 25) - 16, (1 << 24)):
+        x = rng.integers(-50, 51, n).astype(np.int32)
+        outs.append((cp.cumsum(cp.array(x)), x))
+        xf = rng.uniform(-1, 1, n).astype(np.float32)
+        outs.append((cp.cumsum(cp.array(xf)), xf))
+    for got, x in outs:
+        if x.dtype == np.int32:
+            np.testing.assert_array_equal(got.get(), np.cumsum(x, dtype=np.int64))
+        else:
+            ref = O.cumsum_f64(x)
+            floor = np.finfo(np.float32).eps * np.abs(x.astype(np.float64)).sum()
+            assert np.max(np.abs(got.get() - ref) / np.maximum(np.abs(ref), floor)) <= 1e-4
+    import ctypes
+
+    from macmetalpy_b200 import _cuda_backend as cb
+
+    code = ctypes.c_int(-1)
+    assert cb.lib.mmp_check_device_error(ctypes.byref(code)) == 0 and code.value == 0
