@@ -150,6 +150,15 @@ int mmp_compile(const char *source, const char *name, const char *options,
                 void **func, char *log, size_t log_size);
 int mmp_launch(void *func, const unsigned grid[3], const unsigned block[3],
                unsigned shared_bytes, void **args);
+/* mmp_launch of a kernel that takes this library's per-device scratch (as
+ * mmp_scratch returns it) in two of its arguments: takes a region of at
+ * least scratch_bytes, writes its address into the void * that
+ * args[scr_slot] points to and the ticket array's into args[tick_slot]'s,
+ * then launches -- one call where mmp_scratch + mmp_launch take two.  The
+ * slots must index `args`. */
+int mmp_launch_scratch(void *func, const unsigned grid[3], const unsigned block[3],
+                       unsigned shared_bytes, void **args, size_t scratch_bytes,
+                       int scr_slot, int tick_slot);
 /* Blocks of `block_threads` threads that fit on one SM at once (grid sizing
  * for the compiled function; runFunction picks its own in the reference). */
 int mmp_occupancy(void *func, int block_threads, unsigned shared_bytes, int *blocks_per_sm);

@@ -74,6 +74,8 @@ SIGNATURES = {
                            ctypes.c_char_p, _sz]),
     "mmp_launch": (_int, [_vp, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint),
                           ctypes.c_uint, ctypes.POINTER(_vp)]),
+    "mmp_launch_scratch": (_int, [_vp, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint), ctypes.c_uint,
+                                   ctypes.POINTER(_vp), ctypes.c_size_t, _int, _int]),
     "mmp_occupancy": (_int, [_vp, _int, ctypes.c_uint, ctypes.POINTER(_int)]),
     "mmp_reduce": (_int, [_int, _int, _vp, _i64, _int, _vp, ctypes.c_double,
                           ctypes.POINTER(MmpPartial)]),

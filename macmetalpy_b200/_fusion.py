@@ -33,6 +33,8 @@ import numpy as np
 
 from . import _cuda_backend as _cb
 from ._config import get_config
+
+_CFG = get_config()
 from ._dtypes import CUDA_TYPE_NAMES, MMP_CODES
 
 __all__ = [
@@ -1004,11 +1006,12 @@ class _FullReduceLaunch:
     launch (the launch copies the values, so the array is free right
     after)."""
 
-    __slots__ = ("fn", "grid", "n", "args", "ptrs", "dyn", "lock")
+    __slots__ = ("fn", "grid", "n", "args", "ptrs", "dyn", "lock", "acc_bytes", "nargs")
 
     def __init__(self, fn, grid, n, template):
-        self.fn = fn
+        self.fn = ctypes.c_void_p(fn)
         self.grid = (ctypes.c_uint * 3)(int(grid), 1, 1)
+        self.acc_bytes = 64 * int(grid)
         self.n = n
         objs, dyn = [], []
         for x in template:
@@ -1026,10 +1029,13 @@ class _FullReduceLaunch:
         tail = [ctypes.c_longlong(n), ctypes.c_void_p(0), ctypes.c_int(0), ctypes.c_double(0.0),
                 ctypes.c_void_p(0), ctypes.c_void_p(0), ctypes.c_void_p(0)]
         self.args = objs + tail
+        self.nargs = len(self.args)
         self.ptrs = (ctypes.c_void_p * len(self.args))(*[ctypes.addressof(o) for o in self.args])
         self.lock = threading.Lock()
 
-    def launch(self, ins, scal, out_ptr, code, ddof, scr, tick, part):
+    def launch(self, ins, scal, out_ptr, code, ddof, scr=None, tick=None, part=0):
+        """Launch; with scr None the library fills in its scratch region in
+        the same call (mmp_launch_scratch)."""
         with self.lock:
             for o, kind, slot, dt in self.dyn:
                 if kind == "in":
@@ -1042,11 +1048,17 @@ class _FullReduceLaunch:
             a[-6].value = out_ptr
             a[-5].value = code
             a[-4].value = ddof
-            a[-3].value = scr
-            a[-2].value = tick
             a[-1].value = part
-            _cb.check(_cb.lib.mmp_launch(ctypes.c_void_p(self.fn), self.grid, _BLOCK3, 0, self.ptrs),
-                      "fused kernel launch")
+            if scr is None:
+                n = self.nargs
+                rc = _cb.lib.mmp_launch_scratch(self.fn, self.grid, _BLOCK3, 0, self.ptrs, self.acc_bytes + 256,
+                                                n - 3, n - 2)
+            else:
+                a[-3].value = scr
+                a[-2].value = tick
+                rc = _cb.lib.mmp_launch(self.fn, self.grid, _BLOCK3, 0, self.ptrs)
+            if rc:
+                _cb.check(rc, "fused kernel launch")
 
 
 def _remember(key, value):
@@ -1145,12 +1157,13 @@ def run_reduce(node, shape, opc: int, out_ptr: int, out_dt, ddof: float = 0.0,
     """
     T = node._dtype
     V = _RED_V[T.itemsize]
-    code = MMP_CODES[np.dtype(out_dt)]
+    code = MMP_CODES[out_dt if isinstance(out_dt, np.dtype) else np.dtype(out_dt)]
     if axis_split is None:
         t = tkey = None
         if node._leaves is not None:
             ins, scal, lk = _leaf_key(node, V)
-            tkey = ("red", opc, node._sig, lk, tuple(shape), bool(get_config().fast_math))
+            tkey = ("red", opc, node._sig, lk, shape if shape.__class__ is tuple else tuple(shape),
+                    bool(_CFG.fast_math))
             t = _tmpl.get(tkey)
         if t is None:
             plan = _Plan(node, shape, V)
@@ -1167,17 +1180,18 @@ def run_reduce(node, shape, opc: int, out_ptr: int, out_dt, ddof: float = 0.0,
             if tkey is not None and _same_slots(plan, ins, scal):
                 _remember(tkey, t)
             ins, scal = plan.inputs, plan.scalars
-        acc_bytes = 64 * t.grid[0]
+        if not want_partial:
+            t.launch(ins, scal, out_ptr, code, float(ddof))
+            return None
+        acc_bytes = t.acc_bytes
         scr = ctypes.c_void_p()
         tick = ctypes.c_void_p()
         _cb.check(_cb.lib.mmp_scratch(acc_bytes + 256, ctypes.byref(scr), ctypes.byref(tick)))
-        part_ptr = (scr.value + acc_bytes) if want_partial else 0
+        part_ptr = scr.value + acc_bytes
         t.launch(ins, scal, out_ptr, code, float(ddof), scr.value, tick.value, part_ptr)
-        if want_partial:
-            p = _cb.MmpPartial()
-            _cb.check(_cb.lib.mmp_d2h(ctypes.byref(p), ctypes.c_void_p(part_ptr), ctypes.sizeof(p)))
-            return p
-        return None
+        p = _cb.MmpPartial()
+        _cb.check(_cb.lib.mmp_d2h(ctypes.byref(p), ctypes.c_void_p(part_ptr), ctypes.sizeof(p)))
+        return p
     plan = _Plan(node, shape, V)
     be = _cb.CudaBackend()
     outer, kk, inner = (int(v) for v in axis_split)

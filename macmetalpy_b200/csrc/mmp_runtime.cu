@@ -561,6 +561,19 @@ int mmp_launch(void *func, const unsigned grid[3], const unsigned block[3],
   return MMP_OK;
 }
 
+int mmp_launch_scratch(void *func, const unsigned grid[3], const unsigned block[3], unsigned shared_bytes,
+                       void **args, size_t scratch_bytes, int scr_slot, int tick_slot) {
+  if (!args || scr_slot < 0 || tick_slot < 0 || !args[scr_slot] || !args[tick_slot])
+    return set_error(MMP_E_ARG, "bad argument to mmp_launch_scratch");
+  void *scr = nullptr;
+  unsigned *tick = nullptr;
+  int rc = mmp::scratch(scratch_bytes, &scr, &tick);
+  if (rc) return rc;
+  *(void **)args[scr_slot] = scr;
+  *(void **)args[tick_slot] = (void *)tick;
+  return mmp_launch(func, grid, block, shared_bytes, args);
+}
+
 int mmp_occupancy(void *func, int block_threads, unsigned shared_bytes, int *blocks_per_sm) {
   if (!func || !blocks_per_sm || block_threads <= 0) return set_error(MMP_E_ARG, "bad argument to mmp_occupancy");
   int rc = ensure_ready();

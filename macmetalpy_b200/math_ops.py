@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .ndarray import ndarray
+from .ndarray import _elementwise_fast, ndarray
 
 __all__ = [
     "sqrt", "exp", "log", "abs", "absolute", "fabs", "power", "negative", "positive", "sign", "square",
@@ -25,7 +25,9 @@ __all__ = [
 
 def _u(op):
     def f(x, out=None, **kwargs):
-        r = ndarray._elementwise(op, x)
+        r = _elementwise_fast(op, (x,))
+        if r is None:
+            r = ndarray._elementwise(op, x)
         if out is not None:
             out[...] = r
             return out

@@ -109,6 +109,19 @@ def _elementwise_fast(op_name, operands):
     array operands share one shape, no operand needs a cast to the loop
     dtype, and no operand graph reaches the depth cap; anything else goes
     the general way (same result, more checks)."""
+    if len(operands) == 1:  # unary on an array: no lists
+        o = operands[0]
+        if o.__class__ is not ndarray:
+            return None
+        loop, out = _resolve(op_name, (o._dtype,))
+        nd = o._fusion_node
+        if nd is None:
+            nd = _fu.InputNode(o)
+        elif nd._depth >= _fu._MAX_DEPTH:
+            return None
+        if nd._dtype != loop:
+            return None
+        return ndarray._lazy(_fu.unary_node(op_name, nd, o._shape, out, loop))
     specs = []
     shape = None
     for o in operands:
@@ -176,6 +189,19 @@ class ndarray:
         n = math.prod(shape) if shape else 1
         buf = _cb.DeviceBuffer(max(n * dtype.itemsize, 1))
         return cls(buf, shape, dtype)
+
+    @classmethod
+    def _empty0(cls, dtype) -> "ndarray":
+        """A new 0-d array of ``dtype`` (an np.dtype), uninitialised."""
+        a = cls.__new__(cls)
+        a._buffer = _cb.DeviceBuffer(dtype.itemsize)
+        a._shape = ()
+        a._dtype = dtype
+        a._strides = ()
+        a._offset = 0
+        a._base = None
+        a._fusion_node = None
+        return a
 
     @classmethod
     def _lazy(cls, node) -> "ndarray":
@@ -685,15 +711,18 @@ class ndarray:
         return ndarray._lazy(node)
 
     def _unary_op(self, op_name: str) -> "ndarray":
-        return ndarray._elementwise(op_name, self)
+        r = _elementwise_fast(op_name, (self,))
+        return r if r is not None else ndarray._elementwise(op_name, self)
 
     def _binary_op(self, other, op_name: str) -> "ndarray":
-        if op_name == "pow_op" and not isinstance(other, ndarray) and self._dtype.kind == "f" \
-                and (isinstance(other, (numbers.Number, np.generic)) or np.ndim(other) == 0):
+        if op_name == "pow_op" and other.__class__ is not ndarray and self._dtype.kind == "f" \
+                and (other.__class__ in _SCALAR_TYPES or isinstance(other, (numbers.Number, np.generic))
+                     or np.ndim(other) == 0):
             e = float(other)
             if e == 2.0:  # numpy's fast scalar power: x**2 is square(x)
-                return ndarray._elementwise("square_op", self)
-        return ndarray._elementwise(op_name, self, other)
+                return self._unary_op("square_op")
+        r = _elementwise_fast(op_name, (self, other))
+        return r if r is not None else ndarray._elementwise(op_name, self, other)
 
     def _rbinary_op(self, other, op_name: str) -> "ndarray":
         return ndarray._elementwise(op_name, other, self)
@@ -846,7 +875,12 @@ class ndarray:
     def __ipow__(self, o): return self._inplace(o, "pow_op")
 
     def __matmul__(self, other):
+        """``a @ b`` for 1-D and 2-D operands; like the reference's operator
+        (ndarray.py:1398-1450) it raises ValueError above 2-D, where
+        ``matmul()`` broadcasts batches."""
         from . import linalg_top
+        if self.ndim > 2 or (other.ndim if other.__class__ is ndarray else np.ndim(other)) > 2:
+            raise ValueError("matmul requires 1-D or 2-D arrays")
         return linalg_top.matmul(self, other)
 
     def __rmatmul__(self, other):

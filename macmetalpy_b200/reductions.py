@@ -53,7 +53,10 @@ _NP_FN = {
 _NO_IDENTITY = {"max": "maximum", "min": "minimum", "argmax": "argmax", "argmin": "argmin",
                 "nanmax": "fmax", "nanmin": "fmin"}
 
+from ._config import get_config  # noqa: E402
+
 _dt_cache: dict = {}
+_CFG = get_config()
 
 
 def _asarray(a) -> ndarray:
@@ -65,10 +68,7 @@ def _asarray(a) -> ndarray:
 
 def out_dtype(kind: str, dt) -> np.dtype:
     """numpy's result dtype of reduction ``kind`` on ``dt``, resolved."""
-    from ._config import get_config
-
-    cfg = get_config()
-    key = (kind, np.dtype(dt), cfg.float64_behavior)
+    key = (kind, dt if isinstance(dt, np.dtype) else np.dtype(dt), _CFG.float64_behavior)
     r = _dt_cache.get(key)
     if r is None:
         if kind in ("argmax", "argmin"):
@@ -97,11 +97,21 @@ def _norm_axes(axis, ndim):
 
 
 def _scalar_result(dt) -> ndarray:
-    return ndarray._empty((), dt)
+    return ndarray._empty0(np.dtype(dt))
 
 
 def _reduce(a, kind: str, axis=None, keepdims=False, ddof=0.0, dtype=None, out=None, partial=False,
             out_dt=None):
+    # the common case first: a lazy expression reduced to one value
+    if (axis is None and a.__class__ is ndarray and a._fusion_node is not None and dtype is None
+            and not keepdims and not partial and out_dt is None):
+        dt = a._dtype
+        k = kind if (dt.kind == "f" or not kind.startswith("nan")) else kind[3:]
+        if k not in _NO_IDENTITY or a.size:
+            odt = _dt_cache.get((k, dt, _CFG.float64_behavior)) or out_dtype(k, dt)
+            res = ndarray._empty0(odt)
+            _fu.run_reduce(a._fusion_node, a._shape, OPC[k], res._buffer.ptr, odt, ddof)
+            return res if out is None else _finish(res, out)
     a = _asarray(a)
     if dtype is not None:
         a = a.astype(resolve_dtype(dtype), copy=False)
