@@ -598,15 +598,16 @@ def dist_suite(cp, gen):
     global array is world x that.  Matmul is strong-scaled: A (16384,16384)
     row-sharded, B broadcast from rank 0; the broadcast alone and the local
     GEMM alone are timed too.  Device time (events on the library stream,
-    where the collectives also run), max over ranks; values count every
-    rank's bytes / FLOPs.  ``parity``: see dist_parity."""
+    where the collectives also run) over 10 back-to-back calls after a
+    barrier (the ranks' start skew is paid once), max over ranks; values
+    count every rank's bytes / FLOPs.  ``parity``: see dist_parity."""
     from macmetalpy_b200 import distributed as D
     from macmetalpy_b200 import linalg_top
     from macmetalpy_b200._cuda_backend import Event
 
     W, R = D.world(), D.rank()
 
-    def timed(fn, iters=3, warm=2):
+    def timed(fn, iters=10, warm=2):
         for _ in range(warm):
             fn()
         D.barrier()

@@ -113,8 +113,8 @@ int mmp_synchronize(void);
  * look-back wait ran out, 3 = GEMM pipeline wait ran out, 4 = sort scatter
  * offset out of range, 5 = gather / scatter / compaction offset out of
  * range, 6 = the self-test wait ran out (mmp_selftest_bounded_wait),
- * 8 = a peer's flag did not arrive in mmp_reduce_allranks or
- * mmp_scan_allranks. */
+ * 8 = a peer's flag did not arrive in mmp_reduce_allranks,
+ * mmp_scan_allranks or mmp_allreduce_sum_peer. */
 int mmp_check_device_error(int *code);
 
 /* ---- timing */
@@ -310,7 +310,8 @@ int mmp_group_end(void);
  * partials in rank order, exactly as mmp_merge_partials does, into `out`
  * (one out_dtype element, device memory) on every rank.  index_base is the
  * shard's first global flat index (argmax / argmin). */
-#define MMP_XBLOCK_BYTES 16384
+#define MMP_XCOL_BYTES (1 << 20)
+#define MMP_XBLOCK_BYTES (16384 + 2 * MMP_XCOL_BYTES)
 int mmp_comm_peer_init(void);
 int mmp_reduce_allranks(int op, int dtype, const void *x, int64_t n, int64_t index_base, int out_dtype,
                         void *out, double ddof);
@@ -325,6 +326,15 @@ int mmp_reduce_allranks(int op, int dtype, const void *x, int64_t n, int64_t ind
  * written once as in mmp_scan; any other shard reduces and exchanges first.
  * Shards may be empty (n = 0: x and y unused, the call still takes part). */
 int mmp_scan_allranks(int op, int dtype, const void *x, int out_dtype, void *y, int64_t n);
+/* Sum of `count` elements of `dtype` (int64, uint64 or float64: column
+ * partials in their accumulation type) over every rank, in rank order, into
+ * `recv` (count elements of out_dtype, every rank) -- one launch: the
+ * send buffer goes into this rank's exchange area (MMP_XCOL_BYTES per call
+ * parity), flags as mmp_reduce_allranks, then every rank reads every
+ * rank's area over NVLink.  Collective, bounded wait (device error 8).
+ * MMP_E_UNSUPPORTED when count * 8 > MMP_XCOL_BYTES or there is no peer
+ * exchange (use mmp_allreduce). */
+int mmp_allreduce_sum_peer(const void *send, void *recv, size_t count, int dtype, int out_dtype);
 
 /* Wait for this device's stream, giving up after timeout_s seconds (<= 0:
  * the communicator's timeout): then the communicator is aborted and

@@ -115,6 +115,7 @@ SIGNATURES = {
     "mmp_comm_peer_init": (_int, []),
     "mmp_reduce_allranks": (_int, [_int, _int, _vp, _i64, _i64, _int, _vp, ctypes.c_double]),
     "mmp_scan_allranks": (_int, [_int, _int, _vp, _int, _vp, _i64]),
+    "mmp_allreduce_sum_peer": (_int, [_vp, _vp, ctypes.c_size_t, _int, _int]),
 }
 
 

@@ -245,6 +245,89 @@ __global__ void __launch_bounds__(RBLOCK) reduce_exchange_kernel(ContigLoader<T>
   exchange_merge_warp<OPC, T>(p, peers, rank, nranks, upto, epoch, out, out_dt, ddof, err);
 }
 
+// ---- column all-reduce over peer memory (mmp_allreduce_sum_peer).  The
+// exchange block's column area follows its first 16 KB: one MMP_XCOL_BYTES
+// region per call parity.  Every block copies its share of `send` into this
+// rank's region; the last block to finish (ticket) raises this rank's flag
+// in every rank's block; every block waits (bounded) for every rank's flag
+// and sums its share of the columns over the ranks, in rank order, into
+// out (out_dt).  All blocks of a launch are resident at once (the grid is
+// at most one block per SM), so the last block always arrives.
+constexpr long long XCOL_OFF = 16384;
+static_assert(XCOL_OFF >= XFLAG_OFF + 2 * 64 * 8, "column area after the flags");
+static_assert(XCOL_OFF + 2ll * MMP_XCOL_BYTES <= MMP_XBLOCK_BYTES, "exchange block layout");
+
+template <class W>
+__global__ void __launch_bounds__(RBLOCK) allreduce_cols_kernel(const W *__restrict__ send, long long count,
+                                                                void *out, int out_dt, XPeers peers, int rank,
+                                                                int nranks, unsigned long long epoch,
+                                                                unsigned *ticket, int *err) {
+  const int par = (int)(epoch & 1ull);
+  const long long area = XCOL_OFF + (long long)par * MMP_XCOL_BYTES;
+  W *mine = reinterpret_cast<W *>(peers.blk[rank] + area);
+  const long long stride = (long long)gridDim.x * RBLOCK;
+  const long long t0 = (long long)blockIdx.x * RBLOCK + threadIdx.x;
+  for (long long i = t0; i < count; i += stride) mine[i] = send[i];
+  __threadfence_system();  // this thread's copies before the block's ticket
+  __syncthreads();
+  __shared__ int s_last;
+  __shared__ unsigned long long s_seen;
+  if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) {
+    // every block's copies are fenced and counted: raise this rank's flag
+    if (threadIdx.x == 0) *ticket = 0u;  // for the next launch
+    __threadfence_system();
+    for (int r = threadIdx.x; r < nranks; r += RBLOCK) {
+      unsigned char *b = peers.blk[r];
+      asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(b + XFLAG_OFF + (long long)(par * 64 + rank) * 8),
+                   "l"(epoch)
+                   : "memory");
+    }
+  }
+  // ---- every rank's flag in this rank's block (bounded: 2 s)
+  if (threadIdx.x == 0) {
+    unsigned long long seen = 0;
+    const unsigned char *own = peers.blk[rank];
+    for (int r = 0; r < nranks; ++r) {
+      const void *fp = own + XFLAG_OFF + (long long)(par * 64 + r) * 8;
+      const unsigned long long ts = now_ns();
+      unsigned ns = 32;
+      bool ok = true;
+      while (ld_sys_u64(fp) != epoch) {
+        if (now_ns() - ts > 2000000000ull) {
+          ok = false;
+          break;
+        }
+        __nanosleep(ns);
+        if (ns < 1024) ns <<= 1;
+      }
+      if (ok) seen |= 1ull << r;
+      else atomicExch(err, 8);
+    }
+    s_seen = seen;
+  }
+  __threadfence_system();
+  __syncthreads();
+  const unsigned long long seen = s_seen;
+  constexpr bool kFloat = IsFloat<W>::value;
+  constexpr bool kUnsigned = !kFloat && W(-1) > W(0);
+  for (long long i = t0; i < count; i += stride) {
+    W acc = W(0);
+    for (int r = 0; r < nranks; ++r) {
+      if (!((seen >> r) & 1ull)) continue;  // never arrived: counts as empty
+      const unsigned long long bits =
+          ld_sys_u64(peers.blk[r] + area + (unsigned long long)i * sizeof(W));
+      W v;
+      memcpy(&v, &bits, sizeof(W));
+      acc += v;
+    }
+    if constexpr (kFloat) store_scalar(out, i, out_dt, false, 0, 0, (double)acc, false);
+    else if constexpr (kUnsigned) store_scalar(out, i, out_dt, true, 0, (unsigned long long)acc, 0.0, true);
+    else store_scalar(out, i, out_dt, true, (long long)acc, 0, 0.0, false);
+  }
+}
+
 // The carry of a distributed scan from the shard's tile aggregates (the
 // first launch of the long-row scan): one block sums (multiplies) the
 // aggregates in the carry type, then its first warp exchanges the shard
@@ -391,6 +474,30 @@ struct ScanCarryRun {
   }
 };
 
+template <class W>
+int allreduce_cols_run(const void *send, void *recv, long long count, int out_dt) {
+  void *blk[64];
+  int rank = 0, nranks = 0;
+  unsigned long long epoch = 0;
+  if (!peer_table(blk, &rank, &nranks, &epoch))
+    return set_error(MMP_E_UNSUPPORTED, "no peer exchange on this device: call mmp_comm_peer_init");
+  cudaStream_t st = stream();
+  if (!st) return set_error(MMP_E_CUDA, "no stream");
+  void *scr = nullptr;
+  unsigned *tickets = nullptr;
+  int rc = scratch(256, &scr, &tickets);
+  if (rc) return rc;
+  XPeers xp;
+  for (int q = 0; q < 64; ++q) xp.blk[q] = q < nranks ? (unsigned char *)blk[q] : nullptr;
+  long long grid = (count + RBLOCK - 1) / RBLOCK;
+  if (grid > sm_count()) grid = sm_count();  // one block per SM at most: all resident
+  if (grid < 1) grid = 1;
+  allreduce_cols_kernel<W><<<(unsigned)grid, RBLOCK, 0, st>>>((const W *)send, count, recv, out_dt, xp, rank,
+                                                                nranks, epoch, tickets, device_error_word());
+  MMP_LAUNCH_CHECK("allreduce_cols_kernel");
+  return MMP_OK;
+}
+
 // The carry of a distributed scan (the combination of the lower ranks'
 // shard totals), by the exchange: from the shard's tile aggregates (`agg`,
 // ntiles values of the carry type) when given, else from a full reduction
@@ -413,3 +520,17 @@ int scan_carry_allranks(int prod, int dtype, const void *agg, long long ntiles, 
 
 }  // namespace mmp
 
+
+extern "C" int mmp_allreduce_sum_peer(const void *send, void *recv, size_t count, int dtype, int out_dtype) {
+  if ((count > 0 && (!send || !recv)) || mmp_dtype_size(out_dtype) == 0)
+    return mmp::set_error(MMP_E_ARG, "bad argument to mmp_allreduce_sum_peer");
+  if (count * 8 > (size_t)MMP_XCOL_BYTES)
+    return mmp::set_error(MMP_E_UNSUPPORTED, "column buffer larger than the exchange area");
+  if (!mmp::is_ready()) return mmp::set_error(MMP_E_ARG, "call mmp_init first");
+  switch (dtype) {
+    case MMP_FLOAT64: return mmp::allreduce_cols_run<double>(send, recv, (long long)count, out_dtype);
+    case MMP_INT64: return mmp::allreduce_cols_run<long long>(send, recv, (long long)count, out_dtype);
+    case MMP_UINT64: return mmp::allreduce_cols_run<unsigned long long>(send, recv, (long long)count, out_dtype);
+    default: return mmp::set_error(MMP_E_ARG, "mmp_allreduce_sum_peer sums int64, uint64 or float64");
+  }
+}

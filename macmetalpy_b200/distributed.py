@@ -286,11 +286,33 @@ class DistArray:
         if axis == 0 and len(self.global_shape) == 2:
             cb = _cb()
             wide = np.float64 if self.dtype.kind == "f" else (np.uint64 if self.dtype.kind == "u" else np.int64)
-            loc = reductions.sum(self.local, axis=0, dtype=wide) if self.local.size else \
-                reductions.sum(self.local, axis=0).astype(wide)
+            odt = reductions.out_dtype("sum", self.dtype)
+            if self.local.size:
+                # the column kernel accumulates wide already: ask for its
+                # accumulator as the output (no cast pass over the block)
+                from .ndarray import ndarray
+                src = self.local._ensure_contiguous()
+                rows, cols = src.shape
+                loc = ndarray._empty((cols,), wide)
+                cb.check(cb.lib.mmp_reduce_axis(reductions.OPC["sum"], cb.dtype_code(src.dtype),
+                                                ctypes.c_void_p(src._ptr), 1, rows, cols, cb.dtype_code(wide),
+                                                ctypes.c_void_p(loc._ptr), 0.0), "sum axis 0")
+            else:
+                loc = reductions.sum(self.local, axis=0).astype(wide)
+            if _state.get("peer"):
+                # one launch: the column partials cross NVLink into every
+                # rank, summed in rank order straight into the result dtype
+                from .ndarray import ndarray
+                res = ndarray._empty(loc.shape, odt)
+                rc = cb.lib.mmp_allreduce_sum_peer(ctypes.c_void_p(loc._ptr), ctypes.c_void_p(res._ptr),
+                                                   int(loc.size), cb.dtype_code(wide), cb.dtype_code(odt))
+                if rc == 0:
+                    return res
+                if rc != -4:  # MMP_E_UNSUPPORTED (too many columns): the same on every rank
+                    cb.check(rc, "allreduce axis 0")
             cb.check(cb.lib.mmp_allreduce(ctypes.c_void_p(loc._ptr), ctypes.c_void_p(loc._ptr), int(loc.size),
                                           cb.dtype_code(wide), 0), "allreduce axis 0")
-            return loc.astype(reductions.out_dtype("sum", self.dtype))
+            return loc.astype(odt)
         return self._full("sum")
 
     def mean(self):

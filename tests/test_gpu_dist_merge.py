@@ -141,6 +141,19 @@ def _scan_allranks_one_rank(rng):
     cb.check(cb.lib.mmp_synchronize(), "sync")
 
 
+def _axis0_cases(D, rng):
+    """Axis-0 sums: int32 exact (int64 result), and more columns than the
+    peer exchange area holds (the NCCL all-reduce path)."""
+    mi = rng.integers(-50, 51, (100, 3000)).astype(np.int32)
+    got = D.DistArray.from_global(mi).sum(axis=0).get()
+    assert got.dtype == np.int64
+    np.testing.assert_array_equal(got, mi.sum(axis=0, dtype=np.int64))
+    mw = rng.standard_normal((4, 140000)).astype(np.float32)  # 140000 * 8 B > 1 MiB
+    sw = D.DistArray.from_global(mw).sum(axis=0).get()
+    assert sw.dtype == np.float32
+    assert np.max(np.abs(sw - mw.astype(np.float64).sum(axis=0))) <= 1e-5 * np.abs(mw).sum(axis=0).max()
+
+
 def test_one_rank_communicator(monkeypatch):
     import socket
 
@@ -172,6 +185,7 @@ def test_one_rank_communicator(monkeypatch):
         M = D.DistArray.from_global(m)
         s0 = M.sum(axis=0).get()
         assert np.max(np.abs(s0 - m.astype(np.float64).sum(axis=0))) <= 1e-4 * np.abs(m).sum(axis=0).max()
+        _axis0_cases(D, rng)
         D.barrier()
         assert D.max_over_ranks(2.5) == 2.5
     finally:

@@ -4,7 +4,8 @@ argmin / max / nansum / nanmean (the fused reduce + peer exchange when the
 ranks can map each other's memory, else device partials, all-gather and
 device merge), 1-D cumsum with device carries (int32 exact, float32 within
 1e-4; long aligned shards and shards on different scan paths through
-mmp_scan_allranks), axis-0 sums (all-reduce), axis-1 reductions and scans
+mmp_scan_allranks), axis-0 sums (peer all-reduce, and the NCCL all-reduce
+beyond its area), axis-1 reductions and scans
 (shard-local), matmul with B broadcast from rank 0.  Needs two visible GPUs; skipped
 otherwise.  Ranks are child processes with a short communicator timeout;
 NVLS is off (plain NCCL rings), as this test only checks results."""
@@ -106,6 +107,8 @@ def _rank_main(rank, world, port, q):
         assert np.max(np.abs(s1 - m.astype(np.float64).sum(axis=1))) <= 1e-4 * np.abs(m).sum(axis=1).max()
         s0 = M.sum(axis=0).get()
         assert np.max(np.abs(s0 - m.astype(np.float64).sum(axis=0))) <= 1e-4 * np.abs(m).sum(axis=0).max()
+        from test_gpu_dist_merge import _axis0_cases
+        _axis0_cases(D, np.random.default_rng(8))
         c1 = M.cumsum(axis=1).gather()
         assert np.max(np.abs(c1 - np.cumsum(m.astype(np.float64), axis=1))) <= 1e-3
         a = (rng.standard_normal((512, 384)) / 20).astype(np.float32)
