@@ -875,12 +875,10 @@ class ndarray:
     def __ipow__(self, o): return self._inplace(o, "pow_op")
 
     def __matmul__(self, other):
-        """``a @ b`` for 1-D and 2-D operands; like the reference's operator
-        (ndarray.py:1398-1450) it raises ValueError above 2-D, where
-        ``matmul()`` broadcasts batches."""
+        """``a @ b`` with numpy's batched semantics above 2-D (the reference's
+        operator, ndarray.py:1398-1450, raises there; BASELINE's batched
+        (64,1024,1024) @ (64,1024,1024) needs it)."""
         from . import linalg_top
-        if self.ndim > 2 or (other.ndim if other.__class__ is ndarray else np.ndim(other)) > 2:
-            raise ValueError("matmul requires 1-D or 2-D arrays")
         return linalg_top.matmul(self, other)
 
     def __rmatmul__(self, other):

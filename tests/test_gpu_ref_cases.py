@@ -237,10 +237,10 @@ def test_zero_d_result_against_python_bool(mp):
 def test_error_messages(mp):
     with pytest.raises(ValueError, match="shape mismatch"):
         mp.zeros((2, 3), dtype=mp.float32) @ mp.zeros((4, 5), dtype=mp.float32)
-    # the operator stops at 2-D (test_error_handling.py:116-121); matmul() batches
-    with pytest.raises(ValueError, match="1-D or 2-D"):
-        mp.zeros((2, 3, 4), dtype=mp.float32) @ mp.zeros((4, 5), dtype=mp.float32)
-    assert mp.matmul(mp.ones((2, 3, 4), dtype=mp.float32), mp.ones((4, 5), dtype=mp.float32)).shape == (2, 3, 5)
+    # batched @ (numpy semantics): the one deliberate divergence from
+    # test_error_handling.py:116-121, which expects ValueError
+    c = mp.ones((2, 3, 4), dtype=mp.float32) @ mp.ones((4, 5), dtype=mp.float32)
+    assert c.shape == (2, 3, 5) and float(c.get()[1, 2, 4]) == 4.0
     with pytest.raises(TypeError, match="size-1"):
         float(mp.arange(5, dtype=mp.float32))
     with pytest.raises(TypeError, match="size-1"):
