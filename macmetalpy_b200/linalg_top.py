@@ -64,8 +64,6 @@ def matmul(x1, x2, out=None, *, mode: str = "auto", **kwargs):
 
     def bstride(x, rows, cols):
         xb = x.shape[:-2]
-        if math.prod(xb) if xb else 1 == 1:
-            pass
         if (math.prod(xb) if xb else 1) == B:
             if tuple(xb) != tuple(batch_shape):
                 return None

@@ -6,7 +6,8 @@ device merge), 1-D cumsum with device carries (int32 exact, float32 within
 1e-4; long aligned shards and shards on different scan paths through
 mmp_scan_allranks), axis-0 sums (peer all-reduce, and the NCCL all-reduce
 beyond its area), axis-1 reductions and scans
-(shard-local), matmul with B broadcast from rank 0.  Needs two visible GPUs; skipped
+(shard-local), matmul with B broadcast from rank 0 (a ragged K, and a rank
+with no rows).  Needs two visible GPUs; skipped
 otherwise.  Ranks are child processes with a short communicator timeout;
 NVLS is off (plain NCCL rings), as this test only checks results."""
 
@@ -118,6 +119,17 @@ def _rank_main(rank, world, port, q):
         C = A.matmul(Bl).gather()
         r = O.matmul_f64(a, b)
         assert np.linalg.norm(C - r) / np.linalg.norm(r) <= 1e-5
+        # a longer, ragged K; then a one-row A, so rank 1 holds no rows and
+        # still takes part in the broadcast
+        for (mm, kk, nn) in ((300, 4100, 260), (1, 4096, 64)):
+            a2 = (rng.standard_normal((mm, kk)) / 60).astype(np.float32)
+            b2 = (rng.standard_normal((kk, nn)) / 60).astype(np.float32)
+            B2 = array(b2) if rank == 0 else zeros(b2.shape, dtype=np.float32)
+            C2 = D.DistArray.from_global(a2).matmul(B2).gather()
+            r2 = O.matmul_f64(a2, b2)
+            assert C2.shape == (mm, nn)
+            assert np.linalg.norm(C2 - r2) / np.linalg.norm(r2) <= 1e-5
+            np.testing.assert_array_equal(B2.get(), b2)  # the broadcast landed in place
         D.barrier()
         D.finalize()
         q.put((rank, "ok"))
