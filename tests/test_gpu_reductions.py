@@ -183,3 +183,41 @@ def test_empty_and_errors(cp):
         cp.max(e)
     with pytest.raises(ValueError):
         cp.argmax(e)
+
+
+def test_lazy_full_reduction_paths(cp):
+    """The short path for a lazy expression reduced to one value and the
+    general path agree: out=, the nan-kinds folded to plain kinds on an
+    integer expression, result dtypes, an empty lazy input, a repeated
+    expression (launch template) with new operands, and keepdims (general
+    path) on the same expression."""
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal(100003).astype(np.float32)
+    X = cp.array(x)
+    ref = np.sqrt(np.abs(x.astype(np.float64))) + np.exp(-(x.astype(np.float64) ** 2))
+    o = cp.empty((), dtype=np.float32)
+    r = cp.sum(cp.sqrt(cp.abs(X)) + cp.exp(-X ** 2), out=o)
+    assert r is o
+    assert relerr(o.get(), ref.sum()) <= 1e-5
+    k = cp.sum(cp.sqrt(cp.abs(X)) + cp.exp(-X ** 2), keepdims=True)
+    assert k.shape == (1,) and relerr(k.get()[0], ref.sum()) <= 1e-5
+    m = cp.mean(cp.sqrt(cp.abs(X)) + cp.exp(-X ** 2))
+    assert m.dtype == np.float32 and relerr(m.get(), ref.mean()) <= 1e-5
+    xi = rng.integers(-50, 51, 77777).astype(np.int32)
+    XI = cp.array(xi)
+    s = cp.nansum(XI * 3 + 1)  # no NaN in integers: nansum is sum, int64
+    assert s.dtype == np.int64 and int(s.get()) == int((xi.astype(np.int64) * 3 + 1).sum())
+    mx = cp.nanmax(XI - 7)
+    assert int(mx.get()) == int(xi.max()) - 7
+    e = cp.array(np.zeros(0, np.float32))
+    assert float(cp.sum(e + 1).get()) == 0.0
+    with pytest.raises(ValueError):
+        cp.max(e + 1)
+    # the same expression again over new arrays: the cached launch takes the
+    # new pointers
+    for seed in (1, 2):
+        y = np.random.default_rng(seed).standard_normal(4096).astype(np.float32)
+        Y = cp.array(y)
+        got = cp.sum(cp.sqrt(cp.abs(Y)) + cp.exp(-Y ** 2)).get()
+        want = (np.sqrt(np.abs(y.astype(np.float64))) + np.exp(-(y.astype(np.float64) ** 2))).sum()
+        assert relerr(got, want) <= 1e-5
