@@ -1,10 +1,11 @@
-"""Failure detection of the distributed reduction on 2 GPUs, without a GPU
+"""Failure detection of the distributed exchanges on 2 GPUs, without a GPU
 fault: rank 1 stays alive (its exchange block stays mapped) but never joins
-the reduction; rank 0's fused reduce + exchange waits for rank 1's flag,
+the call; rank 0's exchange -- the fused reduce + exchange, the scan's
+carry exchange, the axis-0 column all-reduce -- waits for rank 1's flag,
 gives up after its bounded wait (2 s of device time), sets device error 8
 and returns, and rank 0's synchronize raises instead of hanging.  Both
 ranks then finish normally.  Needs two visible GPUs; skipped otherwise.
-NVLS is off; the exchange uses plain peer stores."""
+NVLS is off; the exchanges use plain peer stores."""
 
 import os
 import socket
@@ -33,7 +34,7 @@ def _port():
     return p
 
 
-def _rank_main(rank, port, q, done):
+def _rank_main(rank, port, q, done, op):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     try:
@@ -45,12 +46,14 @@ def _rank_main(rank, port, q, done):
             done.wait(60)
             D.finalize()
             return
-        x = np.arange(1 << 20, dtype=np.float32)
-        X = D.DistArray.from_global(x)
+        if op == "sum_axis0":
+            X = D.DistArray.from_global(np.ones((64, 1000), dtype=np.float32))
+        else:
+            X = D.DistArray.from_global(np.arange(1 << 20, dtype=np.float32))
         D.barrier()
         if rank == 0:
             t0 = time.monotonic()
-            r = X.sum()
+            r = X.sum() if op == "sum" else (X.cumsum() if op == "cumsum" else X.sum(axis=0))
             try:
                 D.synchronize()
                 got = "no error"
@@ -72,12 +75,13 @@ def _rank_main(rank, port, q, done):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-def test_rank_that_never_joins_ends_in_an_error():
+@pytest.mark.parametrize("op", ["sum", "cumsum", "sum_axis0"])
+def test_rank_that_never_joins_ends_in_an_error(op):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     done = ctx.Event()
     port = _port()
-    ps = [ctx.Process(target=_rank_main, args=(r, port, q, done)) for r in range(2)]
+    ps = [ctx.Process(target=_rank_main, args=(r, port, q, done, op)) for r in range(2)]
     for p in ps:
         p.start()
     res = [q.get(timeout=240) for _ in ps]
