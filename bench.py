@@ -423,7 +423,9 @@ def main():
         "gpu_launches": args.steps * len(ops),
     }
     if not args.no_e2e:
-        line["e2e"] = e2e_c2(cp, d, steps=4, dist=dist)
+        # 8 steps: the pipeline's one-time fill (the first step's uploads,
+        # ~80 ms at N = 1) is amortised over them
+        line["e2e"] = e2e_c2(cp, d, steps=8, dist=dist)
     if rank == 0 and not args.no_cpu and world == 1:
         line["cpu_baseline"] = cpu_baseline()
     if not args.no_suite:
