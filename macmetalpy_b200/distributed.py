@@ -345,6 +345,12 @@ class DistArray:
     def min(self):
         return self._full("min")
 
+    def nanmax(self):
+        return self._full("nanmax")
+
+    def nanmin(self):
+        return self._full("nanmin")
+
     def argmax(self) -> int:
         return int(self._full("argmax").get())
 
@@ -358,8 +364,10 @@ class DistArray:
 
         if axis in (1, -1) and len(self.global_shape) == 2:
             return DistArray(reductions.cumsum(self.local, axis=1), self.global_shape, self.start, self.stop)
+        if axis in (0, -2) and len(self.global_shape) == 2:
+            return self._cumsum_rows()
         if len(self.global_shape) != 1 and axis is not None:
-            raise NotImplementedError("distributed cumsum: 1-D, axis=1 of 2-D, or axis=None")
+            raise NotImplementedError("distributed cumsum: 1-D, axis 0 or 1 of 2-D, or axis=None")
         local = self.local.reshape(-1) if len(self.global_shape) != 1 else self.local
         if _state.get("peer"):
             # one collective call: the lower ranks' totals cross NVLink as peer
@@ -383,6 +391,44 @@ class DistArray:
         if len(self.global_shape) != 1:  # axis=None of an N-d array: flat result
             n = int(np.prod(self.global_shape))
             return DistArray(res, (n,), self._flat_base(), self._flat_base() + int(local.size))
+        return DistArray(res, self.global_shape, self.start, self.stop)
+
+    def _cumsum_rows(self) -> "DistArray":
+        """cumsum along axis 0 of a row-sharded 2-D array: every rank's column
+        totals (the column kernel's accumulator, float64 / int64 / uint64)
+        are all-gathered on the device, the rows of the ranks below this one
+        summed into the column carry, and the carry added to the local
+        column scan in one fused pass (float: in float64, rounded once to
+        the result dtype; integers exact)."""
+        from . import reductions
+        from .creation import zeros
+        from .ndarray import ndarray
+
+        cb = _cb()
+        kind = self.dtype.kind
+        wide = np.dtype(np.float64 if kind == "f" else (np.uint64 if kind == "u" else np.int64))
+        odt = reductions.scan_out_dtype(self.dtype)
+        cols = int(self.global_shape[1])
+        src = self.local._ensure_contiguous()
+        if src.size:
+            tot = ndarray._empty((cols,), wide)
+            cb.check(cb.lib.mmp_reduce_axis(reductions.OPC["sum"], cb.dtype_code(src.dtype), ctypes.c_void_p(src._ptr),
+                                            1, int(src.shape[0]), cols, cb.dtype_code(wide),
+                                            ctypes.c_void_p(tot._ptr), 0.0), "column totals")
+        else:
+            tot = zeros((cols,), dtype=wide)
+        allt = ndarray._empty((world() * cols,), wide)
+        cb.check(cb.lib.mmp_allgather(ctypes.c_void_p(tot._ptr), ctypes.c_void_p(allt._ptr), cols,
+                                      cb.dtype_code(wide)), "column totals all-gather")
+        r = rank()
+        if not src.size:
+            res = ndarray._empty(src.shape, odt)
+        elif r == 0:
+            res = reductions.cumsum(src, axis=0)
+        else:
+            carry = reductions.sum(allt.reshape(world(), cols)[:r], axis=0)
+            res = (reductions.cumsum(src, axis=0).astype(wide) + carry).astype(odt)
+            res._materialize_if_lazy()
         return DistArray(res, self.global_shape, self.start, self.stop)
 
     # -- matmul: A row-sharded, B broadcast from rank 0

@@ -186,6 +186,11 @@ def test_one_rank_communicator(monkeypatch):
         s0 = M.sum(axis=0).get()
         assert np.max(np.abs(s0 - m.astype(np.float64).sum(axis=0))) <= 1e-4 * np.abs(m).sum(axis=0).max()
         _axis0_cases(D, rng)
+        c0 = M.cumsum(axis=0).gather()
+        assert np.max(np.abs(c0 - np.cumsum(m.astype(np.float64), axis=0))) <= 1e-4 * np.abs(m).sum(axis=0).max()
+        mi = rng.integers(-9, 10, (300, 7)).astype(np.int32)
+        np.testing.assert_array_equal(D.DistArray.from_global(mi).cumsum(axis=0).gather(),
+                                      np.cumsum(mi, axis=0, dtype=np.int64))
         D.barrier()
         assert D.max_over_ranks(2.5) == 2.5
     finally:

@@ -6,8 +6,8 @@ device merge), 1-D cumsum with device carries (int32 exact, float32 within
 1e-4; long aligned shards and shards on different scan paths through
 mmp_scan_allranks), axis-0 sums (peer all-reduce, and the NCCL all-reduce
 beyond its area), axis-1 reductions and scans
-(shard-local), matmul with B broadcast from rank 0 (a ragged K, and a rank
-with no rows).  Needs two visible GPUs; skipped
+(shard-local), axis-0 scans (column totals all-gathered into a carry), matmul
+with B broadcast from rank 0 (a ragged K, and a rank with no rows).  Needs two visible GPUs; skipped
 otherwise.  Ranks are child processes with a short communicator timeout;
 NVLS is off (plain NCCL rings), as this test only checks results."""
 
@@ -92,6 +92,20 @@ def _rank_main(rank, world, port, q):
         assert abs(float(XN.nansum()) - np.nansum(xn.astype(np.float64))) <= 1e-4 * np.nansum(np.abs(xn))
         assert abs(float(XN.nanmean()) - np.nanmean(xn.astype(np.float64))) <= 1e-4 * abs(np.nanmean(xn))
         assert XN.argmax() == O.argmax(xn)
+        # the other merge rules of the exchange
+        assert abs(float(X.std()) - x64.std()) <= 1e-4 * x64.std()
+        assert float(X.min()) == float(x.min())
+        xn64 = xn.astype(np.float64)
+        assert abs(float(XN.nanvar()) - np.nanvar(xn64)) <= 1e-4 * np.nanvar(xn64)
+        assert abs(float(XN.nanstd()) - np.nanstd(xn64)) <= 1e-4 * np.nanstd(xn64)
+        assert float(XN.nanmax()) == float(np.nanmax(xn))
+        assert float(XN.nanmin()) == float(np.nanmin(xn))
+        sg = rng.choice(np.array([-1, 1], np.int32), 200_001)
+        assert int(D.DistArray.from_global(sg).prod()) == int(np.prod(sg.astype(np.int64)))
+        xi2 = rng.integers(-1000, 1000, 300_001).astype(np.int32)
+        xi2[[5, 250_000]] = 5000  # a tie across the shards
+        XI2 = D.DistArray.from_global(xi2)
+        assert XI2.argmax() == 5 and XI2.argmin() == int(np.argmin(xi2))
         xi = rng.integers(-100, 101, 3_000_017).astype(np.int32)
         XI = D.DistArray.from_global(xi)
         assert int(XI.sum()) == int(xi.sum(dtype=np.int64))
@@ -112,6 +126,16 @@ def _rank_main(rank, world, port, q):
         _axis0_cases(D, np.random.default_rng(8))
         c1 = M.cumsum(axis=1).gather()
         assert np.max(np.abs(c1 - np.cumsum(m.astype(np.float64), axis=1))) <= 1e-3
+        # axis 0 crosses the shard boundary: the lower ranks' column totals are the carry
+        c0 = M.cumsum(axis=0).gather()
+        assert c0.dtype == np.float32
+        assert np.max(np.abs(c0 - np.cumsum(m.astype(np.float64), axis=0))) <= 1e-4 * np.abs(m).sum(axis=0).max()
+        mi0 = rng.integers(-(1 << 31), (1 << 31) - 1, (777, 130), dtype=np.int64).astype(np.int32)
+        ci0 = D.DistArray.from_global(mi0).cumsum(axis=0).gather()
+        assert ci0.dtype == np.int64
+        np.testing.assert_array_equal(ci0, np.cumsum(mi0, axis=0, dtype=np.int64))
+        one = D.DistArray.from_global(np.ones((1, 9), np.int32)).cumsum(axis=0).gather()  # rank 1: no rows
+        np.testing.assert_array_equal(one, np.ones((1, 9), np.int64))
         a = (rng.standard_normal((512, 384)) / 20).astype(np.float32)
         b = (rng.standard_normal((384, 640)) / 20).astype(np.float32)
         A = D.DistArray.from_global(a)
