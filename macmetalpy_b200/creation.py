@@ -17,8 +17,11 @@ import numpy as np
 
 from . import _cuda_backend as _cb
 from . import _fusion as _fu
+from ._config import get_config
 from ._dtypes import resolve_dtype
 from .ndarray import ndarray
+
+_CFG = get_config()
 
 __all__ = [
     "array", "asarray", "asanyarray", "ascontiguousarray", "empty", "empty_like", "zeros", "zeros_like",
@@ -33,10 +36,19 @@ def _shape(shape):
 
 
 def array(obj, dtype=None, copy=True, order="C", ndmin=0) -> ndarray:
-    """Create a device array from ``obj`` (numpy array, list, scalar, ndarray)."""
+    """Create a device array from ``obj`` (numpy array, list, scalar, ndarray).
+
+    On a multi-rank job with ``set_config(shard_threshold=n)``, host data of
+    at least n elements (and at least one dimension) becomes this rank's row
+    block: a ``distributed.DistArray``."""
     if isinstance(obj, ndarray):
         r = obj.astype(dtype) if dtype is not None and np.dtype(dtype) != obj.dtype else (obj.copy() if copy else obj)
     else:
+        if _CFG.shard_threshold is not None and obj.__class__.__name__ != "DistArray":
+            from . import distributed
+            d = distributed._shard_host(obj, dtype, _CFG.shard_threshold)
+            if d is not None:
+                return d
         host = np.asarray(obj, dtype=dtype)
         r = ndarray._from_numpy(host, resolve_dtype(dtype if dtype is not None else host.dtype))
     while r.ndim < ndmin:
@@ -47,6 +59,8 @@ def array(obj, dtype=None, copy=True, order="C", ndmin=0) -> ndarray:
 def asarray(obj, dtype=None, order=None) -> ndarray:
     """Like :func:`array` but returns ``obj`` itself when already suitable."""
     if isinstance(obj, ndarray) and (dtype is None or np.dtype(dtype) == obj.dtype):
+        return obj
+    if obj.__class__.__name__ == "DistArray" and dtype is None:
         return obj
     return array(obj, dtype=dtype, copy=False)
 

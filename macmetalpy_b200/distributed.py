@@ -143,6 +143,68 @@ def max_over_ranks(v: float) -> float:
     return float(t.get()[0])
 
 
+def _shard_host(obj, dtype, threshold: int):
+    """The row block of host data for ``array()`` when sharding applies (a
+    multi-rank job, at least ``threshold`` elements, one dimension or more),
+    else None.  Every rank must pass the same data (SPMD)."""
+    if not _state["init"] or _state["world"] < 2:
+        return None
+    host = np.asarray(obj, dtype=dtype)
+    if host.ndim == 0 or host.size < threshold:
+        return None
+    return DistArray.from_global(host)
+
+
+def _reduce_call(a, kind, axis=None, keepdims=False, ddof=0.0, dtype=None, out=None):
+    """reductions.<kind>(a, axis) for a DistArray: full reductions through the
+    exchange, axis 0 of a 2-D sum through the column all-reduce, other axes
+    shard-local."""
+    from . import reductions
+
+    if keepdims or dtype is not None or out is not None:
+        raise NotImplementedError("distributed reductions take no keepdims, dtype or out")
+    if axis is not None:
+        if isinstance(axis, (tuple, list)):
+            if len(axis) != 1:
+                raise NotImplementedError("distributed reductions over one axis or all")
+            axis = axis[0]
+        ax = int(axis) % a.ndim
+        if ax != 0:  # along the rows of every block
+            return a.map(lambda x: reductions._reduce(x, kind, ax, ddof=ddof) if kind not in ("argmax", "argmin")
+                         else reductions._arg(x, kind, ax, None, False))
+        if a.ndim == 2 and kind == "sum":
+            return a.sum(axis=0)
+        if a.ndim != 1:
+            raise NotImplementedError(f"distributed {kind} along the sharded axis of a {a.ndim}-d array")
+    if kind in ("var", "std", "nanvar", "nanstd"):
+        return getattr(a, kind)(ddof)
+    return getattr(a, kind)()
+
+
+def _scan_call(a, op, axis=None, dtype=None, out=None):
+    """cumsum (op 0) / cumprod (op 1) of a DistArray."""
+    from . import reductions
+
+    if dtype is not None or out is not None:
+        raise NotImplementedError("distributed scans take no dtype or out")
+    if a.ndim == 2 and axis is not None and int(axis) % 2 == 1:
+        return a.map(lambda x: reductions._scan(x, op, 1))
+    if op == 0:
+        return a.cumsum(axis)
+    raise NotImplementedError("distributed cumprod: along axis 1 of a 2-D array only")
+
+
+def _ufunc(op_name: str, operands):
+    """An elementwise op with a DistArray among its operands: the same op on
+    this rank's blocks (see DistArray._operand)."""
+    from .ndarray import ndarray
+
+    lead = next(o for o in operands if isinstance(o, DistArray))
+    args = [lead._operand(o) for o in operands]
+    out = ndarray._elementwise(op_name, *args)
+    return DistArray(out, lead.global_shape[:1] + tuple(out.shape[1:]), lead.start, lead.stop)
+
+
 def row_partition(n: int, world_size: int) -> list[tuple[int, int]]:
     """Contiguous [start, stop) blocks of n rows over world_size ranks; the
     first n % world_size ranks take one extra row."""
@@ -204,11 +266,13 @@ class DistArray:
     def from_global(cls, host: np.ndarray, dtype=None) -> "DistArray":
         """Each rank uploads its own row block of a host array every rank
         can produce (e.g. from the same seed)."""
-        from .creation import array
+        from ._dtypes import resolve_dtype
+        from .ndarray import ndarray
 
-        host = np.asarray(host)
+        host = np.asarray(host, dtype=dtype)
         s, e = row_partition(host.shape[0], world())[rank()]
-        return cls(array(host[s:e], dtype=dtype), tuple(host.shape), s, e)
+        block = np.ascontiguousarray(host[s:e])
+        return cls(ndarray._from_numpy(block, resolve_dtype(block.dtype)), tuple(host.shape), s, e)
 
     @classmethod
     def from_local(cls, local, global_rows: int) -> "DistArray":
@@ -237,17 +301,58 @@ class DistArray:
         host = allb.get().reshape((world(), maxrows) + inner)
         return np.concatenate([host[r, : e - s] for r, (s, e) in enumerate(parts)], axis=0)
 
+    @property
+    def ndim(self):
+        return len(self.global_shape)
+
+    @property
+    def size(self):
+        return int(np.prod(self.global_shape))
+
+    def get(self) -> np.ndarray:
+        """The whole array on the host (``gather``), as ``ndarray.get``."""
+        return self.gather()
+
     # -- elementwise (shard-local)
+    def _operand(self, o):
+        """o as an operand of this rank's block: a DistArray of the same
+        partition gives its block; an array spanning the global rows gives
+        this rank's rows; scalars and arrays that broadcast along the rows
+        pass unchanged."""
+        if isinstance(o, DistArray):
+            if o.global_shape[0] != self.global_shape[0] or (o.start, o.stop) != (self.start, self.stop):
+                raise ValueError("distributed operands must share one row partition")
+            return o.local
+        shp = getattr(o, "shape", None)
+        if shp is not None and len(shp) == len(self.global_shape) and shp[0] == self.global_shape[0] \
+                and self.global_shape[0] > 1:
+            return o[self.start:self.stop]
+        return o
+
     def map(self, fn, *others) -> "DistArray":
-        args = [o.local if isinstance(o, DistArray) else o for o in others]
-        return DistArray(fn(self.local, *args), self.global_shape, self.start, self.stop)
+        args = [self._operand(o) for o in others]
+        out = fn(self.local, *args)
+        return DistArray(out, self.global_shape[:1] + tuple(out.shape[1:]), self.start, self.stop)
 
     def __add__(self, o): return self.map(lambda a, b: a + b, o)
+    def __radd__(self, o): return self.map(lambda a, b: b + a, o)
     def __sub__(self, o): return self.map(lambda a, b: a - b, o)
+    def __rsub__(self, o): return self.map(lambda a, b: b - a, o)
     def __mul__(self, o): return self.map(lambda a, b: a * b, o)
+    def __rmul__(self, o): return self.map(lambda a, b: b * a, o)
     def __truediv__(self, o): return self.map(lambda a, b: a / b, o)
+    def __rtruediv__(self, o): return self.map(lambda a, b: b / a, o)
     def __floordiv__(self, o): return self.map(lambda a, b: a // b, o)
     def __mod__(self, o): return self.map(lambda a, b: a % b, o)
+    def __pow__(self, o): return self.map(lambda a, b: a ** b, o)
+    def __neg__(self): return self.map(lambda a: -a)
+    def __abs__(self): return self.map(lambda a: abs(a))
+    def __lt__(self, o): return self.map(lambda a, b: a < b, o)
+    def __le__(self, o): return self.map(lambda a, b: a <= b, o)
+    def __gt__(self, o): return self.map(lambda a, b: a > b, o)
+    def __ge__(self, o): return self.map(lambda a, b: a >= b, o)
+    def __matmul__(self, o): return self.matmul(o)
+    def astype(self, dtype): return self.map(lambda a: a.astype(dtype))
 
     # -- full reductions: device partial -> all-gather -> device merge
     def _flat_base(self) -> int:

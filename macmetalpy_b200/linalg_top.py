@@ -34,8 +34,13 @@ def _rowmajor(a: ndarray) -> ndarray:
 
 
 def matmul(x1, x2, out=None, *, mode: str = "auto", **kwargs):
-    """Matrix product with numpy semantics (1-D promotion, batch broadcast)."""
+    """Matrix product with numpy semantics (1-D promotion, batch broadcast).
+    A row-block distributed ``x1`` multiplies its block by the replicated
+    ``x2`` (``distributed.DistArray.matmul``)."""
     from .creation import asarray
+
+    if x1.__class__.__name__ == "DistArray":
+        return x1.matmul(asarray(x2))
 
     a = asarray(x1)
     b = asarray(x2)

@@ -664,6 +664,10 @@ class ndarray:
         fast = _elementwise_fast(op_name, operands)
         if fast is not None:
             return fast
+        for o in operands:
+            if o.__class__.__name__ == "DistArray":  # block-distributed: the op on this rank's blocks
+                from . import distributed
+                return distributed._ufunc(op_name, operands)
         ops = []
         specs = []
         shape = None

@@ -112,6 +112,9 @@ def _reduce(a, kind: str, axis=None, keepdims=False, ddof=0.0, dtype=None, out=N
             res = ndarray._empty0(odt)
             _fu.run_reduce(a._fusion_node, a._shape, OPC[k], res._buffer.ptr, odt, ddof)
             return res if out is None else _finish(res, out)
+    if a.__class__ is not ndarray and a.__class__.__name__ == "DistArray":
+        from . import distributed
+        return distributed._reduce_call(a, kind, axis, keepdims, ddof, dtype, out)
     a = _asarray(a)
     if dtype is not None:
         a = a.astype(resolve_dtype(dtype), copy=False)
@@ -252,6 +255,9 @@ amin = min
 
 
 def _arg(a, kind, axis, out, keepdims):
+    if a.__class__.__name__ == "DistArray":
+        from . import distributed
+        return distributed._reduce_call(a, kind, axis, keepdims, 0.0, None, out)
     a = _asarray(a)
     if axis is None:
         if a.ndim == 0:
@@ -301,6 +307,9 @@ def scan_out_dtype(dt) -> np.dtype:
 
 
 def _scan(a, op: int, axis=None, dtype=None, out=None, carry_ptr: int = 0):
+    if a.__class__.__name__ == "DistArray":
+        from . import distributed
+        return distributed._scan_call(a, op, axis, dtype, out)
     a = _asarray(a)
     if dtype is not None:
         a = a.astype(resolve_dtype(dtype), copy=False)

@@ -7,7 +7,8 @@ device merge), 1-D cumsum with device carries (int32 exact, float32 within
 mmp_scan_allranks), axis-0 sums (peer all-reduce, and the NCCL all-reduce
 beyond its area), axis-1 reductions and scans
 (shard-local), axis-0 scans (column totals all-gathered into a carry), matmul
-with B broadcast from rank 0 (a ragged K, and a rank with no rows).  Needs two visible GPUs; skipped
+with B broadcast from rank 0 (a ragged K, and a rank with no rows), and the
+array API on arrays sharded by set_config(shard_threshold=...).  Needs two visible GPUs; skipped
 otherwise.  Ranks are child processes with a short communicator timeout;
 NVLS is off (plain NCCL rings), as this test only checks results."""
 
@@ -65,6 +66,43 @@ def _long_and_mixed_scans(D, rank):
         np.testing.assert_array_equal(Y.get(), want[lo:lo + sizes[rank]])
 
 
+def _threshold_sharding(D, rank):
+    """set_config(shard_threshold=n): host data of at least n elements is
+    uploaded as this rank's row block, and the array API works on it --
+    the C1 expression, full and per-axis reductions, argmax, cumsum and
+    matmul -- against numpy on the whole array; smaller arrays stay whole."""
+    import macmetalpy_b200 as cp
+
+    rng = np.random.default_rng(31)
+    cp.set_config(shard_threshold=100_000)
+    try:
+        xs = rng.standard_normal(300_001).astype(np.float32)
+        XS = cp.array(xs)
+        assert isinstance(XS, D.DistArray) and XS.shape == xs.shape
+        assert isinstance(cp.array(xs[:1000]), cp.ndarray)
+        y = cp.sqrt(cp.abs(XS)) + cp.exp(-XS ** 2)
+        assert isinstance(y, D.DistArray)
+        x64 = xs.astype(np.float64)
+        yref = np.sqrt(np.abs(x64)) + np.exp(-x64 ** 2)
+        assert np.max(np.abs(y.get() - yref) / yref) <= 5e-7
+        assert abs(float(cp.sum(y)) - yref.sum()) <= 1e-5 * yref.sum()
+        assert abs(float(cp.var(XS)) - x64.var()) <= 1e-4 * x64.var()
+        assert cp.argmax(XS) == int(np.argmax(xs))
+        c = cp.cumsum(XS).get()
+        assert np.max(np.abs(c - np.cumsum(x64))) <= 1e-6 * np.abs(x64).sum()
+        m = rng.standard_normal((1000, 300)).astype(np.float32)
+        M = cp.array(m)
+        assert isinstance(M, D.DistArray)
+        assert np.max(np.abs(cp.sum(M, axis=0).get() - m.astype(np.float64).sum(axis=0))) <= 1e-4
+        assert np.max(np.abs(cp.mean(M, axis=1).get() - m.astype(np.float64).mean(axis=1))) <= 1e-5
+        b = (rng.standard_normal((300, 40)) / 20).astype(np.float32)
+        P = (M @ cp.array(b)).get()
+        r = m.astype(np.float64) @ b.astype(np.float64)
+        assert np.linalg.norm(P - r) / np.linalg.norm(r) <= 1e-5
+    finally:
+        cp.set_config(shard_threshold=0)
+
+
 def _rank_main(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -116,6 +154,7 @@ def _rank_main(rank, world, port, q):
         assert np.max(np.abs(got - ref) / ref) <= 1e-4
         if D._state.get("peer"):
             _long_and_mixed_scans(D, rank)
+        _threshold_sharding(D, rank)
         m = rng.standard_normal((1001, 515)).astype(np.float32)
         M = D.DistArray.from_global(m)
         s1 = M.sum(axis=1).gather()

@@ -107,3 +107,24 @@ def test_depth_tracking():
         n = fu.UnaryOpNode("exp_op", n, (10,), np.float32)
     assert n._depth == 5
     assert fu._MAX_DEPTH == 16
+
+
+def test_shard_threshold_config():
+    """set_config(shard_threshold=...) (0 turns it off, negatives refused);
+    without a multi-rank job nothing is sharded, whatever the threshold."""
+    import numpy as np
+    import pytest
+
+    from macmetalpy_b200 import _config, distributed
+
+    cfg = _config.get_config()
+    try:
+        _config.set_config(shard_threshold=100)
+        assert cfg.shard_threshold == 100
+        assert distributed._shard_host(np.ones(1000, np.float32), None, 100) is None  # not initialised
+        _config.set_config(shard_threshold=0)
+        assert cfg.shard_threshold is None
+        with pytest.raises(ValueError):
+            _config.set_config(shard_threshold=-1)
+    finally:
+        cfg.shard_threshold = None
