@@ -128,3 +128,31 @@ def test_shard_threshold_config():
             _config.set_config(shard_threshold=-1)
     finally:
         cfg.shard_threshold = None
+
+
+def test_dist_operand_rules():
+    """How a row-block DistArray lines its operands up with its block (host
+    logic, numpy blocks standing in for device arrays): a DistArray of the
+    same partition gives its block, an array spanning the global rows gives
+    this rank's rows, a row-broadcast operand or a scalar passes unchanged,
+    and a different partition is refused."""
+    import numpy as np
+    import pytest
+
+    from macmetalpy_b200.distributed import DistArray
+
+    g = np.arange(40.0).reshape(10, 4)
+    a = DistArray(g[3:7], (10, 4), 3, 7)  # rows 3..6 of a 10-row array
+    b = DistArray(g[3:7] * 2, (10, 4), 3, 7)
+    np.testing.assert_array_equal(a._operand(b), g[3:7] * 2)
+    np.testing.assert_array_equal(a._operand(g), g[3:7])
+    row = np.ones((1, 4))
+    assert a._operand(row) is row and a._operand(2.5) == 2.5
+    with pytest.raises(ValueError):
+        a._operand(DistArray(g[0:4], (10, 4), 0, 4))
+    c = (a + g) * 2 - b
+    assert isinstance(c, DistArray) and (c.start, c.stop, c.global_shape) == (3, 7, (10, 4))
+    np.testing.assert_array_equal(c.local, 2 * g[3:7])  # (g + g) * 2 - 2g on the block
+    s1 = a.map(lambda x: x.sum(axis=1))  # a per-row result keeps the row partition
+    assert s1.global_shape == (10,) and s1.local.shape == (4,)
+    assert a.ndim == 2 and a.size == 40
